@@ -1,0 +1,186 @@
+/*
+ * nkv.h -- C ABI of the B200 (sm_100a) attention hot path for nano-kvllm.
+ *
+ * The library (libnkv.so) replaces three pieces of the reference's attention
+ * path with hand-written CUDA kernels:
+ *
+ *   1. the paged KV slot write        (Triton store_kvcache_kernel)
+ *   2. paged decode attention         (flash_attn_with_kvcache, block-table form)
+ *   3. KV-cache compression           (torch MyCompressCompact + SnapKV), both the
+ *                                      periodic window form and KvChat's threshold
+ *                                      S -> R form with its query window.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are DEVICE pointers. 16-bit floating point data is
+ *     bfloat16 and is passed as void*. Index tensors are int32.
+ *   - Sizes and strides are host integers. Strides are counted in ELEMENTS.
+ *   - The KV cache of one layer is laid out exactly like the reference's
+ *     per-layer view kv_cache[0|1, layer] of shape
+ *     [num_blocks, block_size, num_kv_heads, head_dim], contiguous, so a slot
+ *     (block_id * block_size + offset) addresses a row of num_kv_heads*head_dim
+ *     elements.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Every call is stream-ordered, performs no host synchronisation and
+ *     allocates no device memory; scratch memory ("workspace") is owned and
+ *     passed in by the caller.
+ *   - Every call returns an nkv_status (0 = success). No C++ exception crosses
+ *     this boundary. Device-side range checks never trap: they skip the bad
+ *     access and set a bit in a sticky per-device error word that
+ *     nkv_read_device_error() returns.
+ */
+#ifndef NKV_H_
+#define NKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nkv_status {
+  NKV_OK = 0,
+  NKV_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad stride */
+  NKV_ERR_UNSUPPORTED = 2,      /* head_dim, block_size or group width outside the kernels' range */
+  NKV_ERR_WORKSPACE = 3,        /* workspace missing or smaller than the *_workspace_size query */
+  NKV_ERR_ALIGNMENT = 4,        /* pointer or stride not 16-byte aligned where TMA or 128-bit loads need it */
+  NKV_ERR_CUDA = 5              /* CUDA launch / driver error (see nkv_last_cuda_error) */
+} nkv_status;
+
+/* Bits of the sticky device error word. */
+#define NKV_DEVERR_STORE_SLOT      0x1u  /* slot_mapping entry outside [-1, num_slots) */
+#define NKV_DEVERR_DECODE_BLOCK    0x2u  /* block_tables entry outside [0, num_blocks) on a live token */
+#define NKV_DEVERR_WAIT_TIMEOUT    0x4u  /* a bounded mbarrier / cluster wait gave up */
+#define NKV_DEVERR_COMPRESS_RANGE  0x8u  /* compression window or slot outside the cache */
+#define NKV_DEVERR_RING_RANGE      0x10u /* query-window ring slot / position out of range */
+
+/* Human-readable name of a status code (static string). */
+const char* nkv_status_string(int status);
+
+/* ABI version of this header (major * 100 + minor). */
+int nkv_abi_version(void);
+
+/* Last CUDA runtime error code seen by an entry point on this thread (0 if none). */
+int nkv_last_cuda_error(void);
+
+/* Reads (and optionally clears) the sticky device error word of the current
+ * device. This is the one call that synchronises: it copies 4 bytes to the
+ * host. Meant for tests and debugging, not for the decode loop. */
+int nkv_read_device_error(uint32_t* out_bits, int clear);
+
+/* ------------------------------------------------------------------------ */
+/* 1. store_kvcache                                                          */
+/* Replaces: store_kvcache / store_kvcache_kernel,                           */
+/*   nanokvllm/layers/attention.py:10-40 (same in KvChat/layers/attention.py:10-40). */
+/* For each token i with s = slot_mapping[i] != -1:                          */
+/*   k_cache[s, :, :] = key[i, :, :];  v_cache[s, :, :] = value[i, :, :]     */
+/* key/value rows are num_kv_heads*head_dim contiguous elements starting at  */
+/* key + i*key_stride (the reference asserts stride(1) == head_dim and       */
+/* stride(-1) == 1; the row stride may be the qkv split stride).             */
+/* num_tokens == 0 or num_slots == 0 is a no-op (the reference's warm-up     */
+/* with empty caches, model_runner.py:97-131).                               */
+int nkv_store_kvcache(const void* key, int64_t key_stride,
+                      const void* value, int64_t value_stride,
+                      void* k_cache, void* v_cache, int64_t num_slots,
+                      const int32_t* slot_mapping, int32_t num_tokens,
+                      int32_t num_kv_heads, int32_t head_dim, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 2. Paged decode attention                                                 */
+/* Replaces: flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,       */
+/*   cache_seqlens=context_lens, block_table=block_tables, softmax_scale,    */
+/*   causal=True) at nanokvllm/layers/attention.py:104-107 and               */
+/*   KvChat/layers/attention.py:113-116.                                     */
+/* out[b, h, :] = softmax(scale * q[b,h] . K[b, h/g, t]^T, t < context_lens[b]) V */
+/* with g = num_q_heads / num_kv_heads and keys found through                */
+/* block_tables[b, t / block_size]. context_lens[b] == 0 writes zeros.       */
+/* q rows: q + b*q_stride_token + h*q_stride_head (head_dim contiguous).     */
+/* out rows: out + b*out_stride_token + h*head_dim.                          */
+/* Supported: head_dim 128, block_size a multiple of 128, g in [1, 16].      */
+/* The workspace must be zero-filled once before its first use; every call   */
+/* leaves it zeroed again, so one buffer serves all layers and CUDA graphs.  */
+size_t nkv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads,
+                                       int32_t num_kv_heads, int32_t head_dim,
+                                       int32_t max_blocks, int32_t block_size);
+int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks,
+                     const int32_t* block_tables, int32_t max_blocks,
+                     const int32_t* context_lens,
+                     void* out, int64_t out_stride_token,
+                     int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t block_size, float softmax_scale,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 3a. Periodic window compression (one layer, all selected sequences)       */
+/* Replaces: MyCompressCompact, nanokvllm/layers/compress_utils.py:100-263,  */
+/*   with get_tail_window_and_tail_slots (:9-72), gather_kv_by_slots (:75-97) */
+/*   and SnapKV(window=obs_window) (nanokvllm/layers/CompressMethod.py:4-58). */
+/* For selected sequence i (batch row b = selected_batch_indices[i]):        */
+/*   L0 = base_context_lens[b]; the window is the last window_blocks FULL    */
+/*   blocks before position L0; the last obs_window window tokens are kept    */
+/*   and scored against q[b]; SnapKV keeps token 0, the top                   */
+/*   keep_tokens-1-obs_window tokens by summed softmax importance (bf16      */
+/*   rounding points of the reference, ties broken towards the lower index)  */
+/*   and the obs_window last tokens; kept rows are compacted in place to the */
+/*   first keep_tokens slots of the window, the partial tail block follows   */
+/*   them, and context_lens[b] = L0 - window_blocks*block_size + keep_tokens. */
+/* out_keep_idx (optional, [num_selected, keep_tokens]) receives the window-  */
+/* relative kept indices; out_new_lens (optional, [num_selected]) the new     */
+/* lengths. Needs num_kv_heads <= 8 (one thread-block cluster per sequence). */
+/* The caller guarantees what the reference asserts (full_blocks >=          */
+/* window_blocks); rows violating it are skipped and flag                    */
+/* NKV_DEVERR_COMPRESS_RANGE.                                                */
+int nkv_window_compress(const void* q, int64_t q_stride_token,
+                        void* k_cache, void* v_cache, int64_t num_blocks,
+                        const int32_t* block_tables, int32_t max_blocks,
+                        const int32_t* base_context_lens, int32_t* context_lens,
+                        const int32_t* selected_batch_indices, int32_t num_selected,
+                        int32_t window_blocks, int32_t keep_tokens, int32_t obs_window,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t block_size, float softmax_scale,
+                        int32_t* out_keep_idx, int32_t* out_new_lens, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 3b. KvChat query window: append this step's queries of active sequences  */
+/* Replaces: QueryWindowManager.append, KvChat/engine/query_window_manager.py:46-58 */
+/* (the Python loop of per-sequence copy_ calls).                            */
+/* ring is [num_ring_slots, num_layers, window_size, num_q_heads, head_dim]. */
+/* For active row j: ring[ring_slot[j], layer_id, ring_pos[j], :, :] =        */
+/*   q[batch_index[j], :, :]. All three index arrays live on the device so    */
+/* the call can sit inside a captured CUDA graph.                            */
+int nkv_query_window_append(const void* q, int64_t q_stride_token,
+                            void* ring, int32_t num_ring_slots, int32_t num_layers,
+                            int32_t window_size, int32_t layer_id,
+                            const int32_t* batch_index, const int32_t* ring_slot,
+                            const int32_t* ring_pos, int32_t num_active,
+                            int32_t num_q_heads, int32_t head_dim, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 3c. KvChat threshold compression S -> R (one layer)                       */
+/* Replaces: MyCompressCompact, KvChat/layers/compress_utils.py:10-171, with */
+/*   TritonGetKVForComp (:218-252) and SnapKV(window=W, num_keep=R-W-1)      */
+/*   (KvChat/layers/CompressMethod.py:4-58).                                 */
+/* For selected sequence i (row b): the source window is positions           */
+/* [max(context_lens[b]-S, 0), +S); its first S-W keys are scored by the W   */
+/* ring queries of ring slot ring_slot_of_selected[i] (all heads, all W      */
+/* queries); SnapKV keeps token 0, the top R-W-1 and the last W; kept rows   */
+/* are compacted to positions [0, R) of the sequence's block table and       */
+/* context_lens[b] = R. out_keep_idx is optional ([num_selected, R]).        */
+int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num_layers,
+                           int32_t window_size, int32_t layer_id,
+                           const int32_t* ring_slot_of_selected,
+                           void* k_cache, void* v_cache, int64_t num_blocks,
+                           const int32_t* block_tables, int32_t max_blocks,
+                           int32_t* context_lens,
+                           const int32_t* selected_batch_indices, int32_t num_selected,
+                           int32_t compress_S, int32_t compress_R,
+                           int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                           int32_t block_size, float softmax_scale,
+                           int32_t* out_keep_idx, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* NKV_H_ */

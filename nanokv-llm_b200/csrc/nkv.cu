@@ -1,0 +1,466 @@
+// C-ABI entry points of libnkv.so (declared in include/nkv.h).
+//
+// Host side of every call: validate arguments (returning an nkv_status, never
+// throwing), encode TMA tensor maps where a kernel needs them, pick the launch
+// shape and launch on the caller's stream. No entry point allocates device
+// memory or synchronises the host, so all of them can be captured in a CUDA
+// graph (the reference's decode graphs, model_runner.py:401-441).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "nkv_common.cuh"
+#include "paged_decode.cuh"
+#include "store_kvcache.cuh"
+#include "threshold_compress.cuh"
+#include "window_compress.cuh"
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return NKV_OK;
+  t_last_cuda_error = static_cast<int>(e);
+  return NKV_ERR_CUDA;
+}
+
+int launch_status() { return cuda_status(cudaGetLastError()); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------- devices
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {0};
+std::mutex g_dev_mutex;
+
+int sm_count(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (g_sm_count[dev] == 0) {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+// ---------------------------------------------------------------- TMA encode
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+// 3-D bf16 map {dim0 (contiguous), dim1, dim2} with byte strides for dims 1, 2,
+// box {64, box1, box2} and 128-byte swizzle (64 bf16 = one 128-byte row).
+int encode_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+              uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box1, uint32_t box2,
+              CUtensorMapL2promotion promo) {
+  auto fn = encode_fn();
+  if (!fn) return NKV_ERR_CUDA;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {64, box1, box2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NKV_OK : NKV_ERR_ALIGNMENT;
+}
+
+// ---------------------------------------------------------------- decode plan
+struct DecodePlan {
+  int g;
+  int chunk_blocks;
+  int chunk_tokens;
+  int max_splits;
+  int pairs;
+  size_t off_split_counters, off_part_ml, off_part_o, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Split size depends only on the shapes (not on the device or the lengths), so
+// the workspace query and the launch always agree.
+DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block_size) {
+  DecodePlan pl{};
+  pl.g = hq / hk;
+  pl.pairs = batch * hk;
+  // Aim for >= ~8 work items per SM of a 148-SM part when every row is full,
+  // with splits of 1..4 blocks of 256 tokens.
+  const int64_t block_units = static_cast<int64_t>(pl.pairs) * std::max(max_blocks, 1);
+  const int64_t target_items = 8 * 148;
+  int cb = static_cast<int>(block_units / target_items);
+  const int max_cb = std::max(1, 1024 / block_size);
+  pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
+  pl.chunk_tokens = pl.chunk_blocks * block_size;
+  pl.max_splits = std::max(1, (std::max(max_blocks, 1) + pl.chunk_blocks - 1) / pl.chunk_blocks);
+  size_t off = 256;  // counters header
+  pl.off_split_counters = off;
+  off = align256(off + sizeof(unsigned int) * pl.pairs);
+  pl.off_part_ml = off;
+  off = align256(off + sizeof(float) * 2 * static_cast<size_t>(pl.pairs) * pl.max_splits * pl.g);
+  pl.off_part_o = off;
+  off = align256(off + sizeof(float) * 128 * static_cast<size_t>(pl.pairs) * pl.max_splits * pl.g);
+  pl.total = off;
+  return pl;
+}
+
+template <int G>
+int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tq,
+                  const nkv::DecodeParams& p, cudaStream_t stream) {
+  using S = nkv::DecodeShape<G>;
+  static bool attr_set[kMaxDevices] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nkv::paged_decode_kernel<G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_set[dev] = true;
+  }
+  const int grid = std::max(1, std::min(sm_count(dev), p.total_items));
+  nkv::paged_decode_kernel<G><<<grid, nkv::kDecodeThreads, S::kSmemBytes, stream>>>(tk, tv, tq, p);
+  return launch_status();
+}
+
+int padded_group(int g) {
+  if (g <= 1) return 1;
+  if (g <= 2) return 2;
+  if (g <= 4) return 4;
+  if (g <= 8) return 8;
+  if (g <= 16) return 16;
+  return 0;
+}
+
+size_t window_smem_bytes(int g, int keys_pad, int keep_tokens) {
+  size_t b = 0;
+  b += sizeof(float) * g * nkv::kCompressHeadDim;            // qs
+  b += sizeof(float) * static_cast<size_t>(g) * keys_pad;   // scores
+  b += sizeof(float) * keys_pad;                             // partial
+  b += sizeof(uint16_t) * (keys_pad + 2);                    // keys
+  b += sizeof(int) * keep_tokens;                            // final_idx
+  b += sizeof(int) * (nkv::kMaxWindowBlocks + 32);           // window blocks + reduction
+  return b;
+}
+
+size_t threshold_smem_bytes(int g, int nk, int keys_pad, int R, bool stage) {
+  size_t b = stage ? static_cast<size_t>(nk) * nkv::kCompressHeadDim * 2 : 0;
+  b += sizeof(float) * g * nkv::kCompressHeadDim;
+  b += 2 * sizeof(float) * static_cast<size_t>(g) * keys_pad;
+  b += sizeof(float) * keys_pad;
+  b += sizeof(uint16_t) * (keys_pad + 2);
+  b += sizeof(int) * (R + 32);
+  return b;
+}
+
+constexpr size_t kMaxSmem = 227 * 1024;
+
+template <typename Kernel, typename Params>
+int launch_cluster(Kernel kernel, const Params& p, int cluster_x, int grid_y, size_t smem,
+                   cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_status(e);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster_x, grid_y, 1);
+  cfg.blockDim = dim3(nkv::kCompressThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, p));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* nkv_status_string(int status) {
+  switch (status) {
+    case NKV_OK: return "NKV_OK";
+    case NKV_ERR_INVALID_ARGUMENT: return "NKV_ERR_INVALID_ARGUMENT";
+    case NKV_ERR_UNSUPPORTED: return "NKV_ERR_UNSUPPORTED";
+    case NKV_ERR_WORKSPACE: return "NKV_ERR_WORKSPACE";
+    case NKV_ERR_ALIGNMENT: return "NKV_ERR_ALIGNMENT";
+    case NKV_ERR_CUDA: return "NKV_ERR_CUDA";
+    default: return "NKV_ERR_UNKNOWN";
+  }
+}
+
+int nkv_abi_version(void) { return 100; }
+
+int nkv_last_cuda_error(void) { return t_last_cuda_error; }
+
+int nkv_read_device_error(uint32_t* out_bits, int clear) {
+  if (!out_bits) return NKV_ERR_INVALID_ARGUMENT;
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, nkv::g_nkv_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_status(e);
+  *out_bits = v;
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(nkv::g_nkv_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return NKV_OK;
+}
+
+// ------------------------------------------------------------------ store
+int nkv_store_kvcache(const void* key, int64_t key_stride, const void* value, int64_t value_stride,
+                      void* k_cache, void* v_cache, int64_t num_slots,
+                      const int32_t* slot_mapping, int32_t num_tokens, int32_t num_kv_heads,
+                      int32_t head_dim, void* stream) {
+  if (num_tokens < 0 || num_slots < 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0 || num_slots == 0) return NKV_OK;
+  if (!key || !value || !k_cache || !v_cache || !slot_mapping) return NKV_ERR_INVALID_ARGUMENT;
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if ((row % 8) != 0 || (key_stride % 8) != 0 || (value_stride % 8) != 0 || !aligned16(key) ||
+      !aligned16(value) || !aligned16(k_cache) || !aligned16(v_cache))
+    return NKV_ERR_ALIGNMENT;
+  if (key_stride < row || value_stride < row) return NKV_ERR_INVALID_ARGUMENT;
+  const int blocks = (num_tokens + nkv::kStoreWarpsPerBlock - 1) / nkv::kStoreWarpsPerBlock;
+  nkv::store_kvcache_kernel<<<blocks, nkv::kStoreWarpsPerBlock * 32, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(key), key_stride / 8, static_cast<const uint4*>(value),
+      value_stride / 8, static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), num_slots,
+      slot_mapping, num_tokens, static_cast<int32_t>(row / 8));
+  return launch_status();
+}
+
+// ------------------------------------------------------------------ decode
+size_t nkv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                       int32_t head_dim, int32_t max_blocks, int32_t block_size) {
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || block_size <= 0 ||
+      num_q_heads % num_kv_heads != 0)
+    return 0;
+  (void)head_dim;
+  return make_decode_plan(batch, num_q_heads, num_kv_heads, max_blocks, block_size).total;
+}
+
+int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks,
+                     const int32_t* block_tables, int32_t max_blocks, const int32_t* context_lens,
+                     void* out, int64_t out_stride_token, int32_t batch, int32_t num_q_heads,
+                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                     float softmax_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_blocks < 0 || num_blocks < 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return NKV_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (num_q_heads % num_kv_heads != 0) return NKV_ERR_INVALID_ARGUMENT;
+  if (head_dim != nkv::kDecodeHeadDim || block_size <= 0 ||
+      block_size % nkv::kDecodeTileTokens != 0)
+    return NKV_ERR_UNSUPPORTED;
+  const int g = num_q_heads / num_kv_heads;
+  const int G = padded_group(g);
+  if (G == 0) return NKV_ERR_UNSUPPORTED;
+  if (!std::isfinite(softmax_scale)) return NKV_ERR_INVALID_ARGUMENT;
+  if (out_stride_token < static_cast<int64_t>(num_q_heads) * head_dim) return NKV_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (q_stride_token % 8) ||
+      (q_stride_head % 8))
+    return NKV_ERR_ALIGNMENT;
+  const DecodePlan pl = make_decode_plan(batch, num_q_heads, num_kv_heads, max_blocks, block_size);
+  if (!workspace || workspace_bytes < pl.total) return NKV_ERR_WORKSPACE;
+  if (num_blocks == 0 || max_blocks == 0) num_blocks = std::max<int64_t>(num_blocks, 0);
+
+  const uint64_t num_slots = static_cast<uint64_t>(std::max<int64_t>(num_blocks, 1)) * block_size;
+  const uint64_t row_bytes = static_cast<uint64_t>(num_kv_heads) * head_dim * 2;
+  CUtensorMap tk, tv, tq;
+  int st;
+  if ((st = encode_3d(&tk, k_cache, head_dim, num_kv_heads, num_slots, head_dim * 2, row_bytes,
+                      1, nkv::kDecodeTileTokens, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
+    return st;
+  if ((st = encode_3d(&tv, v_cache, head_dim, num_kv_heads, num_slots, head_dim * 2, row_bytes,
+                      1, nkv::kDecodeTileTokens, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
+    return st;
+  if ((st = encode_3d(&tq, q, head_dim, num_q_heads, batch, q_stride_head * 2, q_stride_token * 2,
+                      g, 1, CU_TENSOR_MAP_L2_PROMOTION_NONE)) != NKV_OK)
+    return st;
+
+  nkv::DecodeParams p{};
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_token = out_stride_token;
+  p.num_blocks = num_blocks;
+  p.counters = reinterpret_cast<unsigned int*>(ws);
+  p.split_counters = reinterpret_cast<unsigned int*>(ws + pl.off_split_counters);
+  p.part_ml = reinterpret_cast<float*>(ws + pl.off_part_ml);
+  p.part_o = reinterpret_cast<float*>(ws + pl.off_part_o);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.max_blocks = max_blocks;
+  p.batch = batch;
+  p.num_kv_heads = num_kv_heads;
+  p.g = g;
+  p.block_size = block_size;
+  p.chunk_tokens = pl.chunk_tokens;
+  p.max_splits = pl.max_splits;
+  p.total_items = pl.pairs * pl.max_splits;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (G) {
+    case 1: return launch_decode<1>(tk, tv, tq, p, s);
+    case 2: return launch_decode<2>(tk, tv, tq, p, s);
+    case 4: return launch_decode<4>(tk, tv, tq, p, s);
+    case 8: return launch_decode<8>(tk, tv, tq, p, s);
+    default: return launch_decode<16>(tk, tv, tq, p, s);
+  }
+}
+
+// ------------------------------------------------------------------ window compress
+int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, void* v_cache,
+                        int64_t num_blocks, const int32_t* block_tables, int32_t max_blocks,
+                        const int32_t* base_context_lens, int32_t* context_lens,
+                        const int32_t* selected_batch_indices, int32_t num_selected,
+                        int32_t window_blocks, int32_t keep_tokens, int32_t obs_window,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t block_size, float softmax_scale, int32_t* out_keep_idx,
+                        int32_t* out_new_lens, void* stream) {
+  if (num_selected < 0) return NKV_ERR_INVALID_ARGUMENT;
+  if (num_selected == 0) return NKV_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !base_context_lens || !context_lens ||
+      !selected_batch_indices)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return NKV_ERR_INVALID_ARGUMENT;
+  if (head_dim != nkv::kCompressHeadDim || num_kv_heads > 8 || obs_window != 1 || block_size <= 0)
+    return NKV_ERR_UNSUPPORTED;
+  const int g = num_q_heads / num_kv_heads;
+  if (g > 16) return NKV_ERR_UNSUPPORTED;
+  if (window_blocks <= 0 || window_blocks > nkv::kMaxWindowBlocks) return NKV_ERR_UNSUPPORTED;
+  const int window_tokens = window_blocks * block_size;
+  // SnapKV's own guard (CompressMethod.py:17-18) is the caller's job: the
+  // Python layer skips the call, as the reference returns False.
+  const int num_keep = keep_tokens - 1 - obs_window;
+  if (window_tokens - obs_window <= 0 || window_tokens <= num_keep + obs_window || num_keep < 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (q_stride_token % 8))
+    return NKV_ERR_ALIGNMENT;
+  nkv::WindowCompressParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_stride_token = q_stride_token;
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.num_blocks = num_blocks;
+  p.block_tables = block_tables;
+  p.base_lens = base_context_lens;
+  p.context_lens = context_lens;
+  p.selected = selected_batch_indices;
+  p.out_keep_idx = out_keep_idx;
+  p.out_new_lens = out_new_lens;
+  p.scale = softmax_scale;
+  p.max_blocks = max_blocks;
+  p.window_blocks = window_blocks;
+  p.keep_tokens = keep_tokens;
+  p.obs_window = obs_window;
+  p.num_kv_heads = num_kv_heads;
+  p.g = g;
+  p.block_size = block_size;
+  p.num_keys = window_tokens - obs_window;
+  p.keys_pad = ((p.num_keys + nkv::kCompressThreads - 1) / nkv::kCompressThreads) * nkv::kCompressThreads;
+  const size_t smem = window_smem_bytes(g, p.keys_pad, keep_tokens);
+  if (smem > kMaxSmem) return NKV_ERR_UNSUPPORTED;
+  return launch_cluster(nkv::window_compress_kernel, p, num_kv_heads, num_selected, smem,
+                        static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------ KvChat
+int nkv_query_window_append(const void* q, int64_t q_stride_token, void* ring,
+                            int32_t num_ring_slots, int32_t num_layers, int32_t window_size,
+                            int32_t layer_id, const int32_t* batch_index, const int32_t* ring_slot,
+                            const int32_t* ring_pos, int32_t num_active, int32_t num_q_heads,
+                            int32_t head_dim, void* stream) {
+  if (num_active < 0) return NKV_ERR_INVALID_ARGUMENT;
+  if (num_active == 0) return NKV_OK;
+  if (!q || !ring || !batch_index || !ring_slot || !ring_pos) return NKV_ERR_INVALID_ARGUMENT;
+  if (num_ring_slots <= 0 || num_layers <= 0 || window_size <= 0 || layer_id < 0 ||
+      layer_id >= num_layers || num_q_heads <= 0 || head_dim <= 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  const int64_t row = static_cast<int64_t>(num_q_heads) * head_dim;
+  if ((row % 8) || (q_stride_token % 8) || !aligned16(q) || !aligned16(ring)) return NKV_ERR_ALIGNMENT;
+  nkv::query_window_append_kernel<<<num_active, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q), q_stride_token, static_cast<__nv_bfloat16*>(ring),
+      num_ring_slots, num_layers, window_size, layer_id, batch_index, ring_slot, ring_pos,
+      static_cast<int>(row / 8));
+  return launch_status();
+}
+
+int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num_layers,
+                           int32_t window_size, int32_t layer_id,
+                           const int32_t* ring_slot_of_selected, void* k_cache, void* v_cache,
+                           int64_t num_blocks, const int32_t* block_tables, int32_t max_blocks,
+                           int32_t* context_lens, const int32_t* selected_batch_indices,
+                           int32_t num_selected, int32_t compress_S, int32_t compress_R,
+                           int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                           int32_t block_size, float softmax_scale, int32_t* out_keep_idx,
+                           void* stream) {
+  if (num_selected < 0) return NKV_ERR_INVALID_ARGUMENT;
+  if (num_selected == 0) return NKV_OK;
+  if (!ring || !ring_slot_of_selected || !k_cache || !v_cache || !block_tables || !context_lens ||
+      !selected_batch_indices)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return NKV_ERR_INVALID_ARGUMENT;
+  if (head_dim != nkv::kCompressHeadDim || num_kv_heads > 8 || block_size <= 0) return NKV_ERR_UNSUPPORTED;
+  const int g = num_q_heads / num_kv_heads;
+  const int W = window_size;
+  const int num_keep = compress_R - W - 1;
+  if (W <= 0 || compress_S - W <= 0 || compress_S <= num_keep + W || num_keep < 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (!aligned16(ring) || !aligned16(k_cache) || !aligned16(v_cache)) return NKV_ERR_ALIGNMENT;
+  nkv::ThresholdCompressParams p{};
+  p.ring = static_cast<const __nv_bfloat16*>(ring);
+  p.ring_slot_of_selected = ring_slot_of_selected;
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.num_blocks = num_blocks;
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.selected = selected_batch_indices;
+  p.out_keep_idx = out_keep_idx;
+  p.scale = softmax_scale;
+  p.num_ring_slots = num_ring_slots;
+  p.num_layers = num_layers;
+  p.window = W;
+  p.layer_id = layer_id;
+  p.max_blocks = max_blocks;
+  p.S = compress_S;
+  p.R = compress_R;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.g = g;
+  p.block_size = block_size;
+  p.num_keys = compress_S - W;
+  p.keys_pad = ((p.num_keys + nkv::kCompressThreads - 1) / nkv::kCompressThreads) * nkv::kCompressThreads;
+  size_t smem = threshold_smem_bytes(g, p.num_keys, p.keys_pad, compress_R, true);
+  p.stage_keys = 1;
+  if (smem > kMaxSmem) {
+    smem = threshold_smem_bytes(g, p.num_keys, p.keys_pad, compress_R, false);
+    p.stage_keys = 0;
+  }
+  if (smem > kMaxSmem) return NKV_ERR_UNSUPPORTED;
+  return launch_cluster(nkv::threshold_compress_kernel, p, num_kv_heads, num_selected, smem,
+                        static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

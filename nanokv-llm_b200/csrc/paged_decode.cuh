@@ -1,0 +1,513 @@
+// Paged split-KV decode attention for sm_100a: the B200 replacement for
+// flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache, cache_seqlens,
+// block_table, softmax_scale, causal=True) at nanokvllm/layers/attention.py:104-107.
+//
+// Design (HBM-bound: every K/V byte is read exactly once per step):
+//   * Work item = (split s, batch row b, kv head h): up to `chunk` tokens of
+//     one sequence for one kv head and ALL g = Hq/Hk query heads of that group
+//     (GQA grouping: a K/V tile is read once for the whole group).
+//   * Persistent CTAs (one per SM). Warp 4 is the producer: one lane grabs
+//     work items from a global atomic counter (dynamic load balance over the
+//     ragged context lengths), resolves block_tables and streams 128-token K
+//     and V tiles with cp.async.bulk.tensor (TMA, 128B swizzle, L2 evict_first)
+//     into a 3-stage shared-memory ring guarded by full/empty mbarriers. The
+//     item's query rows arrive in the same transaction as its first tile.
+//   * Warps 0-3 consume: each owns 32 tokens of every tile, computes
+//     S = Q K^T with mma.sync m16n8k16 (query heads on M, padded to 16),
+//     keeps a warp-private online softmax (exp2 domain), and accumulates
+//     O += P V with the probabilities re-packed from the S accumulators as the
+//     A operand. At the end of an item the four warp states are merged through
+//     shared memory in a fixed order (deterministic).
+//   * Split combine without a second launch: a multi-split item writes its
+//     unnormalised partial (O, m, l) to the workspace; the last split to arrive
+//     (per-(b,h) atomic counter, reset by that CTA) merges all partials and
+//     writes the bf16 output. The work counter is reset by the last CTA to
+//     finish, so the workspace stays zeroed between calls and inside graphs.
+//   * Tokens past context_lens in the last tile are masked in S (select, not
+//     arithmetic) and their V rows are zeroed in registers, so uninitialised
+//     cache memory (NaN patterns) never reaches the output.
+//
+// Tensor cores: the group width g (2..8 for Qwen3) is too narrow for tcgen05's
+// M >= 64 tiles without wasting >= 87% of each instruction, and the kernel is
+// bandwidth-bound by ~60x, so the warp-level mma.sync path keeps ALU work off
+// the critical path while TMA does the address generation for the gathers.
+#pragma once
+#include "nkv_common.cuh"
+
+namespace nkv {
+
+constexpr int kDecodeHeadDim = 128;
+constexpr int kDecodeTileTokens = 128;       // tokens per pipeline stage
+constexpr int kDecodeConsumerWarps = 4;
+constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
+constexpr int kHalfTileBytes = kDecodeTileTokens * 128;  // 128 rows x 64 dims x 2 B
+constexpr int kDecodeMetaInts = 8;
+
+template <int G>
+struct DecodeShape {
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8 || G == 16, "padded group width");
+  static constexpr int kStages = (G <= 8) ? 3 : 2;
+  static constexpr int kQRows = (G < 8) ? 8 : G;
+  static constexpr int kQHalfBytes = ((kQRows * 128 + 1023) / 1024) * 1024;
+  static constexpr int kStageBytes = 4 * kHalfTileBytes + 2 * kQHalfBytes;
+  static constexpr int kCoRowStride = kDecodeHeadDim + 8;  // floats, padded vs bank conflicts
+  static constexpr int kCombineBytes = kDecodeConsumerWarps * G * kCoRowStride * 4;
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kCombineBytes + 2 * kDecodeConsumerWarps * G * 4 +
+      kStages * (16 + kDecodeMetaInts * 4) + 8 + 64 + 1024 /* alignment slack */;
+};
+
+struct DecodeParams {
+  const int32_t* block_tables;
+  const int32_t* context_lens;
+  __nv_bfloat16* out;
+  int64_t out_stride_token;
+  int64_t num_blocks;
+  unsigned int* counters;        // [0] work counter, [1] finished-CTA counter
+  unsigned int* split_counters;  // [batch * num_kv_heads]
+  float* part_o;                 // [pairs, max_splits, g, 128]
+  float* part_ml;                // [pairs, max_splits, g, 2]
+  float scale_log2;
+  int max_blocks;
+  int batch;
+  int num_kv_heads;
+  int g;
+  int block_size;
+  int chunk_tokens;
+  int max_splits;
+  int total_items;
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kDecodeThreads, 1)
+paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ CUtensorMap tm_q, const DecodeParams p) {
+  using S = DecodeShape<G>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_mem = smem;
+  float* co = reinterpret_cast<float*>(smem + kStages * S::kStageBytes);
+  float* cm = co + kDecodeConsumerWarps * G * S::kCoRowStride;
+  float* cl = cm + kDecodeConsumerWarps * G;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(cl + kDecodeConsumerWarps * G);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* cons_bar = empty_bar + kStages;  // bounded barrier among the 128 consumer threads
+  int* meta = reinterpret_cast<int*>(cons_bar + 1);
+  volatile int* flags = meta + kStages * kDecodeMetaInts;  // [0] abort, [1] last-split
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), kDecodeConsumerWarps);
+    }
+    mbar_init(smem_u32(cons_bar), kDecodeConsumerWarps * 32);
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_barrier_init();
+  }
+  if (warp == kDecodeConsumerWarps && lane == 0) {
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    prefetch_tmap(&tm_q);
+  }
+  __syncthreads();
+
+  const int Hk = p.num_kv_heads;
+  const int g = p.g;
+
+  if (warp == kDecodeConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    const uint64_t pol_stream = l2_policy_evict_first();
+    const uint64_t pol_q = l2_policy_evict_last();
+    const uint32_t q_bytes = static_cast<uint32_t>(2 * g * 128);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    // armed[s] = parity + 1 of the last TMA transaction issued into stage s
+    // that the producer has not yet seen released (0 = none outstanding).
+    uint32_t armed[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) armed[s] = 0;
+    while (ok) {
+      const int item = static_cast<int>(atomicAdd(&p.counters[0], 1u));
+      if (item >= p.total_items) break;
+      const int kvh = item % Hk;
+      const int rest = item / Hk;
+      const int b = rest % p.batch;
+      const int s = rest / p.batch;
+      const int len = __ldg(p.context_lens + b);
+      const int nsplit = len > 0 ? (len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
+      if (s >= nsplit) continue;
+      const int t0 = s * p.chunk_tokens;
+      const int t1 = min(t0 + p.chunk_tokens, len);
+      const int ntiles = len > 0 ? (t1 - t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
+      int j = 0;
+      do {
+        if (flags[0] || !mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) {
+          ok = false;
+          flags[0] = 1;
+          break;
+        }
+        armed[stage] = 0;
+        int* m = meta + stage * kDecodeMetaInts;
+        const int tok = t0 + j * kDecodeTileTokens;
+        m[0] = item;
+        m[1] = j;
+        m[2] = ntiles;
+        m[3] = ntiles > 0 ? min(kDecodeTileTokens, t1 - tok) : 0;
+        m[4] = nsplit;
+        const uint32_t fb = smem_u32(&full_bar[stage]);
+        if (ntiles == 0) {
+          mbar_arrive(fb);
+        } else {
+          int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
+                          tok / p.block_size);
+          int slot;
+          if (blk < 0 || static_cast<int64_t>(blk) >= p.num_blocks) {
+            raise_error(NKV_DEVERR_DECODE_BLOCK);
+            slot = -2 * kDecodeTileTokens;  // fully out of range: TMA fills zeros
+          } else {
+            slot = blk * p.block_size + (tok % p.block_size);
+          }
+          const uint32_t bytes = 4u * kHalfTileBytes + (j == 0 ? q_bytes : 0u);
+          mbar_arrive_expect_tx(fb, bytes);
+          armed[stage] = phase + 1u;
+          const uint32_t base = smem_u32(stage_mem + stage * S::kStageBytes);
+          tma_load_3d(base + 0 * kHalfTileBytes, &tm_k, fb, 0, kvh, slot, pol_stream);
+          tma_load_3d(base + 1 * kHalfTileBytes, &tm_k, fb, 64, kvh, slot, pol_stream);
+          tma_load_3d(base + 2 * kHalfTileBytes, &tm_v, fb, 0, kvh, slot, pol_stream);
+          tma_load_3d(base + 3 * kHalfTileBytes, &tm_v, fb, 64, kvh, slot, pol_stream);
+          if (j == 0) {
+            const uint32_t qb = base + 4 * kHalfTileBytes;
+            tma_load_3d(qb, &tm_q, fb, 0, kvh * g, b, pol_q);
+            tma_load_3d(qb + S::kQHalfBytes, &tm_q, fb, 64, kvh * g, b, pol_q);
+          }
+        }
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      } while (++j < ntiles);
+    }
+    if (ok) {
+      // End-of-work marker for the consumers.
+      if (mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) {
+        meta[stage * kDecodeMetaInts + 0] = -1;
+        mbar_arrive(smem_u32(&full_bar[stage]));
+      } else {
+        flags[0] = 1;
+      }
+    }
+    // Drain: never leave the CTA with a bulk copy still writing its shared
+    // memory (only matters after an abort; normally these return at once).
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      if (armed[s]) mbar_wait_bounded(smem_u32(&full_bar[s]), armed[s] - 1u);
+    }
+    // The last CTA out resets the scheduler counters for the next call.
+    __threadfence();
+    const unsigned int prev = atomicAdd(&p.counters[1], 1u);
+    if (prev == gridDim.x - 1) {
+      atomicExch(&p.counters[0], 0u);
+      atomicExch(&p.counters[1], 0u);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int cw = warp;
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  const int ctid = threadIdx.x;  // 0..127
+  const float scale_log2 = p.scale_log2;
+  const float NEG_INF = -INFINITY;
+
+  // Bounded barrier over the 128 consumer threads (an mbarrier with 128
+  // arrivals per phase): unlike bar.sync it cannot hang if a warp aborted.
+  uint32_t cons_phase = 0;
+  bool alive = true;
+  auto consumer_sync = [&]() {
+    mbar_arrive(smem_u32(cons_bar));
+    if (!mbar_wait_bounded(smem_u32(cons_bar), cons_phase)) {
+      flags[0] = 1;
+      alive = false;
+    }
+    cons_phase ^= 1u;
+  };
+
+  float o[16][4];
+  float m_run[2], l_run[2];
+  uint32_t qa[8][4];
+  int cur_b = 0, cur_kvh = 0, cur_s = 0;
+
+  int stage = 0;
+  uint32_t phase = 0;
+  while (true) {
+    if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), phase)) {
+      flags[0] = 1;
+      break;
+    }
+    const int* m = meta + stage * kDecodeMetaInts;
+    const int item = m[0];
+    if (item < 0) break;
+    const int j = m[1];
+    const int ntiles = m[2];
+    const int nvalid = m[3];
+    const int nsplit = m[4];
+    const uint8_t* sbase = stage_mem + stage * S::kStageBytes;
+
+    if (j == 0) {
+      cur_kvh = item % Hk;
+      const int rest = item / Hk;
+      cur_b = rest % p.batch;
+      cur_s = rest / p.batch;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      m_run[0] = m_run[1] = NEG_INF;
+      l_run[0] = l_run[1] = 0.f;
+      if (ntiles > 0) {
+        const uint8_t* q0 = sbase + 4 * kHalfTileBytes;
+        const uint8_t* q1 = q0 + S::kQHalfBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint8_t* qh = (kk < 4) ? q0 : q1;
+          const uint32_t c = 2u * (kk & 3);
+          uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+          if (gid < g) {
+            a0 = *reinterpret_cast<const uint32_t*>(qh + swz128(gid, c) + 4 * tig);
+            a2 = *reinterpret_cast<const uint32_t*>(qh + swz128(gid, c + 1) + 4 * tig);
+          }
+          if (G == 16 && gid + 8 < g) {
+            a1 = *reinterpret_cast<const uint32_t*>(qh + swz128(gid + 8, c) + 4 * tig);
+            a3 = *reinterpret_cast<const uint32_t*>(qh + swz128(gid + 8, c + 1) + 4 * tig);
+          }
+          qa[kk][0] = a0;
+          qa[kk][1] = a1;
+          qa[kk][2] = a2;
+          qa[kk][3] = a3;
+        }
+      }
+    }
+
+    const int tok_base = cw * 32;
+    if (ntiles > 0 && tok_base < nvalid) {
+      const uint32_t sK0 = smem_u32(sbase);
+      const uint32_t sK1 = sK0 + kHalfTileBytes;
+      const uint32_t sV0 = sK0 + 2 * kHalfTileBytes;
+      const uint32_t sV1 = sK0 + 3 * kHalfTileBytes;
+      float sacc[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+      // S = Q K^T over this warp's 32 tokens.
+#pragma unroll
+      for (int kp = 0; kp < 4; ++kp) {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const uint32_t r = tok_base + nt * 8 + (lane & 7);
+          const uint32_t c16 = kp * 4 + (lane >> 3);
+          const uint32_t addr = ((c16 < 8) ? sK0 : sK1) + swz128(r, c16 & 7u);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(addr, b0, b1, b2, b3);
+          mma_bf16_16816(sacc[nt], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3],
+                         b0, b1);
+          mma_bf16_16816(sacc[nt], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2],
+                         qa[2 * kp + 1][3], b2, b3);
+        }
+      }
+      const bool partial = (tok_base + 32 > nvalid);
+      // Online softmax, rows gid (and gid + 8 when G == 16).
+      constexpr int kRowSets = (G == 16) ? 2 : 1;
+      float pr[4][4];
+#pragma unroll
+      for (int rs = 0; rs < kRowSets; ++rs) {
+        float mx = NEG_INF;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float v = sacc[nt][2 * rs + e] * scale_log2;
+            const int tk = tok_base + nt * 8 + 2 * tig + e;
+            if (partial && tk >= nvalid) v = NEG_INF;
+            sacc[nt][2 * rs + e] = v;
+            mx = fmaxf(mx, v);
+          }
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run[rs], mx);
+        const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
+        const float alpha = fast_exp2(m_run[rs] - m_use);
+        m_run[rs] = m_new;
+        float rsum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float pv = fast_exp2(sacc[nt][2 * rs + e] - m_use);
+            pr[nt][2 * rs + e] = pv;
+            rsum += pv;
+          }
+        }
+        l_run[rs] = l_run[rs] * alpha + rsum;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[n][2 * rs + 0] *= alpha;
+          o[n][2 * rs + 1] *= alpha;
+        }
+      }
+      // O += P V over the warp's two 16-token k-steps.
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const uint32_t a0 = pack_bf16x2(pr[2 * jj][0], pr[2 * jj][1]);
+        const uint32_t a2 = pack_bf16x2(pr[2 * jj + 1][0], pr[2 * jj + 1][1]);
+        const uint32_t a1 = (G == 16) ? pack_bf16x2(pr[2 * jj][2], pr[2 * jj][3]) : 0u;
+        const uint32_t a3 = (G == 16) ? pack_bf16x2(pr[2 * jj + 1][2], pr[2 * jj + 1][3]) : 0u;
+        uint32_t mask_lo = 0xffffffffu, mask_hi = 0xffffffffu;
+        if (partial) {
+          const int ta = tok_base + 16 * jj + 2 * tig;
+          mask_lo = (ta < nvalid ? 0x0000ffffu : 0u) | (ta + 1 < nvalid ? 0xffff0000u : 0u);
+          mask_hi = (ta + 8 < nvalid ? 0x0000ffffu : 0u) | (ta + 9 < nvalid ? 0xffff0000u : 0u);
+        }
+        const int mi = lane >> 3;
+        const uint32_t r = tok_base + 16 * jj + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int dp = 0; dp < 8; ++dp) {
+          const uint32_t c16 = 2 * dp + (mi >> 1);
+          const uint32_t addr = ((c16 < 8) ? sV0 : sV1) + swz128(r, c16 & 7u);
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_trans(addr, v0, v1, v2, v3);
+          v0 &= mask_lo;
+          v2 &= mask_lo;
+          v1 &= mask_hi;
+          v3 &= mask_hi;
+          mma_bf16_16816(o[2 * dp], a0, a1, a2, a3, v0, v1);
+          mma_bf16_16816(o[2 * dp + 1], a0, a1, a2, a3, v2, v3);
+        }
+      }
+    }
+
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty_bar[stage]));
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+
+    if (j + 1 < ntiles) continue;
+
+    // ---------------------------------------------------- item epilogue
+    constexpr int kRowSets = (G == 16) ? 2 : 1;
+#pragma unroll
+    for (int rs = 0; rs < kRowSets; ++rs) {
+      float l = l_run[rs];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      l_run[rs] = l;
+      const int row = gid + 8 * rs;
+      if (tig == 0 && row < g) {
+        cm[cw * G + row] = m_run[rs];
+        cl[cw * G + row] = l;
+      }
+    }
+    consumer_sync();
+    if (!alive) break;
+#pragma unroll
+    for (int rs = 0; rs < kRowSets; ++rs) {
+      const int row = gid + 8 * rs;
+      if (row < g) {
+        float M = NEG_INF;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, cm[w * G + row]);
+        const float f = (m_run[rs] == NEG_INF) ? 0.f : fast_exp2(m_run[rs] - M);
+        float* dst = co + (cw * G + row) * S::kCoRowStride;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          *reinterpret_cast<float2*>(dst + 8 * n + 2 * tig) =
+              make_float2(o[n][2 * rs] * f, o[n][2 * rs + 1] * f);
+        }
+      }
+    }
+    consumer_sync();
+    if (!alive) break;
+
+    const int pair = cur_b * Hk + cur_kvh;
+    for (int row = 0; row < g; ++row) {
+      float M = NEG_INF;
+#pragma unroll
+      for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, cm[w * G + row]);
+      float L = 0.f, acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+        const float mw = cm[w * G + row];
+        const float f = (mw == NEG_INF) ? 0.f : fast_exp2(mw - M);
+        L += cl[w * G + row] * f;
+        acc += co[(w * G + row) * S::kCoRowStride + ctid];
+      }
+      if (nsplit == 1) {
+        const float v = (L > 0.f) ? acc / L : 0.f;
+        p.out[static_cast<int64_t>(cur_b) * p.out_stride_token +
+              static_cast<int64_t>(cur_kvh * g + row) * kDecodeHeadDim + ctid] =
+            __float2bfloat16_rn(v);
+      } else {
+        const int64_t pidx = (static_cast<int64_t>(pair) * p.max_splits + cur_s) * g + row;
+        p.part_o[pidx * kDecodeHeadDim + ctid] = acc;
+        if (ctid == 0) {
+          p.part_ml[pidx * 2 + 0] = M;
+          p.part_ml[pidx * 2 + 1] = L;
+        }
+      }
+    }
+    if (nsplit > 1) {
+      __threadfence();
+      consumer_sync();
+      if (!alive) break;
+      if (ctid == 0) {
+        const unsigned int prev = atomicAdd(&p.split_counters[pair], 1u);
+        const int last = (prev == static_cast<unsigned int>(nsplit - 1)) ? 1 : 0;
+        if (last) atomicExch(&p.split_counters[pair], 0u);
+        flags[1] = last;
+      }
+      consumer_sync();
+      if (!alive) break;
+      if (flags[1]) {
+        __threadfence();
+        for (int row = 0; row < g; ++row) {
+          const int64_t base = static_cast<int64_t>(pair) * p.max_splits * g + row;
+          float M = NEG_INF;
+          for (int s2 = 0; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(p.part_ml + (base + s2 * g) * 2));
+          float L = 0.f, acc = 0.f;
+          for (int s2 = 0; s2 < nsplit; ++s2) {
+            const int64_t pi = base + static_cast<int64_t>(s2) * g;
+            const float ms = __ldcg(p.part_ml + pi * 2);
+            const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
+            L += __ldcg(p.part_ml + pi * 2 + 1) * f;
+            acc += __ldcg(p.part_o + pi * kDecodeHeadDim + ctid) * f;
+          }
+          const float v = (L > 0.f) ? acc / L : 0.f;
+          p.out[static_cast<int64_t>(cur_b) * p.out_stride_token +
+                static_cast<int64_t>(cur_kvh * g + row) * kDecodeHeadDim + ctid] =
+              __float2bfloat16_rn(v);
+        }
+      }
+    }
+    consumer_sync();
+    if (!alive) break;
+  }
+  // Consumers leave only after the producer's end marker (or an abort), so
+  // every TMA transaction they waited on has completed.
+}
+
+}  // namespace nkv

@@ -1,0 +1,238 @@
+"""Torch-facing wrappers of the libnkv C ABI (include/nkv.h).
+
+Every function here validates its tensors the way the reference does (the
+same asserts as nanokvllm/layers/attention.py:33-40 for the store), passes raw
+device pointers and the caller's current CUDA stream to the library, and
+raises on a non-zero status. There is no CPU or Triton fallback: CPU tensors
+are rejected.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "store_kvcache",
+    "flash_decode_with_kvcache",
+    "paged_decode",
+    "decode_workspace",
+    "window_compress",
+    "query_window_append",
+    "threshold_compress",
+]
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, *tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"{name}: CUDA tensors required (libnkv has no CPU path)")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------- store
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """Writes key/value rows into their cache slots (slot == -1 is skipped).
+
+    Same contract and asserts as the reference's store_kvcache
+    (nanokvllm/layers/attention.py:33-40).
+    """
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    if N == 0 or k_cache.numel() == 0:
+        return
+    _require_cuda("store_kvcache", key, value, k_cache, v_cache, slot_mapping)
+    assert key.dtype == torch.bfloat16 and k_cache.dtype == torch.bfloat16
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.is_contiguous()
+    num_slots = k_cache.numel() // D
+    lib = _lib.load()
+    _lib.check("nkv_store_kvcache", lib.nkv_store_kvcache(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+        k_cache.data_ptr(), v_cache.data_ptr(), num_slots,
+        slot_mapping.data_ptr(), N, num_heads, head_dim, _stream(key.device)))
+
+
+# ---------------------------------------------------------------- decode
+class _WorkspacePool:
+    """One zero-initialised decode workspace per device, grown on demand.
+
+    The decode kernel leaves its workspace zeroed after every call, so a
+    single buffer serves every layer, step and captured graph. Call
+    `decode_workspace(...)` with the largest shape before capturing a graph so
+    the capture never allocates.
+    """
+
+    def __init__(self):
+        self._bufs: dict[int, torch.Tensor] = {}
+        self._lock = threading.Lock()
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        with self._lock:
+            buf = self._bufs.get(idx)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+                self._bufs[idx] = buf
+            return buf
+
+
+_WS = _WorkspacePool()
+
+
+def decode_workspace_bytes(batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                           max_blocks: int, block_size: int) -> int:
+    return int(_lib.load().nkv_paged_decode_workspace_size(
+        batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size))
+
+
+def decode_workspace(device: torch.device, batch: int, num_q_heads: int, num_kv_heads: int,
+                     head_dim: int, max_blocks: int, block_size: int) -> torch.Tensor:
+    nbytes = decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size)
+    return _WS.get(device, nbytes)
+
+
+def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 block_tables: torch.Tensor, context_lens: torch.Tensor, softmax_scale: float,
+                 out: torch.Tensor | None = None,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention for one query token per sequence over the paged cache.
+
+    q: [B, Hq, D] bf16 (row stride free, head stride multiple of 8);
+    k_cache/v_cache: [num_blocks, block_size, Hk, D]; block_tables [B, max_blocks]
+    int32; context_lens [B] int32. Returns out [B, Hq, D] bf16.
+    """
+    _require_cuda("paged_decode", q, k_cache, v_cache, block_tables, context_lens)
+    B, Hq, D = q.shape
+    num_blocks, block_size, Hk, Dk = k_cache.shape
+    assert Dk == D and v_cache.shape == k_cache.shape
+    assert q.dtype == torch.bfloat16 and k_cache.dtype == torch.bfloat16 and v_cache.dtype == torch.bfloat16
+    assert q.stride(-1) == 1
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert block_tables.dtype == torch.int32 and context_lens.dtype == torch.int32
+    assert block_tables.dim() == 2 and block_tables.size(0) >= B and block_tables.stride(1) == 1
+    assert context_lens.numel() >= B and context_lens.is_contiguous()
+    max_blocks = block_tables.size(1)
+    if block_tables.stride(0) != max_blocks:
+        block_tables = block_tables.contiguous()
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=q.device)
+    assert out.stride(-1) == 1 and out.stride(1) == D
+    if B == 0:
+        return out
+    if workspace is None:
+        workspace = decode_workspace(q.device, B, Hq, Hk, D, max_blocks, block_size)
+    lib = _lib.load()
+    _lib.check("nkv_paged_decode", lib.nkv_paged_decode(
+        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), num_blocks,
+        block_tables.data_ptr(), max_blocks, context_lens.data_ptr(), out.data_ptr(), out.stride(0),
+        B, Hq, Hk, D, block_size, float(softmax_scale), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _stream(q.device)))
+    return out
+
+
+def flash_decode_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                              cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+                              softmax_scale: float | None = None, causal: bool = True,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Drop-in for the reference's flash_attn_with_kvcache decode call
+    (nanokvllm/layers/attention.py:104-107): q is [B, 1, Hq, D], the result
+    is [B, 1, Hq, D]. With one query token `causal` changes nothing."""
+    assert q.dim() == 4 and q.size(1) == 1, "decode path: exactly one query token per sequence"
+    if softmax_scale is None:
+        softmax_scale = q.size(-1) ** -0.5
+    o = paged_decode(q[:, 0], k_cache, v_cache, block_table, cache_seqlens, softmax_scale,
+                     out=None if out is None else out[:, 0])
+    return o.unsqueeze(1)
+
+
+# ---------------------------------------------------------------- window compression
+def window_compress(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    block_tables: torch.Tensor, base_context_lens: torch.Tensor,
+                    context_lens: torch.Tensor, selected: torch.Tensor, window_blocks: int,
+                    keep_tokens: int, obs_window: int = 1, softmax_scale: float | None = None,
+                    out_keep_idx: torch.Tensor | None = None,
+                    out_new_lens: torch.Tensor | None = None) -> None:
+    """Periodic window compression of one layer (SnapKV scoring + compaction).
+
+    `selected` is an int32 device tensor of batch indices; context_lens is
+    updated in place. softmax_scale defaults to SnapKV's 1/sqrt(head_dim).
+    """
+    _require_cuda("window_compress", q, k_cache, v_cache, block_tables, base_context_lens,
+                  context_lens, selected)
+    m = selected.numel()
+    if m == 0:
+        return
+    num_blocks, block_size, Hk, D = k_cache.shape
+    Hq = q.size(1)
+    assert q.stride(-1) == 1 and q.stride(1) == D
+    assert selected.dtype == torch.int32 and selected.is_contiguous()
+    assert block_tables.dtype == torch.int32 and block_tables.is_contiguous()
+    assert base_context_lens.dtype == torch.int32 and context_lens.dtype == torch.int32
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    lib = _lib.load()
+    _lib.check("nkv_window_compress", lib.nkv_window_compress(
+        q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), num_blocks,
+        block_tables.data_ptr(), block_tables.size(1), base_context_lens.data_ptr(),
+        context_lens.data_ptr(), selected.data_ptr(), m, window_blocks, keep_tokens, obs_window,
+        Hq, Hk, D, block_size, float(softmax_scale), _ptr(out_keep_idx), _ptr(out_new_lens),
+        _stream(q.device)))
+
+
+# ---------------------------------------------------------------- KvChat threshold path
+def query_window_append(q: torch.Tensor, ring: torch.Tensor, layer_id: int,
+                        batch_index: torch.Tensor, ring_slot: torch.Tensor,
+                        ring_pos: torch.Tensor) -> None:
+    """ring[ring_slot[j], layer_id, ring_pos[j]] = q[batch_index[j]] for every j."""
+    _require_cuda("query_window_append", q, ring, batch_index, ring_slot, ring_pos)
+    n = batch_index.numel()
+    if n == 0:
+        return
+    slots, layers, W, Hq, D = ring.shape
+    assert q.size(1) == Hq and q.size(2) == D and q.stride(-1) == 1 and q.stride(1) == D
+    assert ring.is_contiguous()
+    lib = _lib.load()
+    _lib.check("nkv_query_window_append", lib.nkv_query_window_append(
+        q.data_ptr(), q.stride(0), ring.data_ptr(), slots, layers, W, layer_id,
+        batch_index.data_ptr(), ring_slot.data_ptr(), ring_pos.data_ptr(), n, Hq, D,
+        _stream(q.device)))
+
+
+def threshold_compress(ring: torch.Tensor, ring_slot_of_selected: torch.Tensor, layer_id: int,
+                       k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                       context_lens: torch.Tensor, selected: torch.Tensor, S: int, R: int,
+                       softmax_scale: float | None = None,
+                       out_keep_idx: torch.Tensor | None = None) -> None:
+    """KvChat threshold compression S -> R of one layer; context_lens[sel] = R."""
+    _require_cuda("threshold_compress", ring, ring_slot_of_selected, k_cache, v_cache,
+                  block_tables, context_lens, selected)
+    m = selected.numel()
+    if m == 0:
+        return
+    slots, layers, W, Hq, D = ring.shape
+    num_blocks, block_size, Hk, Dk = k_cache.shape
+    assert Dk == D and ring.is_contiguous() and block_tables.is_contiguous()
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    lib = _lib.load()
+    _lib.check("nkv_threshold_compress", lib.nkv_threshold_compress(
+        ring.data_ptr(), slots, layers, W, layer_id, ring_slot_of_selected.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), num_blocks, block_tables.data_ptr(),
+        block_tables.size(1), context_lens.data_ptr(), selected.data_ptr(), m, S, R, Hq, Hk, D,
+        block_size, float(softmax_scale), _ptr(out_keep_idx), _stream(k_cache.device)))

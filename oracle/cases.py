@@ -1,0 +1,58 @@
+"""Parameter tables of the golden cases, shared by tests/golden/make_golden.py
+(which runs the reference on them) and the parity tests. Test infrastructure only.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .inputs import CONFIG1, CONFIG1_COMPRESS, bf16, make_paged_batch
+
+SNAPKV_CASES = [
+    # name, seed, m, Hq, Hk, L, window, num_keep, outlier
+    ("cfg1_g2", 101, 2, 16, 8, 1024, 1, 511, 0.0),
+    ("qwen8b_g4", 102, 2, 32, 8, 1024, 1, 511, 0.0),
+    ("qwen8b_g4_outlier", 103, 2, 32, 8, 1024, 1, 511, 4.0),
+    ("qwen32b_g8", 104, 1, 64, 8, 1024, 1, 511, 0.0),
+    ("mha", 105, 1, 8, 8, 1024, 1, 511, 0.0),
+    ("tp8_g4", 106, 3, 4, 1, 1024, 1, 511, 0.0),
+    ("kvchat_w50", 107, 1, 16, 8, 767, 50, 462, 0.0),
+]
+
+
+def snapkv_inputs(seed, m, Hq, Hk, L, window, outlier):
+    rng = np.random.default_rng(seed)
+    Q = rng.standard_normal((m, Hq, window, 128), dtype=np.float32)
+    K = rng.standard_normal((m, Hk, L, 128), dtype=np.float32)
+    if outlier:
+        for h in range(Hk):
+            dims = rng.choice(128, size=6, replace=False)
+            K[:, h, :, dims] *= outlier
+    return bf16(Q), bf16(K)
+
+
+WINDOW_CASES = [
+    # name, paged batch kwargs, selected, window_blocks, keep_blocks, keep_extra
+    ("config1", CONFIG1, CONFIG1_COMPRESS["selected"], 4, 2, 1),
+    ("gqa4_multi", dict(seed=7, lens=[1300, 2100, 1050, 1800, 999, 1024], Hq=32, Hk=8, D=128,
+                        block_size=256, num_blocks=48), [0, 1, 3, 5], 4, 2, 1),
+    ("outlier_g4", dict(seed=8, lens=[2304, 1500], Hq=32, Hk=8, D=128, block_size=256,
+                        num_blocks=20, outlier_sigma=4.0, outlier_frac=0.05), [0, 1], 4, 2, 1),
+]
+
+
+THRESHOLD_CASES = [
+    # name, seed, prompt, Hq, Hk, W, S_cfg, R_cfg, num_layers, compress layer
+    ("cfg5_p256", 21, 256, 16, 8, 50, 511, 257, 1, 0),
+    ("cfg5_p100_rotated", 22, 100, 16, 8, 50, 511, 257, 2, 0),
+]
+
+
+def threshold_inputs(seed: int, P: int, Hq: int, Hk: int, W: int, S_cfg: int, L: int):
+    """Paged batch of one sequence at length S = P + S_cfg plus W steps of
+    per-layer queries [W, L, 1, Hq, 128]."""
+    S = P + S_cfg
+    pb = make_paged_batch(seed=seed, lens=[S], Hq=Hq, Hk=Hk, D=128, block_size=256)
+    rng = np.random.default_rng(seed + 1000)
+    qsteps = bf16(rng.standard_normal((W, L, 1, Hq, 128), dtype=np.float32))
+    return pb, qsteps

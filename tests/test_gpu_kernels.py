@@ -1,0 +1,357 @@
+"""GPU parity of libnkv's kernels against the CPU oracle (which the golden
+vectors pin to the reference). Every call goes through the C ABI via
+nanokv_b200.ops.
+
+Tolerances: store and compaction are bit-exact; decode attention is within
+max-abs 2e-2 and relative (Frobenius) 1e-2 of the fp32 oracle; kept index
+sets are bit-exact against the oracle except for indices whose importance
+lies within one bf16 ulp of the cut (the reference's own rounding grain).
+"""
+
+import json
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention import paged_decode_ref, store_kvcache_ref
+from oracle.cases import THRESHOLD_CASES, WINDOW_CASES, threshold_inputs
+from oracle.inputs import digest, make_paged_batch
+from oracle.snapkv import tie_band_ok
+from oracle.threshold_compress import QueryWindowRef, threshold_compress_ref
+from oracle.window_compress import window_compress_ref, window_importance
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+ATOL = 2e-2
+RTOL = 1e-2
+
+
+def _ops():
+    from nanokv_b200 import ops
+    return ops
+
+
+def _deverr():
+    from nanokv_b200 import _lib
+    return _lib.read_device_error(clear=True)
+
+
+def _bf16_ulp(x: float) -> float:
+    if x == 0:
+        return 0.0
+    e = math.floor(math.log2(abs(x)))
+    return 2.0 ** (e - 7)
+
+
+# ------------------------------------------------------------------ store
+def test_store_kvcache_bit_exact(cuda_lib):
+    ops = _ops()
+    pb = make_paged_batch(seed=3, lens=[5, 300, 256, 1, 700], Hq=16, Hk=8, num_blocks=12)
+    N = 64
+    rng = np.random.default_rng(4)
+    num_slots = pb.k_cache.shape[0] * pb.k_cache.shape[1]
+    slots = rng.choice(num_slots, size=N, replace=False).astype(np.int32)
+    slots[::7] = -1  # graph padding rows
+    slot_mapping = torch.from_numpy(slots)
+    # q/k/v come out of one fused qkv projection: strided rows
+    qkv = torch.randn(N, (16 + 8 + 8) * 128, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    _, k, v = qkv.split([16 * 128, 8 * 128, 8 * 128], dim=-1)
+    k = k.view(N, 8, 128)
+    v = v.view(N, 8, 128)
+    kc, vc = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(k, v, kc, vc, slot_mapping)
+    kc_d, vc_d = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+    qkv_d = qkv.to(DEV)
+    _, kd, vd = qkv_d.split([16 * 128, 8 * 128, 8 * 128], dim=-1)
+    ops.store_kvcache(kd.view(N, 8, 128), vd.view(N, 8, 128), kc_d, vc_d, slot_mapping.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(kc_d.cpu().view(torch.int16), kc.view(torch.int16))
+    assert torch.equal(vc_d.cpu().view(torch.int16), vc.view(torch.int16))
+    assert _deverr() == 0
+
+
+def test_store_kvcache_bad_slot_flags_and_skips(cuda_lib):
+    ops = _ops()
+    kc = torch.zeros(2, 256, 1, 128, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    k = torch.ones(2, 1, 128, dtype=torch.bfloat16, device=DEV)
+    sm = torch.tensor([3, 512], dtype=torch.int32, device=DEV)  # 512 == num_slots: out of range
+    ops.store_kvcache(k, k, kc, vc, sm)
+    torch.cuda.synchronize()
+    assert _deverr() & 0x1
+    assert kc.view(-1, 128)[3].float().sum().item() == 128
+    assert kc.float().sum().item() == 128
+
+
+def test_store_empty_cache_is_noop(cuda_lib):
+    ops = _ops()
+    k = torch.ones(3, 2, 128, dtype=torch.bfloat16, device=DEV)
+    empty = torch.tensor([], device=DEV, dtype=torch.bfloat16)
+    # the reference skips the store while the caches are empty (warm-up)
+    ops.store_kvcache(k, k, empty.view(0, 256), empty.view(0, 256),
+                      torch.zeros(3, dtype=torch.int32, device=DEV))
+
+
+# ------------------------------------------------------------------ decode
+def _check_decode(pb, Hq, scale=None, q=None, nan_tail=False):
+    ops = _ops()
+    D = 128
+    scale = scale if scale is not None else D ** -0.5
+    q = pb.q if q is None else q
+    kc, vc = pb.k_cache.clone(), pb.v_cache.clone()
+    if nan_tail:
+        # poison every slot past each sequence's length inside its last block
+        bs = pb.block_size
+        for b in range(pb.block_tables.size(0)):
+            L = int(pb.context_lens[b])
+            if L > 0 and L % bs:
+                blk = int(pb.block_tables[b, (L - 1) // bs])
+                kc[blk, L % bs:] = float("nan")
+                vc[blk, L % bs:] = float("nan")
+    ref = paged_decode_ref(q, kc, vc, pb.block_tables, pb.context_lens, scale)
+    out = ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), pb.block_tables.to(DEV),
+                           pb.context_lens.to(DEV), scale)
+    torch.cuda.synchronize()
+    o = out.float().cpu()
+    assert torch.isfinite(o).all()
+    diff = (o - ref).abs()
+    rel = (o - ref).norm() / ref.norm().clamp_min(1e-12)
+    assert diff.max().item() <= ATOL, f"max abs {diff.max().item()}"
+    assert rel.item() <= RTOL, f"rel {rel.item()}"
+    assert _deverr() == 0
+    return out
+
+
+def test_decode_config1(cuda_lib):
+    from oracle.inputs import make_config1
+    _check_decode(make_config1(), Hq=16)
+
+
+@pytest.mark.parametrize("Hq,Hk", [(8, 8), (16, 8), (32, 8), (64, 8), (4, 1), (16, 1), (24, 8)])
+def test_decode_group_widths(cuda_lib, Hq, Hk):
+    lens = [1, 2, 127, 128, 129, 255, 256, 257, 600, 1024, 1500, 2049]
+    pb = make_paged_batch(seed=Hq * 10 + Hk, lens=lens, Hq=Hq, Hk=Hk)
+    _check_decode(pb, Hq)
+
+
+def test_decode_zero_length_rows_are_zero(cuda_lib):
+    pb = make_paged_batch(seed=11, lens=[0, 300, 0, 5], Hq=16, Hk=8, num_blocks=4)
+    out = _check_decode(pb, 16)
+    assert torch.count_nonzero(out[0]) == 0 and torch.count_nonzero(out[2]) == 0
+
+
+def test_decode_ignores_nan_past_length(cuda_lib):
+    pb = make_paged_batch(seed=12, lens=[77, 300, 513, 1000], Hq=32, Hk=8)
+    _check_decode(pb, 32, nan_tail=True)
+
+
+def test_decode_strided_q_and_scale(cuda_lib):
+    pb = make_paged_batch(seed=13, lens=[900, 33, 4000], Hq=32, Hk=8)
+    wide = torch.zeros(3, 48, 128, dtype=torch.bfloat16)
+    wide[:, 8:40] = pb.q
+    q = wide[:, 8:40]  # row stride 48*128, head stride 128
+    _check_decode(pb, 32, scale=0.05, q=q)
+
+
+def test_decode_long_context_many_splits(cuda_lib):
+    pb = make_paged_batch(seed=14, lens=[32768, 9000], Hq=64, Hk=8)
+    _check_decode(pb, 64)
+
+
+def test_decode_config2_shape_subset(cuda_lib):
+    """Qwen3-8B shapes (Hq 32, Hk 8) with BASELINE config 2's length law
+    U[1024, 8192] on a 48-sequence subset."""
+    rng = np.random.default_rng(0)
+    lens = rng.integers(1024, 8193, 48).tolist()
+    pb = make_paged_batch(seed=15, lens=lens, Hq=32, Hk=8)
+    _check_decode(pb, 32)
+
+
+def test_decode_repeated_calls_reuse_workspace(cuda_lib):
+    """The workspace must come back zeroed: many calls, same results."""
+    ops = _ops()
+    pb = make_paged_batch(seed=16, lens=[3000, 100, 2500, 7000], Hq=32, Hk=8)
+    args = (pb.q.to(DEV), pb.k_cache.to(DEV), pb.v_cache.to(DEV), pb.block_tables.to(DEV),
+            pb.context_lens.to(DEV), 128 ** -0.5)
+    first = ops.paged_decode(*args).clone()
+    for _ in range(5):
+        again = ops.paged_decode(*args)
+        assert torch.equal(first, again)
+    ws = ops.decode_workspace(torch.device(DEV), 4, 32, 8, 128, pb.block_tables.size(1), 256)
+    torch.cuda.synchronize()
+    assert int(ws[:8].sum().item()) == 0  # scheduler counters reset
+
+
+def test_decode_bad_block_flags(cuda_lib):
+    ops = _ops()
+    pb = make_paged_batch(seed=17, lens=[600], Hq=16, Hk=8)
+    bt = pb.block_tables.clone()
+    bt[0, 1] = 10_000
+    ops.paged_decode(pb.q.to(DEV), pb.k_cache.to(DEV), pb.v_cache.to(DEV), bt.to(DEV),
+                     pb.context_lens.to(DEV), 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert _deverr() & 0x2
+
+
+def test_decode_matches_flash_attn_if_available(cuda_lib):
+    """Cross-check against the reference's own decode kernel when flash-attn
+    runs on this GPU (its source is not part of the reference tree)."""
+    try:
+        from flash_attn import flash_attn_with_kvcache
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"flash_attn unavailable: {e}")
+    ops = _ops()
+    from oracle.inputs import make_config1
+    pb = make_config1()
+    args = [t.to(DEV) for t in (pb.q, pb.k_cache, pb.v_cache)]
+    try:
+        ref = flash_attn_with_kvcache(args[0].unsqueeze(1), args[1], args[2],
+                                      cache_seqlens=pb.context_lens.to(DEV),
+                                      block_table=pb.block_tables.to(DEV),
+                                      softmax_scale=128 ** -0.5, causal=True)
+        torch.cuda.synchronize()
+    except Exception as e:
+        pytest.skip(f"flash_attn_with_kvcache does not run here: {e}")
+    out = ops.flash_decode_with_kvcache(args[0].unsqueeze(1), args[1], args[2],
+                                        cache_seqlens=pb.context_lens.to(DEV),
+                                        block_table=pb.block_tables.to(DEV),
+                                        softmax_scale=128 ** -0.5)
+    torch.cuda.synchronize()
+    d = (out.float() - ref.float()).abs().max().item()
+    assert d <= ATOL
+
+
+# ------------------------------------------------------------------ window compression
+def _window_case_gpu(name, kw, selected, wb, kb, ke, golden):
+    ops = _ops()
+    pb = make_paged_batch(**kw)
+    k0, v0 = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(pb.k_new, pb.v_new, k0, v0, pb.slot_mapping)
+    keep_tokens = kb * pb.block_size + ke
+    num_keep = keep_tokens - 2
+    kd, vd = k0.to(DEV), v0.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    base = cl.clone()
+    sel = torch.tensor(selected, dtype=torch.int32, device=DEV)
+    keep_out = torch.full((len(selected), keep_tokens), -7, dtype=torch.int32, device=DEV)
+    newl = torch.zeros(len(selected), dtype=torch.int32, device=DEV)
+    ops.window_compress(pb.q.to(DEV), kd, vd, pb.block_tables.to(DEV), base, cl, sel, wb,
+                        keep_tokens, out_keep_idx=keep_out, out_new_lens=newl)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    gk = keep_out.cpu().long()
+    # oracle on the same inputs
+    k1, v1, cl1 = k0.clone(), v0.clone(), pb.context_lens.clone()
+    okeep, onew = window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1,
+                                      selected, pb.block_size, wb, kb, ke)
+    assert cl.cpu().tolist() == cl1.tolist()
+    assert newl.cpu().tolist() == onew.tolist()
+    # kept sets: exact, or differing only within one bf16 ulp of the cut
+    window = window_importance(pb.q, k0, pb.block_tables, pb.context_lens, selected,
+                               pb.block_size, wb)
+    exact = 0
+    for i in range(len(selected)):
+        assert gk[i, 0] == 0 and gk[i, -1] == wb * pb.block_size - 1
+        assert torch.all(gk[i].diff() > 0)
+        if torch.equal(gk[i], okeep[i]):
+            exact += 1
+            continue
+        cut = torch.sort(window[i].float(), descending=True).values[num_keep - 1].item()
+        ok, why = tie_band_ok(window[i], gk[i, 1:1 + num_keep], okeep[i, 1:1 + num_keep], num_keep,
+                              band=_bf16_ulp(cut))
+        assert ok, why
+    # compaction is bit-exact given the kernel's own kept set
+    k2, v2, cl2 = k0.clone(), v0.clone(), pb.context_lens.clone()
+    window_compress_ref(pb.q, k2, v2, pb.block_tables, pb.context_lens.clone(), cl2, selected,
+                        pb.block_size, wb, kb, ke, keep_idx_override=gk)
+    assert torch.equal(kd.cpu().view(torch.int16), k2.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v2.view(torch.int16))
+    # and against the reference's golden kept set (same tie rule)
+    g = golden
+    ref_keep = torch.from_numpy(g[f"{name}/keep_idx"]).long()
+    ref_imp = torch.from_numpy(g[f"{name}/importance_bits"].astype(np.int16)).view(torch.bfloat16).float()
+    for i in range(len(selected)):
+        cut = torch.sort(ref_imp[i], descending=True).values[num_keep - 1].item()
+        ok, why = tie_band_ok(ref_imp[i], gk[i, 1:1 + num_keep], ref_keep[i, 1:1 + num_keep],
+                              num_keep, band=_bf16_ulp(cut))
+        assert ok, why
+    return exact
+
+
+@pytest.mark.parametrize("case", WINDOW_CASES, ids=[c[0] for c in WINDOW_CASES])
+def test_window_compress_parity(cuda_lib, golden_dir, case):
+    g = np.load(golden_dir / "window_compress.npz")
+    name, kw, selected, wb, kb, ke = case
+    _window_case_gpu(name, kw, selected, wb, kb, ke, g)
+
+
+def test_window_compress_tp_shapes(cuda_lib):
+    """TP 8 shard of Qwen3-8B (1 kv head, 4 q heads) and TP 2 (4 kv heads)."""
+    ops = _ops()
+    for Hq, Hk in [(4, 1), (16, 4)]:
+        pb = make_paged_batch(seed=40 + Hk, lens=[1100, 1800, 2600], Hq=Hq, Hk=Hk)
+        kd, vd = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+        cl = pb.context_lens.to(DEV)
+        sel = torch.tensor([0, 2], dtype=torch.int32, device=DEV)
+        keep = torch.zeros(2, 513, dtype=torch.int32, device=DEV)
+        ops.window_compress(pb.q.to(DEV), kd, vd, pb.block_tables.to(DEV), cl.clone(), cl, sel, 4,
+                            513, out_keep_idx=keep)
+        k1, v1, cl1 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+        window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1, [0, 2],
+                            256, 4, 2, 1, keep_idx_override=keep.cpu().long())
+        torch.cuda.synchronize()
+        assert torch.equal(kd.cpu().view(torch.int16), k1.view(torch.int16))
+        assert torch.equal(vd.cpu().view(torch.int16), v1.view(torch.int16))
+        assert cl.cpu().tolist() == cl1.tolist()
+        assert _deverr() == 0
+
+
+# ------------------------------------------------------------------ KvChat
+@pytest.mark.parametrize("case", THRESHOLD_CASES, ids=[c[0] for c in THRESHOLD_CASES])
+def test_threshold_compress_parity(cuda_lib, golden_dir, case):
+    ops = _ops()
+    name, seed, P, Hq, Hk, W, S_cfg, R_cfg, L, layer = case
+    S, R = P + S_cfg, P + R_cfg
+    pb, qsteps = threshold_inputs(seed, P, Hq, Hk, W, S_cfg, L)
+    # device ring written by the append kernel, one step at a time
+    ring = torch.zeros(2, L, W, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    bidx = torch.zeros(1, dtype=torch.int32, device=DEV)
+    rslot = torch.ones(1, dtype=torch.int32, device=DEV)  # use ring slot 1
+    qref = QueryWindowRef(L, W, Hq, 128)
+    qref.activate(0)
+    for step in range(W):
+        pos = torch.tensor([step % W], dtype=torch.int32, device=DEV)
+        for lyr in range(L if step < W - 1 else layer + 1):
+            ops.query_window_append(qsteps[step, lyr].to(DEV), ring, lyr, bidx, rslot, pos)
+            qref.append([0], lyr, qsteps[step, lyr])
+    torch.cuda.synchronize()
+    # the ring holds exactly the window the reference gathers (up to rotation)
+    g_ring = ring[1, layer].cpu()
+    q_sub = qref.gather([0], layer)[0].permute(1, 0, 2)  # [W, Hq, D]
+    assert sorted(digest(r) for r in g_ring) == sorted(digest(r) for r in q_sub)
+    kd, vd = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    keep = torch.zeros(1, R, dtype=torch.int32, device=DEV)
+    ops.threshold_compress(ring, rslot, layer, kd, vd, pb.block_tables.to(DEV), cl, bidx, S, R,
+                           out_keep_idx=keep)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    assert cl.cpu().tolist() == [R]
+    gk = keep.cpu().long()
+    g = np.load(golden_dir / "threshold.npz")
+    ref_keep = torch.from_numpy(g[f"{name}/keep_idx"]).long()
+    ref_imp = torch.from_numpy(g[f"{name}/importance_bits"].astype(np.int16)).view(torch.bfloat16).float()
+    num_keep = R - W - 1
+    cut = torch.sort(ref_imp[0], descending=True).values[num_keep - 1].item()
+    ok, why = tie_band_ok(ref_imp[0], gk[0, 1:1 + num_keep], ref_keep[0, 1:1 + num_keep], num_keep,
+                          band=_bf16_ulp(cut))
+    assert ok, why
+    assert torch.equal(gk[0, 1 + num_keep:], torch.arange(S - W, S))
+    k2, v2, cl2 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    threshold_compress_ref(qref.gather([0], layer), k2, v2, pb.block_tables, cl2, [0], S, R, W,
+                           keep_idx_override=gk)
+    assert torch.equal(kd.cpu().view(torch.int16), k2.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v2.view(torch.int16))

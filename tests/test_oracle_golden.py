@@ -1,0 +1,138 @@
+"""Pins the CPU oracle to the reference: every golden vector under
+tests/golden/ was produced by the reference's own functions
+(tests/golden/make_golden.py). CPU only."""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention import paged_decode_ref, store_kvcache_ref
+from oracle.cases import SNAPKV_CASES, THRESHOLD_CASES, WINDOW_CASES, snapkv_inputs, threshold_inputs
+from oracle.inputs import digest, make_paged_batch
+from oracle.snapkv import snapkv_importance, snapkv_keep, tie_band_ok
+from oracle.threshold_compress import QueryWindowRef, threshold_compress_ref
+from oracle.window_compress import compression_events, window_compress_ref
+
+
+def _npz(golden_dir, name):
+    return np.load(golden_dir / name, allow_pickle=False)
+
+
+def _bits_to_float(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16).float()
+
+
+@pytest.mark.parametrize("case", SNAPKV_CASES, ids=[c[0] for c in SNAPKV_CASES])
+def test_snapkv_matches_reference(golden_dir, case):
+    name, seed, m, Hq, Hk, L, window, num_keep, outlier = case
+    g = _npz(golden_dir, "snapkv.npz")
+    Q, K = snapkv_inputs(seed, m, Hq, Hk, L, window, outlier)
+    assert digest(Q) == str(g[f"{name}/q_digest"]), "input generator drifted"
+    assert digest(K) == str(g[f"{name}/k_digest"]), "input generator drifted"
+    imp = snapkv_importance(Q, K, window)
+    # importance: bit-identical to the reference's bf16 key_importance
+    ref_imp = torch.from_numpy(g[f"{name}/importance_bits"]).view(torch.bfloat16)
+    assert torch.equal(imp.view(torch.int16), ref_imp.view(torch.int16))
+    final, _ = snapkv_keep(Q, K, num_keep, window)
+    ref_final = torch.from_numpy(g[f"{name}/final_idx"]).long()
+    assert final.shape == ref_final.shape
+    # bos and the observation window are fixed; kept sets agree up to swaps
+    # inside the exact-tie group at the cut (torch.topk's tie order is unspecified)
+    assert torch.equal(final[:, 0], ref_final[:, 0])
+    assert torch.equal(final[:, 1 + num_keep:], ref_final[:, 1 + num_keep:])
+    for i in range(m):
+        ok, why = tie_band_ok(imp[i], final[i, 1:1 + num_keep], ref_final[i, 1:1 + num_keep],
+                              num_keep, band=0.0)
+        assert ok, why
+        assert torch.all(ref_final[i, 1:1 + num_keep].diff() > 0)
+
+
+@pytest.mark.parametrize("case", WINDOW_CASES, ids=[c[0] for c in WINDOW_CASES])
+def test_window_compress_matches_reference(golden_dir, case):
+    name, kw, selected, wb, kb, ke = case
+    g = _npz(golden_dir, "window_compress.npz")
+    meta = json.loads(str(g["meta_json"]))[name]
+    pb = make_paged_batch(**kw)
+    assert digest(pb.k_cache) == str(g[f"{name}/k_cache_in_digest"])
+    assert digest(pb.q) == str(g[f"{name}/q_digest"])
+    k0, v0 = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(pb.k_new, pb.v_new, k0, v0, pb.slot_mapping)
+    assert digest(k0) == str(g[f"{name}/k_cache_stored_digest"])
+
+    # 1. oracle selection vs the reference's (tie swaps only)
+    k1, v1, cl1 = k0.clone(), v0.clone(), pb.context_lens.clone()
+    keep_idx, new_lens = window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(),
+                                             cl1, selected, pb.block_size, wb, kb, ke)
+    ref_keep = torch.from_numpy(g[f"{name}/keep_idx"]).long()
+    imp = _bits_to_float(g[f"{name}/importance_bits"])
+    num_keep = kb * pb.block_size + ke - 2
+    for i in range(len(selected)):
+        ok, why = tie_band_ok(imp[i], keep_idx[i, 1:1 + num_keep], ref_keep[i, 1:1 + num_keep],
+                              num_keep, band=0.0)
+        assert ok, why
+    assert cl1.tolist() == g[f"{name}/context_lens_after"].tolist()
+    events = compression_events(pb.block_tables, selected, new_lens, pb.block_size, 0)
+    assert events == meta["events"]
+
+    # 2. given the reference's kept set, the compacted caches are bit-exact
+    k2, v2, cl2 = k0.clone(), v0.clone(), pb.context_lens.clone()
+    window_compress_ref(pb.q, k2, v2, pb.block_tables, pb.context_lens.clone(), cl2, selected,
+                        pb.block_size, wb, kb, ke, keep_idx_override=ref_keep)
+    assert digest(k2) == str(g[f"{name}/k_cache_out_digest"])
+    assert digest(v2) == str(g[f"{name}/v_cache_out_digest"])
+
+
+@pytest.mark.parametrize("case", THRESHOLD_CASES, ids=[c[0] for c in THRESHOLD_CASES])
+def test_threshold_compress_matches_reference(golden_dir, case):
+    name, seed, P, Hq, Hk, W, S_cfg, R_cfg, L, layer = case
+    g = _npz(golden_dir, "threshold.npz")
+    meta = json.loads(str(g["meta_json"]))[name]
+    S, R = P + S_cfg, P + R_cfg
+    pb, qsteps = threshold_inputs(seed, P, Hq, Hk, W, S_cfg, L)
+    assert digest(qsteps) == str(g[f"{name}/qsteps_digest"])
+    qwm = QueryWindowRef(L, W, Hq, 128)
+    qwm.activate(0)
+    for step in range(W):
+        for lyr in range(L if step < W - 1 else layer + 1):
+            qwm.append([0], lyr, qsteps[step, lyr])
+    q_sub = qwm.gather([0], layer)
+    ref_keep = torch.from_numpy(g[f"{name}/keep_idx"]).long()
+    imp = _bits_to_float(g[f"{name}/importance_bits"])
+    num_keep = R - W - 1
+
+    k1, v1, cl1 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    keep = threshold_compress_ref(q_sub, k1, v1, pb.block_tables, cl1, [0], S, R, W)
+    ok, why = tie_band_ok(imp[0], keep[0, 1:1 + num_keep], ref_keep[0, 1:1 + num_keep], num_keep)
+    assert ok, why
+    assert cl1.tolist() == g[f"{name}/context_lens_after"].tolist()
+
+    k2, v2, cl2 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    threshold_compress_ref(q_sub, k2, v2, pb.block_tables, cl2, [0], S, R, W,
+                           keep_idx_override=ref_keep)
+    assert digest(k2) == str(g[f"{name}/k_cache_out_digest"])
+    assert digest(v2) == str(g[f"{name}/v_cache_out_digest"])
+    ev = meta["events"]
+    if layer + 1 >= L:  # events are recorded on the last layer only
+        assert len(ev) == 1 and ev[0]["R"] == R and ev[0]["keep_blocks"] == (R + 255) // 256
+    else:
+        assert ev == []
+
+
+def test_decode_oracle_small_exact():
+    """The fp32 decode restatement on a hand-checkable case: one sequence of
+    3 tokens, Hq == Hk == 1, against an explicit softmax."""
+    torch.manual_seed(0)
+    D = 128
+    k_cache = torch.randn(2, 256, 1, D).to(torch.bfloat16)
+    v_cache = torch.randn(2, 256, 1, D).to(torch.bfloat16)
+    q = torch.randn(1, 1, D).to(torch.bfloat16)
+    bt = torch.tensor([[1, 0]], dtype=torch.int32)
+    out = paged_decode_ref(q, k_cache, v_cache, bt, torch.tensor([3], dtype=torch.int32), 0.1)
+    K = k_cache[1, :3, 0].float()
+    V = v_cache[1, :3, 0].float()
+    p = torch.softmax(q[0, 0].float() @ K.T * 0.1, -1)
+    assert torch.allclose(out[0, 0], p @ V, atol=1e-5)
+    zero = paged_decode_ref(q, k_cache, v_cache, bt, torch.tensor([0], dtype=torch.int32), 0.1)
+    assert torch.count_nonzero(zero) == 0
