@@ -1,0 +1,475 @@
+"""Decode-attention throughput of the nano-kvllm B200 path.
+
+One step = one decode token for every sequence through all 36 layers of the
+attention hot path: per layer, store_kvcache of the 256 new K/V rows and
+paged split-KV decode attention over the block tables (config 2 has no
+compression events, so the compression term of the metric is zero; it is
+measured separately on config 3 shapes and reported under "compress").
+
+Workload: Qwen3-8B shapes (32 q / 8 kv heads, head_dim 128, bf16), batch 256,
+context lengths drawn uniformly from [1024, 8192] (seed 0, including the
+current token), block_size 256, random non-contiguous block tables. Synthetic
+values N(0,1). Under torchrun with N ranks each rank holds 8/N kv heads and
+32/N q heads of every layer (the reference's tensor-parallel split); the
+per-layer KV read is ~4.8 GB / N, far larger than the 126 MB L2, so no L2
+flush is needed between steps.
+
+Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "nanokv-llm_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode tok/s (attn+KV-compress) Qwen3-8B b=256"
+LAYERS = 36
+HQ, HK, D = 32, 8, 128
+BATCH = 256
+BLOCK = 256
+LEN_LO, LEN_HI = 1024, 8192
+SEED = 0
+
+
+def workload_lens() -> list[int]:
+    rng = np.random.default_rng(SEED)
+    return rng.integers(LEN_LO, LEN_HI + 1, BATCH).tolist()
+
+
+def config_dict(n: int, resident_layers: int) -> dict:
+    return {
+        "workload": "config2: Qwen3-8B decode attention (store + paged decode per layer), "
+                    "36 layers, batch 256, ctx U[1024,8192], block 256, no compression",
+        "model_shape": "Qwen3-8B attention: 32 q / 8 kv heads, head_dim 128",
+        "layers": LAYERS, "resident_layer_caches": resident_layers,
+        "batch": BATCH, "block_size": BLOCK, "ctx_len": f"U[{LEN_LO},{LEN_HI}] seed {SEED}",
+        "tp": n, "parallelism": f"tp{n} (kv-head sharded)",
+        "l2": "inputs larger than L2: each decode launch streams ~4.8/N GB of KV",
+    }
+
+
+# ---------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------- GPU arm
+def build_state(rank: int, world: int, dev: torch.device):
+    hk, hq = HK // world, HQ // world
+    lens = workload_lens()
+    nblk_seq = [(L + BLOCK - 1) // BLOCK for L in lens]
+    num_blocks = sum(nblk_seq)
+    g = torch.Generator(device="cpu").manual_seed(SEED + 1)
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    tables, o = [], 0
+    for n in nblk_seq:
+        tables.append(perm[o:o + n])
+        o += n
+    max_blocks = max(nblk_seq)
+    bt = torch.tensor([t + [-1] * (max_blocks - len(t)) for t in tables], dtype=torch.int32)
+    slots = [t[(L - 1) // BLOCK] * BLOCK + (L - 1) % BLOCK for t, L in zip(tables, lens)]
+    layer_bytes = 2 * num_blocks * BLOCK * hk * D * 2
+    free, _ = torch.cuda.mem_get_info(dev)
+    budget = free - (4 << 30)
+    resident = max(1, min(LAYERS, budget // layer_bytes))
+    kv = torch.empty(2, resident, num_blocks, BLOCK, hk, D, dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(SEED + 2 + rank)
+    for i in range(2):
+        for layer in range(resident):
+            kv[i, layer].normal_(generator=gen)
+    return dict(lens=lens, hk=hk, hq=hq, num_blocks=num_blocks, max_blocks=max_blocks,
+                block_tables_h=bt, slots_h=torch.tensor(slots, dtype=torch.int32),
+                kv=kv, resident=resident, layer_bytes=layer_bytes)
+
+
+def algorithmic_decode_bytes(lens, hk, hq) -> int:
+    kv = sum(lens) * hk * D * 2 * 2
+    qo = BATCH * hq * D * 2 * 2
+    tables = sum((L + BLOCK - 1) // BLOCK for L in lens) * 4 + BATCH * 4
+    return kv + qo + tables
+
+
+def run_gpu(args, rank, world, dev):
+    from nanokv_b200 import _lib, ops
+
+    _lib.load()
+    st = build_state(rank, world, dev)
+    hk, hq = st["hk"], st["hq"]
+    kv = st["kv"]
+    R = st["resident"]
+    bt = st["block_tables_h"].to(dev)
+    cl = torch.tensor(st["lens"], dtype=torch.int32, device=dev)
+    sm = st["slots_h"].to(dev)
+    scale = D ** -0.5
+    gq = torch.Generator(device=dev).manual_seed(SEED + 100 + rank)
+    # per-layer q/k/v of the step, laid out like the qkv projection output
+    qkv = torch.randn(LAYERS, BATCH, (hq + 2 * hk) * D, device=dev, generator=gq).to(torch.bfloat16)
+    out = torch.empty(LAYERS, BATCH, hq, D, dtype=torch.bfloat16, device=dev)
+    ws = ops.decode_workspace(dev, BATCH, hq, hk, D, st["max_blocks"], BLOCK)
+
+    def layer_views(layer, buf):
+        q, k, v = buf[layer].split([hq * D, hk * D, hk * D], dim=-1)
+        return q.view(BATCH, hq, D), k.view(BATCH, hk, D), v.view(BATCH, hk, D)
+
+    dec_events = []
+
+    def step(record=False, src=qkv):
+        for layer in range(LAYERS):
+            c = layer % R
+            q, k, v = layer_views(layer, src)
+            ops.store_kvcache(k, v, kv[0, c], kv[1, c], sm)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+            ops.paged_decode(q, kv[0, c], kv[1, c], bt, cl, scale, out=out[layer], workspace=ws)
+            if record:
+                e1.record()
+                dec_events.append((e0, e1))
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    dec_ms = [a.elapsed_time(b) for a, b in dec_events]
+
+    # ---- end to end through the public API with host buffers
+    from nanokv_b200.layers.attention import Attention
+    from nanokv_b200.utils.context import reset_context, set_context
+
+    cfg = type("Cfg", (), {"kv_compress_enabled": False})()
+    layers = []
+    for layer in range(LAYERS):
+        a = Attention(hq, D, scale, hk, cfg, LAYERS)
+        a.k_cache, a.v_cache = kv[0, layer % R], kv[1, layer % R]
+        layers.append(a)
+    qkv_h = qkv.cpu().pin_memory()
+    out_h = torch.empty(LAYERS, BATCH, hq, D, dtype=torch.bfloat16).pin_memory()
+    meta_h = {"slot_mapping": st["slots_h"].pin_memory(),
+              "context_lens": torch.tensor(st["lens"], dtype=torch.int32).pin_memory(),
+              "block_tables": st["block_tables_h"].pin_memory()}
+    qkv_d = torch.empty_like(qkv)
+
+    def e2e_step():
+        sm_d = meta_h["slot_mapping"].to(dev, non_blocking=True)
+        cl_d = meta_h["context_lens"].to(dev, non_blocking=True)
+        bt_d = meta_h["block_tables"].to(dev, non_blocking=True)
+        set_context(True, slot_mapping=sm_d, context_lens=cl_d, block_tables=bt_d)
+        for layer in range(LAYERS):
+            qkv_d[layer].copy_(qkv_h[layer], non_blocking=True)
+            q, k, v = layer_views(layer, qkv_d)
+            o = layers[layer].forward(q, k, v, layer)
+            out_h[layer].copy_(o.view(BATCH, hq, D), non_blocking=True)
+        reset_context()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = qkv_h.numel() * 2 + sum(t.numel() * 4 for t in meta_h.values())
+    d2h = out_h.numel() * 2
+
+    # ---- compression cost on config 3 shapes (one event = 20 sequences, one layer)
+    comp = measure_compress(dev, hq, hk)
+
+    # ---- max over ranks
+    vals = torch.tensor([ms, e2e_ms, statistics.mean(dec_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms, dec_avg = vals.tolist()
+    alg = algorithmic_decode_bytes(st["lens"], hk, hq)
+    return dict(ms=ms, e2e_ms=e2e_ms, dec_avg_ms=dec_avg, alg_bytes=alg, clocks=clk,
+                resident=R, h2d=h2d, d2h=d2h, compress=comp)
+
+
+def measure_compress(dev, hq, hk):
+    """One periodic compression event on config 3 shapes: 20 sequences, window
+    4 blocks, keep 2*256+1, one layer; amortised per decode step over the
+    period of 1024 steps and 36 layers."""
+    from nanokv_b200 import ops
+
+    rng = np.random.default_rng(3)
+    lens = rng.integers(1100, 4396, 20).tolist()
+    nblk = [(L + BLOCK - 1) // BLOCK for L in lens]
+    nb = sum(nblk)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(3)).tolist()
+    tables, o = [], 0
+    for n in nblk:
+        tables.append(perm[o:o + n])
+        o += n
+    mb = max(nblk)
+    bt = torch.tensor([t + [-1] * (mb - len(t)) for t in tables], dtype=torch.int32, device=dev)
+    kc = torch.randn(nb, BLOCK, hk, D, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(20, hq, D, device=dev).to(torch.bfloat16)
+    base = torch.tensor(lens, dtype=torch.int32, device=dev)
+    sel = torch.arange(20, dtype=torch.int32, device=dev)
+    cl = base.clone()
+    times = []
+    for i in range(8):
+        cl.copy_(base)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.window_compress(q, kc, vc, bt, base, cl, sel, 4, 513)
+        b.record()
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            times.append(a.elapsed_time(b))
+    t_layer_ms = statistics.median(times)
+    alg = 20 * (1023 * hk * D * 2 + 2 * 2 * (513 + 128) * hk * D * 2 + hq * D * 2)
+    return {"event_layer_us": round(t_layer_ms * 1e3, 2),
+            "event_step_ms": round(t_layer_ms * LAYERS, 4),
+            "amortised_ms_per_step": round(t_layer_ms * LAYERS / 1024, 5),
+            "sequences": 20, "period": 1024,
+            "approx_alg_GBps": round(alg / (t_layer_ms * 1e-3) / 1e9, 1)}
+
+
+# ---------------------------------------------------------------------- CPU arms
+def cpu_decode_sample(seconds: float, hq: int, hk: int):
+    """Times the CPU oracle (fp32 torch restatement of the reference's paged
+    decode, plus the store) on whole sequences of the workload, in workload
+    order, for about `seconds`; returns (tok/s scaled to the full step,
+    sample description, threads)."""
+    from oracle.attention import paged_decode_ref, store_kvcache_ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lens = workload_lens()
+    nb_max = (LEN_HI + BLOCK - 1) // BLOCK
+    g = torch.Generator().manual_seed(11)
+    # one KV pool reused by every sampled sequence (values do not affect timing)
+    kc = torch.randn(nb_max, BLOCK, hk, D, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nb_max, BLOCK, hk, D, generator=g).to(torch.bfloat16)
+    q = torch.randn(1, hq, D, generator=g).to(torch.bfloat16)
+    kn = torch.randn(1, hk, D, generator=g).to(torch.bfloat16)
+    done_tokens, elapsed, nseq = 0, 0.0, 0
+    while elapsed < seconds:
+        L = lens[nseq % len(lens)]
+        nb = (L + BLOCK - 1) // BLOCK
+        bt = torch.arange(nb, dtype=torch.int32).view(1, nb)
+        sm = torch.tensor([L - 1], dtype=torch.int32)
+        t = time.perf_counter()
+        store_kvcache_ref(kn, kn, kc, vc, sm)
+        paged_decode_ref(q, kc, vc, bt, torch.tensor([L], dtype=torch.int32), D ** -0.5)
+        elapsed += time.perf_counter() - t
+        done_tokens += L
+        nseq += 1
+    per_token_s = elapsed / done_tokens
+    step_s = per_token_s * sum(lens) * LAYERS
+    desc = (f"{nseq} whole sequences of the workload ({done_tokens} KV tokens, one layer, "
+            f"{hq} q / {hk} kv heads, {threads} threads) in {elapsed:.1f} s, scaled linearly "
+            f"by KV tokens to 256 sequences x 36 layers")
+    return BATCH / step_s, desc, threads
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    hq, hk = HQ // world, HK // world
+    per_step = max(2.0, 40.0 / max(1, args.steps + args.warmup))
+    vals = []
+    desc = ""
+    threads = 1
+    for i in range(args.warmup + args.steps):
+        v, desc, threads = cpu_decode_sample(per_step, hq, hk)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * BATCH / value, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": config_dict(world, LAYERS),
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads,
+                         "kind": "port", "sample": desc + " (per step)"},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------- main
+def read_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def read_traffic_bytes_per_launch(world: int):
+    """dram bytes per decode launch from the committed ncu summary, if any."""
+    p = REPO / "profiles" / "paged_decode_config2.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith(f"traffic_bytes_per_launch_tp{world}:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "nkv" else args.warmup
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        world = max(world, 1)
+    if HK % world:
+        raise SystemExit(f"world size {world} must divide {HK} kv heads")
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line))
+        return
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    r = run_gpu(args, rank, world, dev)
+    cpu = None
+    if rank == 0 and world == 1:
+        v, desc, threads = cpu_decode_sample(10.0, HQ, HK)
+        cpu = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+    if rank == 0:
+        peak, peak_src = read_peaks()
+        dec_s = r["dec_avg_ms"] * 1e-3
+        achieved = r["alg_bytes"] / dec_s / 1e9
+        traffic = read_traffic_bytes_per_launch(world)
+        value = BATCH * args.steps / (r["ms"] * 1e-3)
+        e2e = BATCH * args.steps / (r["e2e_ms"] * 1e-3)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"] / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (N(0,1) q/k/v and cache, seeded)",
+            "config": config_dict(world, r["resident"]),
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": r["h2d"],
+                    "d2h_bytes_per_step": r["d2h"],
+                    "path": "nanokv_b200.layers.attention.Attention.forward per layer, q/k/v "
+                            "from pinned host memory, outputs copied back"},
+            "roofline": {"kernel": "nkv paged_decode_kernel", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} hbm_gbs",
+                         "traffic": traffic, "alg_bytes_per_launch": r["alg_bytes"],
+                         "avg_launch_us": round(r["dec_avg_ms"] * 1e3, 2)},
+            "cpu_baseline": cpu,
+            "clocks": r["clocks"],
+            "gpu_launches": args.steps * LAYERS * 2,
+            "compress": r["compress"],
+        }
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -96,9 +96,11 @@ int nkv_store_kvcache(const void* key, int64_t key_stride,
 /* block_tables[b, t / block_size]. context_lens[b] == 0 writes zeros.       */
 /* q rows: q + b*q_stride_token + h*q_stride_head (head_dim contiguous).     */
 /* out rows: out + b*out_stride_token + h*head_dim.                          */
-/* Supported: head_dim 128, block_size a multiple of 128, g in [1, 16].      */
-/* The workspace must be zero-filled once before its first use; every call   */
-/* leaves it zeroed again, so one buffer serves all layers and CUDA graphs.  */
+/* Supported: head_dim 128, block_size a multiple of 128, g in [1, 16],      */
+/* batch * num_kv_heads <= 65536.                                            */
+/* The workspace must be zero-filled once before its first use. Every call   */
+/* leaves its counter region zeroed again (partial results elsewhere in the  */
+/* buffer may stay), so one buffer serves all layers, shapes and CUDA graphs.*/
 size_t nkv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads,
                                        int32_t num_kv_heads, int32_t head_dim,
                                        int32_t max_blocks, int32_t block_size);

@@ -94,6 +94,10 @@ struct DecodePlan {
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Upper bound on batch * num_kv_heads per decode call (size of the fixed
+// split-counter region of the workspace).
+constexpr int kMaxDecodePairs = 1 << 16;
+
 // Split size depends only on the shapes (not on the device or the lengths), so
 // the workspace query and the launch always agree.
 DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block_size) {
@@ -109,9 +113,14 @@ DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block
   pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
   pl.chunk_tokens = pl.chunk_blocks * block_size;
   pl.max_splits = std::max(1, (std::max(max_blocks, 1) + pl.chunk_blocks - 1) / pl.chunk_blocks);
-  size_t off = 256;  // counters header
+  // Layout: [scheduler counters][split counters for kMaxDecodePairs pairs]
+  // [partial (m, l)][partial O]. The counter region has a FIXED size so
+  // that, whatever shapes share one workspace, a counter never lands on
+  // bytes another shape used for partial results (only counters must be
+  // zero between calls; partials may hold anything).
+  size_t off = 256;
   pl.off_split_counters = off;
-  off = align256(off + sizeof(unsigned int) * pl.pairs);
+  off = align256(off + sizeof(unsigned int) * kMaxDecodePairs);
   pl.off_part_ml = off;
   off = align256(off + sizeof(float) * 2 * static_cast<size_t>(pl.pairs) * pl.max_splits * pl.g);
   pl.off_part_o = off;
@@ -252,7 +261,8 @@ int nkv_store_kvcache(const void* key, int64_t key_stride, const void* value, in
 size_t nkv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                        int32_t head_dim, int32_t max_blocks, int32_t block_size) {
   if (batch <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || block_size <= 0 ||
-      num_q_heads % num_kv_heads != 0)
+      num_q_heads % num_kv_heads != 0 ||
+      static_cast<int64_t>(batch) * num_kv_heads > kMaxDecodePairs)
     return 0;
   (void)head_dim;
   return make_decode_plan(batch, num_q_heads, num_kv_heads, max_blocks, block_size).total;
@@ -276,6 +286,7 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
   const int g = num_q_heads / num_kv_heads;
   const int G = padded_group(g);
   if (G == 0) return NKV_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(batch) * num_kv_heads > kMaxDecodePairs) return NKV_ERR_UNSUPPORTED;
   if (!std::isfinite(softmax_scale)) return NKV_ERR_INVALID_ARGUMENT;
   if (out_stride_token < static_cast<int64_t>(num_q_heads) * head_dim) return NKV_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (q_stride_token % 8) ||

@@ -205,6 +205,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     if (ok) {
       // End-of-work marker for the consumers.
       if (mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) {
+        armed[stage] = 0;  // released: its last transaction has completed
         meta[stage * kDecodeMetaInts + 0] = -1;
         mbar_arrive(smem_u32(&full_bar[stage]));
       } else {

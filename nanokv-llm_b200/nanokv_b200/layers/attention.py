@@ -1,0 +1,71 @@
+"""Drop-in Attention module for nano-kvllm's decode path on B200.
+
+Same class name, constructor and forward(q, k, v, Layer) as the reference's
+nanokvllm/layers/attention.py:42-108, same order of work per layer:
+
+  1. store_kvcache of the step's K/V rows      -> nkv_store_kvcache
+  2. periodic window compression when the Context asks for it
+                                               -> nkv_window_compress (MyCompressCompact)
+  3. decode attention over the paged cache     -> nkv_paged_decode
+     (flash_attn_with_kvcache in the reference)
+
+Prefill / mixed batches (use_decode_kernel False) are outside this path and
+keep the reference's flash_attn_varlen_func call unchanged.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..ops import store_kvcache  # noqa: F401  (same public name as the reference module)
+from ..utils.context import get_context
+from .compress_utils import MyCompressCompact
+
+
+class Attention(nn.Module):
+
+    def __init__(self, num_heads, head_dim, scale, num_kv_heads, vllm_config, num_layers):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = scale
+        self.num_kv_heads = num_kv_heads
+        self.k_cache = self.v_cache = torch.tensor([])
+        self.kv_compress_enabled = vllm_config.kv_compress_enabled
+        if self.kv_compress_enabled:
+            self.num_layers = num_layers
+            self.kv_compress_window_blocks = vllm_config.kv_compress_window_blocks
+            self.kv_compress_keep_blocks = vllm_config.kv_compress_keep_blocks
+            self.kv_compress_keep_extra_tokens = vllm_config.kv_compress_keep_extra_tokens
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Layer):
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        if k_cache.numel() and v_cache.numel():
+            ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+
+        if (context.use_decode_kernel and self.kv_compress_enabled and context.is_compress_step
+                and context.compress_selected_batch_indices):
+            MyCompressCompact(q_current=q, k_cache=k_cache, v_cache=v_cache, layer_id=Layer,
+                              block_size=k_cache.size(1),
+                              window_blocks=self.kv_compress_window_blocks,
+                              keep_blocks=self.kv_compress_keep_blocks,
+                              keep_extra_tokens=self.kv_compress_keep_extra_tokens,
+                              num_layers=self.num_layers, context=context)
+
+        if not context.use_decode_kernel:
+            from flash_attn import flash_attn_varlen_func  # prefill: not part of this path
+            if context.block_tables is not None:
+                k, v = k_cache, v_cache
+            return flash_attn_varlen_func(q, k, v, max_seqlen_q=context.max_seqlen_q,
+                                          cu_seqlens_q=context.cu_seqlens_q,
+                                          max_seqlen_k=context.max_seqlen_k,
+                                          cu_seqlens_k=context.cu_seqlens_k,
+                                          softmax_scale=self.scale, causal=True,
+                                          block_table=context.block_tables)
+        return ops.flash_decode_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+                                             cache_seqlens=context.context_lens,
+                                             block_table=context.block_tables,
+                                             softmax_scale=self.scale, causal=True)

@@ -86,15 +86,6 @@ def test_store_kvcache_bad_slot_flags_and_skips(cuda_lib):
     assert kc.float().sum().item() == 128
 
 
-def test_store_empty_cache_is_noop(cuda_lib):
-    ops = _ops()
-    k = torch.ones(3, 2, 128, dtype=torch.bfloat16, device=DEV)
-    empty = torch.tensor([], device=DEV, dtype=torch.bfloat16)
-    # the reference skips the store while the caches are empty (warm-up)
-    ops.store_kvcache(k, k, empty.view(0, 256), empty.view(0, 256),
-                      torch.zeros(3, dtype=torch.int32, device=DEV))
-
-
 # ------------------------------------------------------------------ decode
 def _check_decode(pb, Hq, scale=None, q=None, nan_tail=False):
     ops = _ops()
@@ -183,6 +174,16 @@ def test_decode_repeated_calls_reuse_workspace(cuda_lib):
     ws = ops.decode_workspace(torch.device(DEV), 4, 32, 8, 128, pb.block_tables.size(1), 256)
     torch.cuda.synchronize()
     assert int(ws[:8].sum().item()) == 0  # scheduler counters reset
+
+
+def test_decode_workspace_shared_across_shapes(cuda_lib):
+    """One workspace serves calls of different shapes: a multi-split call of a
+    small batch, then a larger batch whose split counters cover bytes the
+    first call used for partial results, then the small one again."""
+    a = make_paged_batch(seed=18, lens=[300, 700, 1024, 1500], Hq=16, Hk=8)
+    b = make_paged_batch(seed=19, lens=[2049, 1, 900, 257, 4000, 128] * 4, Hq=16, Hk=8)
+    for pb in (a, b, a, b):
+        _check_decode(pb, 16)
 
 
 def test_decode_bad_block_flags(cuda_lib):

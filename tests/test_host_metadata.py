@@ -1,0 +1,162 @@
+"""Host-side compression metadata vs traces recorded from the reference
+(tests/golden/host_metadata.json, made by tests/golden/make_golden.py):
+BlockManager + Scheduler.postprocess event application, the periodic
+selection of ModelRunner.prepare_decode, and KvChat's
+prepare_compression_context. CPU only."""
+
+import json
+import types
+from itertools import count
+
+import numpy as np
+import pytest
+
+from nanokv_b200.engine.block_manager import BlockManager
+from nanokv_b200.engine.compress_schedule import (DecodeMetadata, PeriodicCompressScheduler,
+                                                  apply_threshold_events, apply_window_events,
+                                                  prepare_threshold_context)
+from nanokv_b200.engine.query_window import QueryWindowManager
+from nanokv_b200.engine.sequence import Sequence
+from nanokv_b200.utils.context import Context
+
+
+@pytest.fixture(scope="module")
+def trace(golden_dir):
+    return json.loads((golden_dir / "host_metadata.json").read_text())
+
+
+def _seq_state(s):
+    return {"seq_id": s.seq_id, "num_tokens": s.num_tokens, "block_table": list(s.block_table),
+            "num_cached_tokens": s.num_cached_tokens, "tail_uncompressed_len": s.tail_uncompressed_len,
+            "rope_pos": s.rope_pos}
+
+
+def _bm_state(bm):
+    return {"free": list(bm.free_block_ids), "used": sorted(bm.used_block_ids),
+            "ref": [b.ref_count for b in bm.blocks], "hash_set": [b.hash != -1 for b in bm.blocks]}
+
+
+def test_block_manager_and_events_replay(trace):
+    tr = trace["block_manager"]
+    rng = np.random.default_rng(5)
+    shared = rng.integers(0, 50000, 512).tolist()
+    prompts = [shared + rng.integers(0, 50000, 300).tolist(),
+               shared + rng.integers(0, 50000, 40).tolist(),
+               rng.integers(0, 50000, 1100).tolist(),
+               rng.integers(0, 50000, 255).tolist()]
+    assert prompts == tr["prompts"]
+    Sequence.counter = count()
+    bm = BlockManager(num_blocks=40, block_size=256)
+    seqs = [Sequence(p, max_tokens=10**6, ignore_eos=True) for p in prompts]
+    for s in seqs:
+        bm.allocate(s)
+        s.num_computed_tokens = s.num_prompt_tokens
+    recorded = iter(tr["steps"])
+    first = next(recorded)
+    assert [_seq_state(s) for s in seqs] == first["seqs"]
+    assert _bm_state(bm) == first["bm"]
+    checked = 1
+    for step in range(300):
+        for s in seqs:
+            bm.may_append(s)
+        token_ids = rng.integers(0, 50000, len(seqs)).tolist()
+        events = None
+        if step in (120, 260):
+            events = []
+            for bi in (0, 2):
+                s = seqs[bi]
+                new_len = len(s) - 1024 + 513
+                kb = (new_len + 255) // 256
+                events.append({"batch_index": bi, "layer": 0, "new_context_len": new_len,
+                               "keep_blocks": kb,
+                               "freed_block_ids": [x for x in s.block_table[kb:] if x >= 0],
+                               "tail_uncompressed_len_after": 0})
+            events.append(dict(events[0]))
+        apply_window_events(seqs, events, bm)
+        for s, t in zip(seqs, token_ids):
+            s.num_computed_tokens += 1
+            s.append_token(t)
+        if events or step % 50 == 0:
+            rec = next(recorded)
+            assert rec["op"] == f"step{step}"
+            assert rec["events"] == events
+            assert [_seq_state(s) for s in seqs] == rec["seqs"], f"seq state at step {step}"
+            assert _bm_state(bm) == rec["bm"], f"block manager at step {step}"
+            checked += 1
+    assert checked == len(tr["steps"])
+
+
+def test_periodic_selection_matches_prepare_decode(trace):
+    tr = trace["periodic_selection"]
+    Sequence.counter = count()
+    seqs = []
+    for L, t in zip(tr["lens"], tr["tails"]):
+        s = Sequence(list(range(L)))
+        s.block_table = list(range(100, 100 + (L + 255) // 256))
+        s.tail_uncompressed_len = t
+        s.rope_pos = L + 17
+        seqs.append(s)
+    cfg = types.SimpleNamespace(kv_compress_period=tr["period"], kv_compress_topk=tr["topk"],
+                                kv_compress_window_blocks=4)
+    sched = PeriodicCompressScheduler(cfg, 256)
+    for rec in tr["steps"]:
+        meta = DecodeMetadata.build(seqs, 256)
+        is_step, sel, ids = sched.select(seqs)
+        assert sched.decode_step_counter == rec["step"]
+        assert is_step == rec["is_compress_step"]
+        assert sel == rec["selected"] and ids == rec["seq_ids"]
+        assert meta.positions.tolist() == rec["positions"]
+        assert meta.slot_mapping.tolist() == rec["slot_mapping"]
+        assert meta.context_lens.tolist() == rec["context_lens"]
+        if rec["base_lens"] is not None:
+            assert meta.context_lens.tolist() == rec["base_lens"]
+        for s in seqs:
+            s.append_token(1)
+
+
+def test_periodic_fill_context_host_companions():
+    import torch
+
+    Sequence.counter = count()
+    seqs = [Sequence(list(range(L))) for L in (1500, 900, 2000)]
+    for s, t in zip(seqs, (1024, 2000, 1100)):
+        s.block_table = list(range(len(s.block_table), len(s.block_table) + s.num_blocks))
+        s.tail_uncompressed_len = t
+    cfg = types.SimpleNamespace(kv_compress_period=1, kv_compress_topk=20, kv_compress_window_blocks=4)
+    sched = PeriodicCompressScheduler(cfg, 256)
+    meta = DecodeMetadata.build(seqs, 256)
+    ctx = Context(use_decode_kernel=True, context_lens=torch.from_numpy(meta.context_lens))
+    sched.fill_context(ctx, seqs, meta)
+    assert ctx.is_compress_step and ctx.compress_selected_batch_indices == [0, 2]
+    assert ctx.compress_selected_t.tolist() == [0, 2]
+    assert ctx.compress_base_context_lens_host == [1500, 900, 2000]
+    assert ctx.block_tables_host[1][:4] == seqs[1].block_table
+
+
+def test_kvchat_context_decisions(trace):
+    tr = trace["kvchat_context"]
+    cfg = types.SimpleNamespace(kv_compress_S=511, kv_compress_R=257, query_window_size=50)
+    qwm = QueryWindowManager(1, 50, 2, 128, device="cpu")
+    Sequence.counter = count()
+    seqs = [Sequence(list(range(p))) for p in tr["prompts"]]
+    for rec in tr["decisions"]:
+        for s in seqs:
+            s.num_tokens = s.num_prompt_tokens + rec["extra"]
+        ctx = Context()
+        prepare_threshold_context(ctx, seqs, cfg, qwm)
+        assert ctx.compress_need_mask == rec["need"]
+        assert ctx.compress_any == rec["any"]
+        assert ctx.q_window_active_indices == rec["active"]
+        assert (ctx.runtime_compress_S, ctx.runtime_compress_R) == (rec["S"], rec["R"])
+        assert [qwm.has(s.seq_id) for s in seqs] == rec["has"]
+
+
+def test_threshold_events_truncate():
+    Sequence.counter = count()
+    bm = BlockManager(8, 256)
+    s = Sequence(list(range(767)))
+    bm.allocate(s)
+    apply_threshold_events([s], [{"batch_index": 0, "layer": 27, "R": 513, "keep_blocks": 3,
+                                  "freed_block_ids": []}], bm)
+    assert s.num_tokens == 513 and len(s.block_table) == 3
+    assert list(bm.free_block_ids)[-1] == 3 or 3 in bm.free_block_ids
