@@ -148,9 +148,13 @@ def build_state(rank: int, world: int, dev: torch.device):
 
 
 def algorithmic_decode_bytes(lens, hk, hq) -> int:
+    """Bytes one decode launch must move: every live K and V row of the kv
+    heads once, q in and o out, the block-table entries it follows and the
+    context lengths."""
+    b = len(lens)
     kv = sum(lens) * hk * D * 2 * 2
-    qo = BATCH * hq * D * 2 * 2
-    tables = sum((L + BLOCK - 1) // BLOCK for L in lens) * 4 + BATCH * 4
+    qo = b * hq * D * 2 * 2
+    tables = sum((L + BLOCK - 1) // BLOCK for L in lens) * 4 + b * 4
     return kv + qo + tables
 
 
@@ -404,13 +408,57 @@ def read_traffic_bytes_per_launch(world: int):
     return None
 
 
+def run_profile_case(kind: str) -> None:
+    """Small, self-contained launches for ncu captures (a few GB on the
+    device, inputs larger than L2): `decode` runs store + paged decode on one
+    layer of the first 64 config-2 sequences (Qwen3-8B shapes) 4 times;
+    `compress` runs one config-3 window-compression event 4 times."""
+    from nanokv_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if kind == "compress":
+        for _ in range(4):
+            measure_compress(dev, HQ, HK)
+        torch.cuda.synchronize()
+        return
+    lens = workload_lens()[:64]
+    nblk = [(L + BLOCK - 1) // BLOCK for L in lens]
+    nb = sum(nblk)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(SEED + 1)).tolist()
+    tables, o = [], 0
+    for n in nblk:
+        tables.append(perm[o:o + n])
+        o += n
+    mb = max(nblk)
+    bt = torch.tensor([t + [-1] * (mb - len(t)) for t in tables], dtype=torch.int32, device=dev)
+    cl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    sm = torch.tensor([t[(L - 1) // BLOCK] * BLOCK + (L - 1) % BLOCK for t, L in zip(tables, lens)],
+                      dtype=torch.int32, device=dev)
+    kc = torch.randn(nb, BLOCK, HK, D, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    qkv = torch.randn(64, (HQ + 2 * HK) * D, device=dev).to(torch.bfloat16)
+    q, k, v = qkv.split([HQ * D, HK * D, HK * D], dim=-1)
+    for _ in range(4):
+        ops.store_kvcache(k.view(64, HK, D), v.view(64, HK, D), kc, vc, sm)
+        ops.paged_decode(q.view(64, HQ, D), kc, vc, bt, cl, D ** -0.5)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": kind, "kv_tokens": sum(lens),
+                      "alg_bytes": algorithmic_decode_bytes(lens, HK, HQ)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
+    ap.add_argument("--profile", choices=["decode", "compress"], default=None,
+                    help="run a small case for an ncu capture and exit")
     args = ap.parse_args()
+    if args.profile:
+        run_profile_case(args.profile)
+        return
     args.warmup = max(args.warmup, 3) if args.impl == "nkv" else args.warmup
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
