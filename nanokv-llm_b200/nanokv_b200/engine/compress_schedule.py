@@ -97,7 +97,10 @@ class PeriodicCompressScheduler:
         context_lens must already be on the device)."""
         is_step, sel, ids = self.select(seqs)
         ctx.compress_need_mask = None
-        ctx.compress_any = False
+        # True on a step that compresses, so ModelRunner.run_model takes the
+        # eager path (its graphs were captured without compression); the
+        # reference leaves this False and would replay a graph instead.
+        ctx.compress_any = bool(is_step and sel)
         ctx.is_compress_step = is_step
         ctx.compress_selected_batch_indices = sel
         ctx.compress_selected_seq_ids = ids

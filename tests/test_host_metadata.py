@@ -128,6 +128,7 @@ def test_periodic_fill_context_host_companions():
     ctx = Context(use_decode_kernel=True, context_lens=torch.from_numpy(meta.context_lens))
     sched.fill_context(ctx, seqs, meta)
     assert ctx.is_compress_step and ctx.compress_selected_batch_indices == [0, 2]
+    assert ctx.compress_any  # compression steps run eagerly
     assert ctx.compress_selected_t.tolist() == [0, 2]
     assert ctx.compress_base_context_lens_host == [1500, 900, 2000]
     assert ctx.block_tables_host[1][:4] == seqs[1].block_table
