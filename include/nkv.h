@@ -181,6 +181,36 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
                            int32_t block_size, float softmax_scale,
                            int32_t* out_keep_idx, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* 4. Paged decode without a caller-provided workspace                       */
+/* No counterpart in the reference: an addition for callers that cannot      */
+/* allocate device memory -- code that runs while a CUDA graph is being      */
+/* captured, serving runtimes whose memory pool is sealed after start-up,    */
+/* and plugin hosts that hand a kernel its inputs and outputs but no scratch */
+/* buffer. It computes exactly what nkv_paged_decode computes, with the same */
+/* arguments minus the workspace, and allocates nothing: its scratch is a    */
+/* fixed array of NKV_STATIC_SCRATCH_BYTES in the library's device image,    */
+/* present on every GPU that loads libnkv.so until the process exits.        */
+/*   - A problem whose nkv_paged_decode_workspace_size exceeds               */
+/*     NKV_STATIC_SCRATCH_BYTES is rejected with NKV_ERR_WORKSPACE before     */
+/*     anything is launched (16 MiB covers e.g. batch 64 x 8 kv heads of     */
+/*     8k-token contexts; use nkv_paged_decode for larger batches).          */
+/*   - The first call on each device looks up the array's device address     */
+/*     (cudaGetSymbolAddress with that device current); make that first call */
+/*     outside any stream capture.                                           */
+/*   - Every call on a device shares the one array and clears the counters   */
+/*     it needs on `stream` before the launch. Calls that overlap on the GPU */
+/*     (different streams without ordering between them) race on it.        */
+#define NKV_STATIC_SCRATCH_BYTES (16u << 20)
+int nkv_paged_decode_static_scratch(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                    const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                    const int32_t* block_tables, int32_t max_blocks,
+                                    const int32_t* context_lens,
+                                    void* out, int64_t out_stride_token,
+                                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                    int32_t head_dim, int32_t block_size, float softmax_scale,
+                                    void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -475,3 +475,66 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ static scratch
+// Paged decode for callers that cannot allocate device memory (nkv.h,
+// section 4). Its scratch is this fixed array in the library's device image:
+// every GPU that loads the library holds NKV_STATIC_SCRATCH_BYTES of it until
+// the process exits. In host code the name below is only a stand-in symbol,
+// not a device address; the address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_static_decode_scratch[NKV_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+void* g_static_scratch_addr[kMaxDevices] = {nullptr};
+std::mutex g_static_scratch_mutex;
+
+// Device address of g_static_decode_scratch on the current device, looked up
+// once per device with that device current (the first call may load the
+// module, so it belongs outside stream capture).
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= kMaxDevices) return NKV_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_decode_scratch);
+    if (e != cudaSuccess) return cuda_status(e);
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = g_static_scratch_addr[dev];
+  return NKV_OK;
+}
+
+}  // namespace
+
+extern "C" int nkv_paged_decode_static_scratch(
+    const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+    const void* v_cache, int64_t num_blocks, const int32_t* block_tables, int32_t max_blocks,
+    const int32_t* context_lens, void* out, int64_t out_stride_token, int32_t batch,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    float softmax_scale, void* stream) {
+  // Argument validation of nkv_paged_decode: without a workspace it stops at
+  // NKV_ERR_WORKSPACE exactly when every other check passed (nothing launched).
+  const int pre = nkv_paged_decode(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks,
+                                   block_tables, max_blocks, context_lens, out, out_stride_token,
+                                   batch, num_q_heads, num_kv_heads, head_dim, block_size,
+                                   softmax_scale, nullptr, 0, stream);
+  if (pre != NKV_ERR_WORKSPACE) return pre;  // an argument error, or batch == 0 (no-op)
+  const DecodePlan pl = make_decode_plan(batch, num_q_heads, num_kv_heads, max_blocks, block_size);
+  if (pl.total > NKV_STATIC_SCRATCH_BYTES) return NKV_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = static_scratch_address(&scratch);
+  if (st != NKV_OK) return st;
+  // The array keeps the previous call's bytes: zero the scheduler and split
+  // counters this call uses (partial results need no clearing).
+  const size_t counter_bytes = pl.off_split_counters + sizeof(unsigned int) * pl.pairs;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e);
+  return nkv_paged_decode(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks,
+                          block_tables, max_blocks, context_lens, out, out_stride_token, batch,
+                          num_q_heads, num_kv_heads, head_dim, block_size, softmax_scale, scratch,
+                          NKV_STATIC_SCRATCH_BYTES, stream);
+}

@@ -29,6 +29,9 @@ DEVERR_WAIT_TIMEOUT = 0x4
 DEVERR_COMPRESS_RANGE = 0x8
 DEVERR_RING_RANGE = 0x10
 
+# Size of the library's fixed decode scratch (NKV_STATIC_SCRATCH_BYTES, nkv.h).
+STATIC_SCRATCH_BYTES = 16 << 20
+
 _P = c_void_p
 _I32P = c_void_p  # device int32 pointers are passed as raw addresses
 
@@ -61,6 +64,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, c_int64, _P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _I32P,
          c_int32, c_int32, c_int32, _P],
+    ),
+    "nkv_paged_decode_static_scratch": (
+        c_int,
+        [_P, c_int64, c_int64, _P, _P, c_int64, _I32P, c_int32, _I32P, _P, c_int64,
+         c_int32, c_int32, c_int32, c_int32, c_int32, c_float, _P],
     ),
     "nkv_threshold_compress": (
         c_int,
