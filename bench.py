@@ -362,7 +362,8 @@ def cpu_decode_sample(seconds: float, hq: int, hk: int):
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    hq, hk = HQ // world, HK // world
+    # the CPU implementation serves the whole job (all heads) whatever N is
+    hq, hk = HQ, HK
     per_step = max(2.0, 40.0 / max(1, args.steps + args.warmup))
     vals = []
     desc = ""

@@ -182,9 +182,17 @@ constexpr size_t kMaxSmem = 227 * 1024;
 template <typename Kernel, typename Params>
 int launch_cluster(Kernel kernel, const Params& p, int cluster_x, int grid_y, size_t smem,
                    cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return cuda_status(e);
+  // Raise the kernel's dynamic shared-memory limit only when a call needs
+  // more than any earlier call on this device (one host call, not per launch).
+  static size_t smem_set[kMaxDevices] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || smem > smem_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e);
+    if (dev >= 0 && dev < kMaxDevices) smem_set[dev] = smem;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster_x, grid_y, 1);
   cfg.blockDim = dim3(nkv::kCompressThreads, 1, 1);

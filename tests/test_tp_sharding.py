@@ -1,0 +1,88 @@
+"""Tensor-parallel sharding of the path by KV head, on CPU with gloo ranks.
+
+Under TP each rank holds Hk/N kv heads and their Hq/N q heads of every layer
+(nanokvllm/models/qwen3.py:53-59, engine/model_runner.py:140). Two properties
+the multi-GPU path relies on, checked with world_size 2 on the CPU oracle:
+  * decode shards, concatenated over heads, equal the unsharded decode;
+  * after a compression step every rank reports the same new lengths,
+    keep_blocks and freed blocks (rank 0's events drive the host metadata),
+    although each rank ranks tokens by its local heads only.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, repo, out_q):
+    import sys
+    sys.path[:0] = [repo]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle.attention import paged_decode_ref, store_kvcache_ref
+        from oracle.inputs import make_paged_batch
+        from oracle.window_compress import compression_events, window_compress_ref
+
+        Hq, Hk = 16, 8
+        pb = make_paged_batch(seed=5, lens=[300, 1300, 2100, 1500], Hq=Hq, Hk=Hk)
+        hk, hq = Hk // world, Hq // world
+        ks, vs = slice(rank * hk, (rank + 1) * hk), slice(rank * hq, (rank + 1) * hq)
+        kc = pb.k_cache[:, :, ks].contiguous()
+        vc = pb.v_cache[:, :, ks].contiguous()
+        q = pb.q[:, vs].contiguous()
+        store_kvcache_ref(pb.k_new[:, ks].contiguous(), pb.v_new[:, ks].contiguous(), kc, vc,
+                          pb.slot_mapping)
+        dec = paged_decode_ref(q, kc, vc, pb.block_tables, pb.context_lens, 128 ** -0.5)
+        sel = [1, 2, 3]
+        cl = pb.context_lens.clone()
+        keep, new_lens = window_compress_ref(q, kc, vc, pb.block_tables, pb.context_lens.clone(), cl,
+                                             sel, 256, 4, 2, 1)
+        ev = compression_events(pb.block_tables, sel, new_lens, 256, 0)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, {"dec": dec, "events": ev, "lens": cl.tolist(),
+                                          "keep": keep})
+        if rank == 0:
+            out_q.put(gathered)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_kv_head_sharding():
+    from oracle.attention import paged_decode_ref, store_kvcache_ref
+    from oracle.inputs import make_paged_batch
+
+    world = 2
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, repo, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    gathered = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # decode: per-rank head shards concatenate to the unsharded result
+    pb = make_paged_batch(seed=5, lens=[300, 1300, 2100, 1500], Hq=16, Hk=8)
+    kc, vc = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(pb.k_new, pb.v_new, kc, vc, pb.slot_mapping)
+    full = paged_decode_ref(pb.q, kc, vc, pb.block_tables, pb.context_lens, 128 ** -0.5)
+    cat = torch.cat([g["dec"] for g in gathered], dim=1)
+    assert torch.allclose(cat, full, atol=1e-5)
+    # compression metadata agrees across ranks
+    assert gathered[0]["events"] == gathered[1]["events"]
+    assert gathered[0]["lens"] == gathered[1]["lens"] == [300, 789, 1589, 989]
+    assert gathered[0]["keep"].shape == gathered[1]["keep"].shape
