@@ -193,8 +193,8 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
 /* present on every GPU that loads libnkv.so until the process exits.        */
 /*   - A problem whose nkv_paged_decode_workspace_size exceeds               */
 /*     NKV_STATIC_SCRATCH_BYTES is rejected with NKV_ERR_WORKSPACE before     */
-/*     anything is launched (16 MiB covers e.g. batch 64 x 8 kv heads of     */
-/*     8k-token contexts; use nkv_paged_decode for larger batches).          */
+/*     anything is launched (16 MiB covers e.g. batch 256 x 8 kv heads of    */
+/*     8k-token contexts, 8.8 MB; use nkv_paged_decode for larger batches).  */
 /*   - The first call on each device looks up the array's device address     */
 /*     (cudaGetSymbolAddress with that device current); make that first call */
 /*     outside any stream capture.                                           */

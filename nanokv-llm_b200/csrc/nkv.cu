@@ -98,18 +98,26 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 // split-counter region of the workspace).
 constexpr int kMaxDecodePairs = 1 << 16;
 
+// Longest split (tokens of one sequence and kv head per work item).
+#ifndef NKV_DECODE_MAX_SPLIT_TOKENS
+#define NKV_DECODE_MAX_SPLIT_TOKENS 4096
+#endif
+
 // Split size depends only on the shapes (not on the device or the lengths), so
 // the workspace query and the launch always agree.
 DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block_size) {
   DecodePlan pl{};
   pl.g = hq / hk;
   pl.pairs = batch * hk;
-  // Aim for >= ~8 work items per SM of a 148-SM part when every row is full,
-  // with splits of 1..4 blocks of 256 tokens.
+  // Splits as long as possible (every item ends in a cross-warp merge and,
+  // when split, a cross-CTA combine; at 1 KiB-token splits that costs ~13 %
+  // of the bandwidth on B200) while still giving ~2 items per SM of a
+  // 148-SM part when every row is full, so the dynamic scheduler can balance
+  // ragged lengths: 1 block .. NKV_DECODE_MAX_SPLIT_TOKENS.
   const int64_t block_units = static_cast<int64_t>(pl.pairs) * std::max(max_blocks, 1);
-  const int64_t target_items = 8 * 148;
+  const int64_t target_items = 2 * 148;
   int cb = static_cast<int>(block_units / target_items);
-  const int max_cb = std::max(1, 1024 / block_size);
+  const int max_cb = std::max(1, NKV_DECODE_MAX_SPLIT_TOKENS / block_size);
   pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
   pl.chunk_tokens = pl.chunk_blocks * block_size;
   pl.max_splits = std::max(1, (std::max(max_blocks, 1) + pl.chunk_blocks - 1) / pl.chunk_blocks);

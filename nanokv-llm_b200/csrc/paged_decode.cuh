@@ -472,11 +472,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       }
     }
     if (nsplit > 1) {
-      __threadfence();
+      // Hand-off between the CTAs of a row: the CTA barrier orders every
+      // thread's partial stores before thread 0's gpu-scope release; the
+      // acquire half of the same atomic makes the other splits' partials
+      // visible to the last arriver, and the next barrier to its threads.
       consumer_sync();
       if (!alive) break;
       if (ctid == 0) {
-        const unsigned int prev = atomicAdd(&p.split_counters[pair], 1u);
+        const unsigned int prev = atomic_add_acq_rel_gpu(&p.split_counters[pair], 1u);
         const int last = (prev == static_cast<unsigned int>(nsplit - 1)) ? 1 : 0;
         if (last) atomicExch(&p.split_counters[pair], 0u);
         flags[1] = last;
@@ -484,7 +487,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       consumer_sync();
       if (!alive) break;
       if (flags[1]) {
-        __threadfence();
         for (int row = 0; row < g; ++row) {
           const int64_t base = static_cast<int64_t>(pair) * p.max_splits * g + row;
           float M = NEG_INF;

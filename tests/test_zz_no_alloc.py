@@ -55,7 +55,7 @@ def test_static_scratch_refuses_oversized_problem(cuda_lib):
     from nanokv_b200 import _lib
 
     lib = cuda_lib
-    B, Hq, Hk, max_blocks = 256, 32, 8, 32  # the config-2 decode batch
+    B, Hq, Hk, max_blocks = 2048, 32, 8, 32  # 2048 rows of 8k-token contexts: ~35 MB of scratch
     assert lib.nkv_paged_decode_workspace_size(B, Hq, Hk, 128, max_blocks, 256) > _lib.STATIC_SCRATCH_BYTES
     q = torch.zeros(B, Hq, 128, dtype=torch.bfloat16, device=DEV)
     kc = torch.zeros(4, 256, Hk, 128, dtype=torch.bfloat16, device=DEV)
