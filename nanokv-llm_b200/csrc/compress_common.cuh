@@ -1,0 +1,223 @@
+// Building blocks shared by the two compression kernels (periodic window and
+// KvChat threshold): block-wide reductions and scans, the deterministic
+// bf16 top-k, and the in-place row compaction.
+#pragma once
+#include <cooperative_groups.h>
+
+#include "nkv_common.cuh"
+
+namespace nkv {
+
+namespace cg = cooperative_groups;
+
+constexpr int kCompressThreads = 256;
+constexpr int kCompressWarps = kCompressThreads / 32;
+constexpr int kCompressHeadDim = 128;
+constexpr int kCompactChunkRows = 64;
+constexpr int kMaxWindowBlocks = 64;
+constexpr int kReduceSlots = 16 * kCompressWarps;  // floats/ints of scratch for reductions
+
+// ---------------------------------------------------------------- block helpers
+__device__ __forceinline__ int block_sum_int(int v, int* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = __reduce_add_sync(0xffffffffu, v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int tot = 0;
+#pragma unroll
+  for (int w = 0; w < kCompressWarps; ++w) tot += red[w];
+  __syncthreads();
+  return tot;
+}
+
+// Exclusive prefix sum over threads in index order.
+__device__ __forceinline__ int block_excl_scan(int v, int* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) red[warp] = x;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += red[w];
+  __syncthreads();
+  return before + x - v;
+}
+
+// In-place block-wide max (kMax) or sum over each of N per-thread values.
+template <int N, bool kMax>
+__device__ __forceinline__ void block_reduce_vec_impl(float (&v)[N], float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int r = 0; r < N; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float x = __shfl_xor_sync(0xffffffffu, v[r], o);
+      v[r] = kMax ? fmaxf(v[r], x) : v[r] + x;
+    }
+    if (lane == 0) red[r * kCompressWarps + warp] = v[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < N; ++r) {
+    float a = red[r * kCompressWarps];
+#pragma unroll
+    for (int w = 1; w < kCompressWarps; ++w) {
+      const float x = red[r * kCompressWarps + w];
+      a = kMax ? fmaxf(a, x) : a + x;
+    }
+    v[r] = a;
+  }
+  __syncthreads();
+}
+
+template <int N, bool kMax>
+__device__ __forceinline__ void block_reduce_vec(float (&v)[N], float* red) {
+  block_reduce_vec_impl<N, kMax>(v, red);
+}
+
+__device__ __forceinline__ float block_max_float(float v, float* red) {
+  float a[1] = {v};
+  block_reduce_vec_impl<1, true>(a, red);
+  return a[0];
+}
+
+__device__ __forceinline__ float block_sum_float(float v, float* red) {
+  float a[1] = {v};
+  block_reduce_vec_impl<1, false>(a, red);
+  return a[0];
+}
+
+// Bit pattern of a non-negative bf16 value: monotone in the value.
+__device__ __forceinline__ uint32_t bf16_key(float v) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+}
+
+// Selects the `k` largest of keys[0, n) (ties -> lower index) and writes their
+// indices, ascending, to out[0, k). Keys live in shared memory. Each thread
+// owns a contiguous index range so that scans follow index order.
+__device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int* red) {
+  const int per = (n + kCompressThreads - 1) / kCompressThreads;
+  const int lo = threadIdx.x * per;
+  const int hi = min(lo + per, n);
+  uint32_t prefix = 0;
+  for (int bit = 15; bit >= 0; --bit) {
+    const uint32_t cand = prefix | (1u << bit);
+    int c = 0;
+    for (int t = lo; t < hi; ++t) c += (keys[t] >= cand) ? 1 : 0;
+    if (block_sum_int(c, red) >= k) prefix = cand;
+  }
+  // prefix is now the k-th largest key.
+  int gt = 0, eq = 0;
+  for (int t = lo; t < hi; ++t) {
+    gt += (keys[t] > prefix) ? 1 : 0;
+    eq += (keys[t] == prefix) ? 1 : 0;
+  }
+  const int total_gt = block_sum_int(gt, red);
+  const int need_eq = k - total_gt;
+  const int eq_before = block_excl_scan(eq, red);
+  int kept = 0;
+  {
+    int e = eq_before;
+    for (int t = lo; t < hi; ++t) {
+      const bool is_eq = keys[t] == prefix;
+      kept += (keys[t] > prefix || (is_eq && e < need_eq)) ? 1 : 0;
+      e += is_eq ? 1 : 0;
+    }
+  }
+  int pos = block_excl_scan(kept, red);
+  {
+    int e = eq_before;
+    for (int t = lo; t < hi; ++t) {
+      const bool is_eq = keys[t] == prefix;
+      if (keys[t] > prefix || (is_eq && e < need_eq)) out[pos++] = t;
+      e += is_eq ? 1 : 0;
+    }
+  }
+  __syncthreads();
+}
+
+// Moves rows src(i) -> dst(i), i in [0, n), of this CTA's kv-head slice (256
+// bytes of K and of V per row), 64 rows per chunk, with the reads of chunk
+// c+1 overlapping the writes of chunk c. Safe for in-place compaction when
+// source index(i) >= i and destinations are the window's positions 0..n-1:
+//   * every source of a chunk lies at or beyond its own first destination,
+//     so no chunk's writes reach a source of a LATER chunk, and a later
+//     chunk never reads a row an earlier chunk wrote;
+//   * a chunk's sources may lie in the NEXT chunk's destination range, so a
+//     barrier separates the reads of chunk c from the writes of chunk c+1.
+// Rows with src == dst or an unresolved slot (< 0) are skipped.
+template <typename SlotFn>
+__device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
+                                       int num_kv_heads, int head, int n, SlotFn slots) {
+  const int t = threadIdx.x;
+  const int row = t >> 2;      // 64 rows x 4 threads
+  const int quarter = t & 3;   // 4 x 64 bytes of a 256-byte head row
+  auto kptr = [&](int64_t slot) {
+    return reinterpret_cast<uint4*>(k_cache + (slot * num_kv_heads + head) * kCompressHeadDim) +
+           quarter * 4;
+  };
+  auto vptr = [&](int64_t slot) {
+    return reinterpret_cast<uint4*>(v_cache + (slot * num_kv_heads + head) * kCompressHeadDim) +
+           quarter * 4;
+  };
+  uint4 kc[4], vc[4];
+  int64_t dst_c = -1;
+  {
+    int64_t src = -1;
+    if (row < n) slots(row, src, dst_c);
+    if (row < n && src >= 0 && dst_c >= 0 && src != dst_c) {
+      const uint4* ks = kptr(src);
+      const uint4* vs = vptr(src);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        kc[u] = ks[u];
+        vc[u] = vs[u];
+      }
+    } else {
+      dst_c = -1;
+    }
+  }
+  __syncthreads();
+  for (int base = 0; base < n; base += kCompactChunkRows) {
+    const int i = base + kCompactChunkRows + row;
+    uint4 kn[4], vn[4];
+    int64_t dst_n = -1;
+    if (i < n) {
+      int64_t src = -1;
+      slots(i, src, dst_n);
+      if (src >= 0 && dst_n >= 0 && src != dst_n) {
+        const uint4* ks = kptr(src);
+        const uint4* vs = vptr(src);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          kn[u] = ks[u];
+          vn[u] = vs[u];
+        }
+      } else {
+        dst_n = -1;
+      }
+    }
+    if (dst_c >= 0) {
+      uint4* kd = kptr(dst_c);
+      uint4* vd = vptr(dst_c);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        kd[u] = kc[u];
+        vd[u] = vc[u];
+      }
+    }
+    __syncthreads();
+    dst_c = dst_n;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      kc[u] = kn[u];
+      vc[u] = vn[u];
+    }
+  }
+}
+
+}  // namespace nkv

@@ -164,35 +164,14 @@ int padded_group(int g) {
   return 0;
 }
 
-size_t window_smem_bytes(int g, int keys_pad, int keep_tokens) {
-  size_t b = 0;
-  b += sizeof(float) * g * nkv::kCompressHeadDim;            // qs
-  b += sizeof(float) * static_cast<size_t>(g) * keys_pad;   // scores
-  b += sizeof(float) * keys_pad;                             // partial
-  b += sizeof(uint16_t) * (keys_pad + 2);                    // keys
-  b += sizeof(int) * keep_tokens;                            // final_idx
-  b += sizeof(int) * (nkv::kMaxWindowBlocks + 32);           // window blocks + reduction
-  return b;
-}
-
-size_t threshold_smem_bytes(int g, int nk, int keys_pad, int R, bool stage) {
-  size_t b = stage ? static_cast<size_t>(nk) * nkv::kCompressHeadDim * 2 : 0;
-  b += sizeof(float) * g * nkv::kCompressHeadDim;
-  b += 2 * sizeof(float) * static_cast<size_t>(g) * keys_pad;
-  b += sizeof(float) * keys_pad;
-  b += sizeof(uint16_t) * (keys_pad + 2);
-  b += sizeof(int) * (R + 32);
-  return b;
-}
-
 constexpr size_t kMaxSmem = 227 * 1024;
 
+// Launches `kernel` with clusters of cluster_x CTAs along x. `smem_set` is
+// the caller's per-kernel record of the dynamic shared-memory limit already
+// granted on each device; the limit is raised only when a call needs more.
 template <typename Kernel, typename Params>
-int launch_cluster(Kernel kernel, const Params& p, int cluster_x, int grid_y, size_t smem,
-                   cudaStream_t stream) {
-  // Raise the kernel's dynamic shared-memory limit only when a call needs
-  // more than any earlier call on this device (one host call, not per launch).
-  static size_t smem_set[kMaxDevices] = {0};
+int launch_cluster(Kernel kernel, size_t* smem_set, const Params& p, int cluster_x, int grid_y,
+                   size_t smem, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices || smem > smem_set[dev]) {
@@ -214,6 +193,22 @@ int launch_cluster(Kernel kernel, const Params& p, int cluster_x, int grid_y, si
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cuda_status(cudaLaunchKernelEx(&cfg, kernel, p));
+}
+
+template <int G>
+int launch_threshold(const nkv::ThresholdCompressParams& p, int cluster_x, int grid_y,
+                     size_t smem, cudaStream_t stream) {
+  static size_t smem_set[kMaxDevices] = {0};
+  return launch_cluster(nkv::threshold_compress_kernel<G>, smem_set, p, cluster_x, grid_y, smem,
+                        stream);
+}
+
+template <int G>
+int launch_window(const nkv::WindowCompressParams& p, int cluster_x, int grid_y, size_t smem,
+                  cudaStream_t stream) {
+  static size_t smem_set[kMaxDevices] = {0};
+  return launch_cluster(nkv::window_compress_kernel<G>, smem_set, p, cluster_x, grid_y, smem,
+                        stream);
 }
 
 }  // namespace
@@ -406,10 +401,17 @@ int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, vo
   p.block_size = block_size;
   p.num_keys = window_tokens - obs_window;
   p.keys_pad = ((p.num_keys + nkv::kCompressThreads - 1) / nkv::kCompressThreads) * nkv::kCompressThreads;
-  const size_t smem = window_smem_bytes(g, p.keys_pad, keep_tokens);
+  const int G = padded_group(g);
+  const size_t smem = nkv::window_smem_bytes(G, p.keys_pad, keep_tokens);
   if (smem > kMaxSmem) return NKV_ERR_UNSUPPORTED;
-  return launch_cluster(nkv::window_compress_kernel, p, num_kv_heads, num_selected, smem,
-                        static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (G) {
+    case 1: return launch_window<1>(p, num_kv_heads, num_selected, smem, s);
+    case 2: return launch_window<2>(p, num_kv_heads, num_selected, smem, s);
+    case 4: return launch_window<4>(p, num_kv_heads, num_selected, smem, s);
+    case 8: return launch_window<8>(p, num_kv_heads, num_selected, smem, s);
+    default: return launch_window<16>(p, num_kv_heads, num_selected, smem, s);
+  }
 }
 
 // ------------------------------------------------------------------ KvChat
@@ -478,16 +480,26 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
   p.g = g;
   p.block_size = block_size;
   p.num_keys = compress_S - W;
-  p.keys_pad = ((p.num_keys + nkv::kCompressThreads - 1) / nkv::kCompressThreads) * nkv::kCompressThreads;
-  size_t smem = threshold_smem_bytes(g, p.num_keys, p.keys_pad, compress_R, true);
-  p.stage_keys = 1;
-  if (smem > kMaxSmem) {
-    smem = threshold_smem_bytes(g, p.num_keys, p.keys_pad, compress_R, false);
-    p.stage_keys = 0;
+  p.keys_pad = ((p.num_keys + nkv::kThrKeyTile - 1) / nkv::kThrKeyTile) * nkv::kThrKeyTile;
+  p.rows = g * W;
+  p.mtiles = (p.rows + 15) / 16;
+  const int G = padded_group(g);
+  if (G == 0) return NKV_ERR_UNSUPPORTED;
+  // As many 16-row m-tiles per row group as shared memory (and the 8 warps)
+  // allow; more groups re-stream the keys from L2.
+  int gm = std::min(p.mtiles, nkv::kCompressWarps);
+  while (gm > 0 && nkv::threshold_smem_bytes(G, p.keys_pad, gm, compress_R) > kMaxSmem) --gm;
+  if (gm == 0) return NKV_ERR_UNSUPPORTED;
+  p.group_mtiles = gm;
+  const size_t smem = nkv::threshold_smem_bytes(G, p.keys_pad, gm, compress_R);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (G) {
+    case 1: return launch_threshold<1>(p, num_kv_heads, num_selected, smem, s);
+    case 2: return launch_threshold<2>(p, num_kv_heads, num_selected, smem, s);
+    case 4: return launch_threshold<4>(p, num_kv_heads, num_selected, smem, s);
+    case 8: return launch_threshold<8>(p, num_kv_heads, num_selected, smem, s);
+    default: return launch_threshold<16>(p, num_kv_heads, num_selected, smem, s);
   }
-  if (smem > kMaxSmem) return NKV_ERR_UNSUPPORTED;
-  return launch_cluster(nkv::threshold_compress_kernel, p, num_kv_heads, num_selected, smem,
-                        static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -8,24 +8,31 @@
 // decode graph (the reference's Python loop cannot, so graph replays never
 // append; the reference then scores uninitialised rows).
 //
-// threshold_compress_kernel replaces MyCompressCompact
+// threshold_compress_kernel<G> replaces MyCompressCompact
 // (KvChat/layers/compress_utils.py:10-171) with TritonGetKVForComp (:218-252)
 // and SnapKV(window=W, num_keep=R-W-1) (KvChat/layers/CompressMethod.py:4-58).
-// Launch: grid (num_kv_heads, num_selected), one cluster per sequence.
-//   * Keys are positions [0, S-W) of the sequence (TritonGetKVForComp gathers
-//     the first S positions; the compaction window starts at
-//     max(len - S, 0) -- the two coincide whenever compression triggers).
-//   * The CTA stages its kv head's key rows in shared memory once (when they
-//     fit) and, for each of the W window queries, scores all keys for its g
-//     query heads (bf16(q.k), bf16(* scale), sink -> -inf), takes the per-row
-//     softmax (bf16 output) and accumulates it over the window in fp32; the
-//     window sum is rounded to bf16 per head, summed over the group in fp32,
-//     and the cluster sum of those partials is rounded to bf16 -- the two
-//     bf16 roundings of the reference's sum(dim=2).sum(dim=1).
-//   * Top-k / ordering / in-place compaction as in the window kernel; kept
-//     rows go to positions [0, R) of the block table; context_lens[b] = R.
+// Launch: grid (num_kv_heads, num_selected), one cluster per sequence, CTA
+// rank = kv head. The g x W window queries of the group are the rows of a
+// dense [g*W x 128] x [128 x keys] product, so scoring runs on tensor cores:
+//   A. per row group (up to 8 m-tiles of 16 rows, sized to shared memory):
+//      K tiles of 64 keys (positions [0, S-W), gathered through the block
+//      table with cp.async, double-buffered) meet the rows' A fragments in
+//      mma.sync m16n8k16; every score is rounded like the reference
+//      (bf16(q.k), bf16(* scale), sink key 0 -> -inf) and kept as bf16 in
+//      shared memory;
+//   B. per row: max and sum of exp over the keys (fp32);
+//   C. per key: for each head, the bf16 softmax probabilities of its W rows
+//      are added in window order into an fp32 accumulator (deterministic).
+//   Then the window sum is rounded to bf16 per head, summed over the group in
+//   fp32, and the cluster sum of those partials is rounded to bf16 -- the two
+//   bf16 roundings of the reference's sum(dim=2).sum(dim=1). Top-k, ordering
+//   and in-place compaction follow the window kernel; kept rows go to
+//   positions [0, R) of the block table and context_lens[b] = R.
+// Keys are positions [0, S-W) (TritonGetKVForComp gathers the first S
+// positions); the compaction window starts at max(len - S, 0). The two
+// coincide whenever compression triggers (len == S).
 #pragma once
-#include "window_compress.cuh"
+#include "compress_common.cuh"
 
 namespace nkv {
 
@@ -73,28 +80,33 @@ struct ThresholdCompressParams {
   int num_kv_heads;
   int g;
   int block_size;
-  int num_keys;      // S - W
-  int keys_pad;      // rounded up to kCompressThreads
-  int stage_keys;    // 1: key rows staged in shared memory
+  int num_keys;   // S - W
+  int keys_pad;   // num_keys rounded up to kThrKeyTile
+  int rows;       // g * W
+  int mtiles;     // ceil(rows / 16)
+  int group_mtiles;  // m-tiles per row group (<= kCompressWarps)
 };
 
-__device__ __forceinline__ float dot128_bf16_f32(const __nv_bfloat16* krow, const float* qrow) {
-  const uint4* kv = reinterpret_cast<const uint4*>(krow);
-  float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll 4
-  for (int c = 0; c < kCompressHeadDim / 8; ++c) {
-    const uint4 w = kv[c];
-    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = c * 8 + 2 * e;
-      acc0 = fmaf(qrow[d], __uint_as_float(wv[e] << 16), acc0);
-      acc1 = fmaf(qrow[d + 1], __uint_as_float(wv[e] & 0xffff0000u), acc1);
-    }
-  }
-  return acc0 + acc1;
+constexpr int kThrKeyTile = 64;
+constexpr int kThrKRowElems = kCompressHeadDim + 8;  // padded smem row: conflict-free ldmatrix
+
+__host__ __device__ constexpr int thr_score_stride(int keys_pad) { return keys_pad + 8; }
+
+// Shared-memory bytes of threshold_compress_kernel (host and device agree).
+__host__ __device__ constexpr size_t threshold_smem_bytes(int G, int keys_pad, int group_mtiles,
+                                                          int R) {
+  return sizeof(__nv_bfloat16) * 2 * kThrKeyTile * kThrKRowElems                 // K tiles
+         + sizeof(__nv_bfloat16) * static_cast<size_t>(group_mtiles) * 16 *
+               thr_score_stride(keys_pad)                                        // scores
+         + sizeof(float) * 2 * group_mtiles * 16                                 // row max, sum
+         + sizeof(float) * static_cast<size_t>(G) * keys_pad                     // window sums
+         + sizeof(float) * keys_pad                                              // partial
+         + sizeof(uint16_t) * (keys_pad + 2)                                     // keys
+         + sizeof(int) * R                                                       // final index
+         + sizeof(float) * kReduceSlots;                                         // reductions
 }
 
+template <int G>
 __global__ void __launch_bounds__(kCompressThreads, 1)
 threshold_compress_kernel(const ThresholdCompressParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -106,16 +118,19 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   const int kp = p.keys_pad;
   const int bs = p.block_size;
   const int W = p.window;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int ss = thr_score_stride(kp);
 
-  __nv_bfloat16* kst = reinterpret_cast<__nv_bfloat16*>(smem);  // [nk][128] if staged
-  const size_t kst_bytes = p.stage_keys ? static_cast<size_t>(nk) * kCompressHeadDim * 2 : 0;
-  float* qs = reinterpret_cast<float*>(smem + kst_bytes);       // [g][128]
-  float* srow = qs + g * kCompressHeadDim;                       // [g][kp]
-  float* kacc = srow + g * kp;                                   // [g][kp]
-  float* partial = kacc + g * kp;                                // [kp] (cluster-visible)
-  uint16_t* keys = reinterpret_cast<uint16_t*>(partial + kp);    // [kp]
-  int* final_idx = reinterpret_cast<int*>(keys + kp + (kp & 1));  // [R]
-  int* red = final_idx + p.R;                                    // [32]
+  __nv_bfloat16* ktile = reinterpret_cast<__nv_bfloat16*>(smem);           // [2][64][136]
+  __nv_bfloat16* sc = ktile + 2 * kThrKeyTile * kThrKRowElems;             // [group rows][ss]
+  float* rmax = reinterpret_cast<float*>(sc + static_cast<size_t>(p.group_mtiles) * 16 * ss);
+  float* rsum = rmax + p.group_mtiles * 16;
+  float* kacc = rsum + p.group_mtiles * 16;                                 // [G][kp]
+  float* partial = kacc + G * kp;                                           // [kp]
+  uint16_t* keys = reinterpret_cast<uint16_t*>(partial + kp);               // [kp]
+  int* final_idx = reinterpret_cast<int*>(keys + kp + 2);                   // [R]
+  float* red = reinterpret_cast<float*>(final_idx + p.R);                   // [kReduceSlots]
   __shared__ int s_valid;
   __shared__ int s_start;
 
@@ -140,71 +155,134 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     if (!valid && head == 0) raise_error(NKV_DEVERR_COMPRESS_RANGE);
     s_valid = valid;
   }
+  for (int i = threadIdx.x; i < G * kp; i += kCompressThreads) kacc[i] = 0.f;
   __syncthreads();
   const bool valid = s_valid != 0;
   const int start = s_start;
 
   if (valid) {
     const int rslot = __ldg(p.ring_slot_of_selected + sel_i);
-    // stage key rows (positions [0, S - W)) of this kv head
-    if (p.stage_keys) {
-      for (int i = threadIdx.x; i < nk * 16; i += kCompressThreads) {
-        const int t = i >> 4, c = i & 15;
-        const int64_t slot = slot_of(t);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (slot >= 0)
-          v = reinterpret_cast<const uint4*>(
-              p.k_cache + (slot * p.num_kv_heads + head) * kCompressHeadDim)[c];
-        reinterpret_cast<uint4*>(kst + static_cast<int64_t>(t) * kCompressHeadDim)[c] = v;
-      }
-    }
-    for (int i = threadIdx.x; i < g * kp; i += kCompressThreads) kacc[i] = 0.f;
-    __syncthreads();
-    for (int w = 0; w < W; ++w) {
-      const __nv_bfloat16* qbase =
-          p.ring + ((static_cast<int64_t>(rslot) * p.num_layers + p.layer_id) * W + w) *
-                       static_cast<int64_t>(p.num_q_heads) * kCompressHeadDim;
-      for (int i = threadIdx.x; i < g * kCompressHeadDim; i += kCompressThreads) {
-        const int r = i / kCompressHeadDim, d = i % kCompressHeadDim;
-        qs[i] = __bfloat162float(qbase[static_cast<int64_t>(head * g + r) * kCompressHeadDim + d]);
-      }
-      __syncthreads();
-      for (int t = threadIdx.x; t < nk; t += kCompressThreads) {
-        const __nv_bfloat16* krow;
-        if (p.stage_keys) {
-          krow = kst + static_cast<int64_t>(t) * kCompressHeadDim;
+    const __nv_bfloat16* qbase =
+        p.ring + (static_cast<int64_t>(rslot) * p.num_layers + p.layer_id) *
+                     static_cast<int64_t>(W) * p.num_q_heads * kCompressHeadDim;
+    const int ntiles = kp / kThrKeyTile;
+    // query row rho = r * W + w of this group -> its 128 bf16 values (or null)
+    auto qrow = [&](int rho) -> const __nv_bfloat16* {
+      if (rho >= p.rows) return nullptr;
+      const int r = rho / W, w = rho - r * W;
+      return qbase + (static_cast<int64_t>(w) * p.num_q_heads + head * g + r) * kCompressHeadDim;
+    };
+    auto load_ktile = [&](int tile, int buf) {
+      const uint32_t base = smem_u32(ktile + buf * kThrKeyTile * kThrKRowElems);
+      for (int i = threadIdx.x; i < kThrKeyTile * 16; i += kCompressThreads) {
+        const int kr = i >> 4, c = i & 15;
+        const int t = tile * kThrKeyTile + kr;
+        const uint32_t dst = base + (kr * kThrKRowElems + c * 8) * 2;
+        const int64_t slot = (t < nk) ? slot_of(t) : -1;
+        if (slot >= 0) {
+          cp_async_16(dst, p.k_cache + (slot * p.num_kv_heads + head) * kCompressHeadDim + c * 8);
         } else {
-          const int64_t slot = slot_of(t);
-          krow = p.k_cache + (max(slot, int64_t(0)) * p.num_kv_heads + head) * kCompressHeadDim;
+          *reinterpret_cast<uint4*>(ktile + buf * kThrKeyTile * kThrKRowElems +
+                                    kr * kThrKRowElems + c * 8) = make_uint4(0, 0, 0, 0);
         }
-        for (int r = 0; r < g; ++r) {
-          float v = -INFINITY;
-          if (t != 0) v = round_bf16(round_bf16(dot128_bf16_f32(krow, qs + r * kCompressHeadDim)) * p.scale);
-          srow[r * kp + t] = v;
+      }
+      cp_async_commit();
+    };
+
+    for (int group0 = 0; group0 < p.mtiles; group0 += p.group_mtiles) {
+      const int gm = min(p.group_mtiles, p.mtiles - group0);
+      const int row0 = group0 * 16;
+      // ---- A: scores of this row group
+      uint32_t qa[8][4];
+      const bool mma_warp = warp < gm;
+      if (mma_warp) {
+        const __nv_bfloat16* q_lo = qrow(row0 + warp * 16 + gid);
+        const __nv_bfloat16* q_hi = qrow(row0 + warp * 16 + gid + 8);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int d = kk * 16 + 2 * tig;
+          qa[kk][0] = q_lo ? *reinterpret_cast<const uint32_t*>(q_lo + d) : 0u;
+          qa[kk][1] = q_hi ? *reinterpret_cast<const uint32_t*>(q_hi + d) : 0u;
+          qa[kk][2] = q_lo ? *reinterpret_cast<const uint32_t*>(q_lo + d + 8) : 0u;
+          qa[kk][3] = q_hi ? *reinterpret_cast<const uint32_t*>(q_hi + d + 8) : 0u;
+        }
+      }
+      load_ktile(0, 0);
+      for (int tile = 0; tile < ntiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntiles) {
+          load_ktile(tile + 1, buf ^ 1);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (mma_warp) {
+          const uint32_t kb = smem_u32(ktile + buf * kThrKeyTile * kThrKRowElems);
+          const int lrow = warp * 16 + gid;
+#pragma unroll
+          for (int nt = 0; nt < kThrKeyTile / 8; ++nt) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {
+              const uint32_t addr =
+                  kb + ((nt * 8 + (lane & 7)) * kThrKRowElems + (kq * 4 + (lane >> 3)) * 8) * 2;
+              uint32_t b0, b1, b2, b3;
+              ldsm_x4(addr, b0, b1, b2, b3);
+              mma_bf16_16816(acc, qa[2 * kq][0], qa[2 * kq][1], qa[2 * kq][2], qa[2 * kq][3], b0, b1);
+              mma_bf16_16816(acc, qa[2 * kq + 1][0], qa[2 * kq + 1][1], qa[2 * kq + 1][2],
+                             qa[2 * kq + 1][3], b2, b3);
+            }
+            const int t0 = tile * kThrKeyTile + nt * 8 + 2 * tig;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int t = t0 + (e & 1);
+              v[e] = (t == 0 || t >= nk) ? -INFINITY : round_bf16(round_bf16(acc[e]) * p.scale);
+            }
+            *reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(lrow) * ss + t0) =
+                pack_bf16x2(v[0], v[1]);
+            *reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(lrow + 8) * ss + t0) =
+                pack_bf16x2(v[2], v[3]);
+          }
+        }
+        __syncthreads();  // the buffer is refilled by the next iteration
+      }
+      // ---- B: per-row max and sum of exp
+      const int grows = min(gm * 16, p.rows - row0);
+      for (int lr = warp; lr < grows; lr += kCompressWarps) {
+        const __nv_bfloat16* row = sc + static_cast<size_t>(lr) * ss;
+        float m = -INFINITY;
+        for (int t = lane; t < nk; t += 32) m = fmaxf(m, __bfloat162float(row[t]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float z = 0.f;
+        for (int t = lane; t < nk; t += 32) z += expf(__bfloat162float(row[t]) - m);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        if (lane == 0) {
+          rmax[lr] = m;
+          rsum[lr] = z;
         }
       }
       __syncthreads();
-      for (int r = 0; r < g; ++r) {
-        float* row = srow + r * kp;
-        float mx = -INFINITY;
-        for (int t = threadIdx.x; t < nk; t += kCompressThreads) mx = fmaxf(mx, row[t]);
-        mx = block_max_float(mx, reinterpret_cast<float*>(red));
-        float sum = 0.f;
-        for (int t = threadIdx.x; t < nk; t += kCompressThreads) {
-          const float e = expf(row[t] - mx);
-          row[t] = e;
-          sum += e;
+      // ---- C: per key, window-ordered sum of each head's bf16 probabilities
+      for (int t = threadIdx.x; t < nk; t += kCompressThreads) {
+        for (int lr = 0; lr < grows; ++lr) {
+          const int r = (row0 + lr) / W;
+          const float e = expf(__bfloat162float(sc[static_cast<size_t>(lr) * ss + t]) - rmax[lr]);
+          kacc[r * kp + t] += round_bf16(e / rsum[lr]);
         }
-        sum = block_sum_float(sum, reinterpret_cast<float*>(red));
-        for (int t = threadIdx.x; t < nk; t += kCompressThreads)
-          kacc[r * kp + t] += round_bf16(row[t] / sum);
       }
       __syncthreads();
     }
     for (int t = threadIdx.x; t < kp; t += kCompressThreads) {
       float s = 0.f;
-      if (t < nk)
-        for (int r = 0; r < g; ++r) s += round_bf16(kacc[r * kp + t]);
+      if (t < nk) {
+#pragma unroll
+        for (int r = 0; r < G; ++r)
+          if (r < g) s += round_bf16(kacc[r * kp + t]);
+      }
       partial[t] = s;
     }
   }
@@ -222,15 +300,15 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
 
   const int num_keep = p.R - W - 1;
   if (threadIdx.x == 0) final_idx[0] = 0;
-  topk_ascending(keys, nk, num_keep, final_idx + 1, red);
+  topk_ascending(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red));
   for (int i = threadIdx.x; i < W; i += kCompressThreads) final_idx[1 + num_keep + i] = p.S - W + i;
   __syncthreads();
 
-  compact_rows_in_order(p.k_cache, p.v_cache, p.num_kv_heads, head, p.R,
-                        [&](int i, int64_t& src, int64_t& dst) {
-                          src = slot_of(start + final_idx[i]);
-                          dst = slot_of(i);
-                        });
+  compact_rows_pipelined(p.k_cache, p.v_cache, p.num_kv_heads, head, p.R,
+                         [&](int i, int64_t& src, int64_t& dst) {
+                           src = slot_of(start + final_idx[i]);
+                           dst = slot_of(i);
+                         });
   if (head == 0) {
     if (threadIdx.x == 0) p.context_lens[b] = p.R;
     if (p.out_keep_idx) {
