@@ -236,17 +236,35 @@ def run_gpu(args, rank, world, dev):
               "context_lens": torch.tensor(st["lens"], dtype=torch.int32).pin_memory(),
               "block_tables": st["block_tables_h"].pin_memory()}
     qkv_d = torch.empty_like(qkv)
+    copy_stream = torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(LAYERS)]
+    out_ready = [torch.cuda.Event() for _ in range(LAYERS)]
 
     def e2e_step():
+        # Host buffers in, results out, every step. The inputs of all layers
+        # go host->device on a copy stream while the layers run; each layer
+        # waits only for its own inputs and its output is copied back as soon
+        # as its decode is done. The step ends when the last copy has landed.
+        cur = torch.cuda.current_stream(dev)
         sm_d = meta_h["slot_mapping"].to(dev, non_blocking=True)
         cl_d = meta_h["context_lens"].to(dev, non_blocking=True)
         bt_d = meta_h["block_tables"].to(dev, non_blocking=True)
         set_context(True, slot_mapping=sm_d, context_lens=cl_d, block_tables=bt_d)
+        copy_stream.wait_stream(cur)  # qkv_d is free once the previous step used it
+        with torch.cuda.stream(copy_stream):
+            for layer in range(LAYERS):
+                qkv_d[layer].copy_(qkv_h[layer], non_blocking=True)
+                in_ready[layer].record(copy_stream)
         for layer in range(LAYERS):
-            qkv_d[layer].copy_(qkv_h[layer], non_blocking=True)
+            cur.wait_event(in_ready[layer])
             q, k, v = layer_views(layer, qkv_d)
             o = layers[layer].forward(q, k, v, layer)
-            out_h[layer].copy_(o.view(BATCH, hq, D), non_blocking=True)
+            out_ready[layer].record(cur)
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(out_ready[layer])
+                o.record_stream(copy_stream)
+                out_h[layer].copy_(o.view(BATCH, hq, D), non_blocking=True)
+        cur.wait_stream(copy_stream)
         reset_context()
 
     for _ in range(args.warmup):
@@ -267,15 +285,21 @@ def run_gpu(args, rank, world, dev):
 
     # ---- compression cost on config 3 shapes (one event = 20 sequences, one layer)
     comp = measure_compress(dev, hq, hk)
+    # ---- the other BASELINE configs as kernel-level lines (rank 0's shard);
+    # the big KV of the main workload is released first
+    lens = st["lens"]
+    del kv, st, layers
+    torch.cuda.empty_cache()
+    extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world)}
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e_ms, statistics.mean(dec_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms, dec_avg = vals.tolist()
-    alg = algorithmic_decode_bytes(st["lens"], hk, hq)
+    alg = algorithmic_decode_bytes(lens, hk, hq)
     return dict(ms=ms, e2e_ms=e2e_ms, dec_avg_ms=dec_avg, alg_bytes=alg, clocks=clk,
-                resident=R, h2d=h2d, d2h=d2h, compress=comp)
+                resident=R, h2d=h2d, d2h=d2h, compress=comp, extra=extra)
 
 
 def measure_compress(dev, hq, hk):
@@ -319,6 +343,124 @@ def measure_compress(dev, hq, hk):
             "amortised_ms_per_step": round(t_layer_ms * LAYERS / 1024, 5),
             "sequences": 20, "period": 1024,
             "approx_alg_GBps": round(alg / (t_layer_ms * 1e-3) / 1e9, 1)}
+
+
+def measure_kvchat(dev, world):
+    """BASELINE config 5 (KvChat threshold path) on Qwen3-0.6B shapes: one
+    sequence, prompt 256, KV length oscillating between prompt+257 and
+    prompt+511. A decode step (28 layers of store + query-window append +
+    paged decode) is captured in a CUDA graph and replayed; a compression
+    event (28 layers of threshold compression) runs eagerly, as in the
+    reference, every 254 steps."""
+    from nanokv_b200 import ops
+
+    L, hq, hk, P, W = 28, 16 // world, 8 // world, 256, 50
+    S, R = P + 511, P + 257
+    mid = P + 384
+    nb = (S + BLOCK - 1) // BLOCK
+    kc = [torch.randn(nb, BLOCK, hk, D, device=dev).to(torch.bfloat16) for _ in range(L)]
+    vc = [torch.randn_like(k) for k in kc]
+    bt = torch.arange(nb, dtype=torch.int32, device=dev).view(1, nb)
+    cl = torch.tensor([mid], dtype=torch.int32, device=dev)
+    sm = torch.tensor([mid - 1], dtype=torch.int32, device=dev)
+    qkv = torch.randn(L, 1, (hq + 2 * hk) * D, device=dev).to(torch.bfloat16)
+    out = torch.empty(L, 1, hq, D, dtype=torch.bfloat16, device=dev)
+    ring = torch.zeros(1, L, W, hq, D, dtype=torch.bfloat16, device=dev)
+    zero = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = ops.decode_workspace(dev, 1, hq, hk, D, nb, BLOCK)
+
+    def step():
+        for layer in range(L):
+            q, k, v = qkv[layer].split([hq * D, hk * D, hk * D], dim=-1)
+            q, k, v = q.view(1, hq, D), k.view(1, hk, D), v.view(1, hk, D)
+            ops.store_kvcache(k, v, kc[layer], vc[layer], sm)
+            ops.query_window_append(q, ring, layer, zero, zero, zero)
+            ops.paged_decode(q, kc[layer], vc[layer], bt, cl, D ** -0.5, out=out[layer], workspace=ws)
+
+    step()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(5):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 50
+    a.record()
+    for _ in range(n):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    step_us = a.elapsed_time(b) / n * 1e3
+    del graph
+
+    sel = torch.zeros(1, dtype=torch.int32, device=dev)
+    times = []
+    for it in range(4):
+        torch.cuda.synchronize(dev)
+        cl.fill_(S)
+        a.record()
+        for layer in range(L):
+            ops.threshold_compress(ring, zero, layer, kc[layer], vc[layer], bt, cl, sel, S, R)
+        b.record()
+        torch.cuda.synchronize(dev)
+        if it:
+            times.append(a.elapsed_time(b))
+    event_ms = statistics.median(times)
+    period = S - R + 2  # steps between triggers: R+1 .. S
+    amort = event_ms * 1e3 / period
+    return {"workload": "config5: Qwen3-0.6B shapes, 28 layers, B=1, prompt 256, S=+511, R=+257, "
+                        "W=50; decode step replayed from a CUDA graph at KV length 640",
+            "decode_step_us": round(step_us, 1), "compress_event_ms": round(event_ms, 3),
+            "period_steps": period, "amortised_compress_us_per_step": round(amort, 2),
+            "tok_per_s": round(1e6 / (step_us + amort), 1)}
+
+
+def measure_config4(dev, world):
+    """BASELINE config 4 decode on Qwen3-32B attention shapes (64 q / 8 kv
+    heads, g = 8): batch 16 x 32,768-token contexts, one layer's store +
+    decode timed over 2 alternating layer caches (2.1 GB each at TP1), scaled
+    to 64 layers. Compression does not fire within config 4's 512 steps under
+    the reference's rules, so the step is store + decode."""
+    from nanokv_b200 import ops
+
+    hq, hk, B, Lctx, layers = 64 // world, 8 // world, 16, 32768, 64
+    nb = B * Lctx // BLOCK
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(4)).view(B, -1)
+    bt = perm.to(torch.int32).to(dev)
+    cl = torch.full((B,), Lctx, dtype=torch.int32, device=dev)
+    sm = (bt[:, -1].to(torch.int64) * BLOCK + BLOCK - 1).to(torch.int32)
+    caches = [(torch.empty(nb, BLOCK, hk, D, dtype=torch.bfloat16, device=dev).normal_(),
+               torch.empty(nb, BLOCK, hk, D, dtype=torch.bfloat16, device=dev).normal_())
+              for _ in range(2)]
+    qkv = torch.randn(B, (hq + 2 * hk) * D, device=dev).to(torch.bfloat16)
+    q, k, v = qkv.split([hq * D, hk * D, hk * D], dim=-1)
+    q, k, v = q.view(B, hq, D), k.view(B, hk, D), v.view(B, hk, D)
+    ws = ops.decode_workspace(dev, B, hq, hk, D, Lctx // BLOCK, BLOCK)
+    out = torch.empty(B, hq, D, dtype=torch.bfloat16, device=dev)
+
+    def layer(i):
+        kc, vc = caches[i % 2]
+        ops.store_kvcache(k, v, kc, vc, sm)
+        ops.paged_decode(q, kc, vc, bt, cl, D ** -0.5, out=out, workspace=ws)
+
+    for i in range(4):
+        layer(i)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    a.record()
+    for i in range(n):
+        layer(i)
+    b.record()
+    torch.cuda.synchronize(dev)
+    t = a.elapsed_time(b) / n * 1e-3
+    alg = algorithmic_decode_bytes([Lctx] * B, hk, hq)
+    return {"workload": "config4: Qwen3-32B attention shapes (64 q / 8 kv heads), B=16, ctx 32768, "
+                        "64 layers (store + decode); per-layer time measured, scaled x64",
+            "layer_us": round(t * 1e6, 1), "decode_GBps": round(alg / t / 1e9, 1),
+            "tok_per_s": round(B / (t * layers), 1)}
 
 
 # ---------------------------------------------------------------------- CPU arms
@@ -502,8 +644,9 @@ def main():
             "config": config_dict(world, r["resident"]),
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"],
-                    "path": "nanokv_b200.layers.attention.Attention.forward per layer, q/k/v "
-                            "from pinned host memory, outputs copied back"},
+                    "path": "nanokv_b200.layers.attention.Attention.forward per layer; every "
+                            "step copies all layers' q/k/v from pinned host memory (copy stream, "
+                            "overlapped with compute) and copies every output back"},
             "roofline": {"kernel": "nkv paged_decode_kernel", "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} hbm_gbs",
@@ -513,6 +656,7 @@ def main():
             "clocks": r["clocks"],
             "gpu_launches": args.steps * LAYERS * 2,
             "compress": r["compress"],
+            **r["extra"],
         }
         print(json.dumps(line))
     if world > 1:
