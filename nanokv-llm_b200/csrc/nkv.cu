@@ -301,7 +301,7 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
   if (!std::isfinite(softmax_scale)) return NKV_ERR_INVALID_ARGUMENT;
   if (out_stride_token < static_cast<int64_t>(num_q_heads) * head_dim) return NKV_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (q_stride_token % 8) ||
-      (q_stride_head % 8))
+      (q_stride_head % 8) || (reinterpret_cast<uintptr_t>(out) & 7u) || (out_stride_token % 4))
     return NKV_ERR_ALIGNMENT;
   const DecodePlan pl = make_decode_plan(batch, num_q_heads, num_kv_heads, max_blocks, block_size);
   if (!workspace || workspace_bytes < pl.total) return NKV_ERR_WORKSPACE;

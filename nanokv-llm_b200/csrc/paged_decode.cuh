@@ -6,23 +6,28 @@
 //   * Work item = (split s, batch row b, kv head h): up to `chunk` tokens of
 //     one sequence for one kv head and ALL g = Hq/Hk query heads of that group
 //     (GQA grouping: a K/V tile is read once for the whole group).
-//   * Persistent CTAs (one per SM). Warp 4 is the producer: one lane grabs
-//     work items from a global atomic counter (dynamic load balance over the
-//     ragged context lengths), resolves block_tables and streams 128-token K
-//     and V tiles with cp.async.bulk.tensor (TMA, 128B swizzle, L2 evict_first)
-//     into a 3-stage shared-memory ring guarded by full/empty mbarriers. The
-//     item's query rows arrive in the same transaction as its first tile.
-//   * Warps 0-3 consume: each owns 32 tokens of every tile, computes
-//     S = Q K^T with mma.sync m16n8k16 (query heads on M, padded to 16),
-//     keeps a warp-private online softmax (exp2 domain), and accumulates
-//     O += P V with the probabilities re-packed from the S accumulators as the
-//     A operand. At the end of an item the four warp states are merged through
-//     shared memory in a fixed order (deterministic).
-//   * Split combine without a second launch: a multi-split item writes its
-//     unnormalised partial (O, m, l) to the workspace; the last split to arrive
-//     (per-(b,h) atomic counter, reset by that CTA) merges all partials and
-//     writes the bf16 output. The work counter is reset by the last CTA to
-//     finish, so the workspace stays zeroed between calls and inside graphs.
+//   * Persistent CTAs (one per SM), three warp roles:
+//       - warp 4, the producer: one lane grabs work items from a global atomic
+//         counter (dynamic load balance over the ragged context lengths),
+//         resolves block_tables and streams 128-token K and V tiles with
+//         cp.async.bulk.tensor (TMA, 128B swizzle, L2 evict_first, no
+//         multicast) into a 3-stage shared-memory ring guarded by full/empty
+//         mbarriers; the item's query rows ride in its first tile's transaction;
+//       - warps 0-3, the consumers: each owns 32 tokens of every tile,
+//         computes S = Q K^T with mma.sync m16n8k16 (query heads on M, padded
+//         to 16), keeps a warp-private online softmax (exp2 domain) and
+//         accumulates O += P V with P re-packed from the S accumulators. At
+//         the end of an item they only dump their raw (m, l, O) into a
+//         hand-off slot and go on with the next item;
+//       - warp 5, the merger: takes a slot, merges the four warp states in a
+//         fixed order (deterministic), and writes the bf16 output -- or, for
+//         a split row, the fp32 partial plus an acq_rel arrival on the row's
+//         counter; the last split to arrive merges all partials and writes
+//         the output, then resets the counter.
+//     The merge, the global writes and the cross-CTA hand-off therefore never
+//     stall the tensor-core warps or the TMA ring.
+//   * The work counter is reset by the last CTA to finish, so the workspace
+//     counters are back at zero after every call (graph-replay safe).
 //   * Tokens past context_lens in the last tile are masked in S (select, not
 //     arithmetic) and their V rows are zeroed in registers, so uninitialised
 //     cache memory (NaN patterns) never reaches the output.
@@ -39,7 +44,9 @@ namespace nkv {
 constexpr int kDecodeHeadDim = 128;
 constexpr int kDecodeTileTokens = 128;       // tokens per pipeline stage
 constexpr int kDecodeConsumerWarps = 4;
-constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
+constexpr int kDecodeProducerWarp = kDecodeConsumerWarps;
+constexpr int kDecodeMergerWarp = kDecodeConsumerWarps + 1;
+constexpr int kDecodeThreads = (kDecodeConsumerWarps + 2) * 32;
 constexpr int kHalfTileBytes = kDecodeTileTokens * 128;  // 128 rows x 64 dims x 2 B
 constexpr int kDecodeMetaInts = 8;
 
@@ -50,11 +57,15 @@ struct DecodeShape {
   static constexpr int kQRows = (G < 8) ? 8 : G;
   static constexpr int kQHalfBytes = ((kQRows * 128 + 1023) / 1024) * 1024;
   static constexpr int kStageBytes = 4 * kHalfTileBytes + 2 * kQHalfBytes;
-  static constexpr int kCoRowStride = kDecodeHeadDim + 8;  // floats, padded vs bank conflicts
-  static constexpr int kCombineBytes = kDecodeConsumerWarps * G * kCoRowStride * 4;
-  static constexpr int kSmemBytes =
-      kStages * kStageBytes + kCombineBytes + 2 * kDecodeConsumerWarps * G * 4 +
-      kStages * (16 + kDecodeMetaInts * 4) + 8 + 64 + 1024 /* alignment slack */;
+  // hand-off slots between consumers and merger
+  static constexpr int kSlots = (G <= 4) ? 2 : 1;
+  static constexpr int kORowStride = kDecodeHeadDim + 4;  // floats; 16-byte aligned rows
+  static constexpr int kSlotOFloats = kDecodeConsumerWarps * G * kORowStride;
+  static constexpr int kSlotMLFloats = 2 * kDecodeConsumerWarps * G;
+  static constexpr int kSlotBytes = (kSlotOFloats + kSlotMLFloats) * 4 + 16;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kSlots * kSlotBytes +
+                                    (2 * kStages + 2 * kSlots) * 8 +
+                                    kStages * kDecodeMetaInts * 4 + 16 + 1024 /* alignment */;
 };
 
 struct DecodeParams {
@@ -84,6 +95,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, float4 v) {
+  uint2 u;
+  u.x = pack_bf16x2(v.x, v.y);
+  u.y = pack_bf16x2(v.z, v.w);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -91,18 +109,25 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_q, const DecodeParams p) {
   using S = DecodeShape<G>;
   constexpr int kStages = S::kStages;
+  constexpr int kSlots = S::kSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stage_mem = smem;
-  float* co = reinterpret_cast<float*>(smem + kStages * S::kStageBytes);
-  float* cm = co + kDecodeConsumerWarps * G * S::kCoRowStride;
-  float* cl = cm + kDecodeConsumerWarps * G;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(cl + kDecodeConsumerWarps * G);
+  uint8_t* slot_mem = smem + kStages * S::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(slot_mem + kSlots * S::kSlotBytes);
   uint64_t* empty_bar = full_bar + kStages;
-  uint64_t* cons_bar = empty_bar + kStages;  // bounded barrier among the 128 consumer threads
-  int* meta = reinterpret_cast<int*>(cons_bar + 1);
-  volatile int* flags = meta + kStages * kDecodeMetaInts;  // [0] abort, [1] last-split
+  uint64_t* slot_full = empty_bar + kStages;   // 128 consumer arrivals
+  uint64_t* slot_empty = slot_full + kSlots;   // 1 merger arrival
+  int* meta = reinterpret_cast<int*>(slot_empty + kSlots);
+  volatile int* flags = meta + kStages * kDecodeMetaInts;  // [0] abort
+
+  auto slot_o = [&](int s) { return reinterpret_cast<float*>(slot_mem + s * S::kSlotBytes); };
+  auto slot_m = [&](int s) { return slot_o(s) + S::kSlotOFloats; };
+  auto slot_l = [&](int s) { return slot_m(s) + kDecodeConsumerWarps * G; };
+  auto slot_hdr = [&](int s) {
+    return reinterpret_cast<int*>(slot_l(s) + kDecodeConsumerWarps * G);  // [item, nsplit]
+  };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -112,12 +137,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), kDecodeConsumerWarps);
     }
-    mbar_init(smem_u32(cons_bar), kDecodeConsumerWarps * 32);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(smem_u32(&slot_full[s]), kDecodeConsumerWarps * 32);
+      mbar_init(smem_u32(&slot_empty[s]), 1);
+    }
     flags[0] = 0;
-    flags[1] = 0;
     fence_barrier_init();
   }
-  if (warp == kDecodeConsumerWarps && lane == 0) {
+  if (warp == kDecodeProducerWarp && lane == 0) {
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
     prefetch_tmap(&tm_q);
@@ -126,8 +153,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
 
   const int Hk = p.num_kv_heads;
   const int g = p.g;
+  const float NEG_INF = -INFINITY;
 
-  if (warp == kDecodeConsumerWarps) {
+  if (warp == kDecodeProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane != 0) return;
     const uint64_t pol_stream = l2_policy_evict_first();
@@ -141,6 +169,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     uint32_t armed[kStages];
 #pragma unroll
     for (int s = 0; s < kStages; ++s) armed[s] = 0;
+    // Items are grabbed one at a time, only when the ring has room for their
+    // first tile: claiming the next item early lets a busy CTA hold work an
+    // idle one could have taken, which lengthens the tail (measured slower).
     while (ok) {
       const int item = static_cast<int>(atomicAdd(&p.counters[0], 1u));
       if (item >= p.total_items) break;
@@ -228,34 +259,167 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     return;
   }
 
+  if (warp == kDecodeMergerWarp) {
+    // -------------------------------------------------------------- merger
+    int slot = 0;
+    uint32_t sphase = 0;
+    const int d0 = 4 * lane;  // this lane's 4 dims
+    while (true) {
+      if (!mbar_wait_bounded(smem_u32(&slot_full[slot]), sphase)) {
+        flags[0] = 1;
+        break;
+      }
+      const int* hdr = slot_hdr(slot);
+      const int item = hdr[0];
+      if (item < 0) break;
+      const int nsplit = hdr[1];
+      const int kvh = item % Hk;
+      const int rest = item / Hk;
+      const int b = rest % p.batch;
+      const int s = rest / p.batch;
+      const int pair = b * Hk + kvh;
+      const float* so = slot_o(slot);
+      const float* sm = slot_m(slot);
+      const float* sl = slot_l(slot);
+      for (int row = 0; row < g; ++row) {
+        float M = NEG_INF;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, sm[w * G + row]);
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+          const float mw = sm[w * G + row];
+          const float f = (mw == NEG_INF) ? 0.f : fast_exp2(mw - M);
+          L += sl[w * G + row] * f;
+          const float4 ow =
+              *reinterpret_cast<const float4*>(so + (w * G + row) * S::kORowStride + d0);
+          acc.x += ow.x * f;
+          acc.y += ow.y * f;
+          acc.z += ow.z * f;
+          acc.w += ow.w * f;
+        }
+        if (nsplit == 1) {
+          const float inv = (L > 0.f) ? 1.f / L : 0.f;
+          store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
+                           static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
+                       make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        } else {
+          const int64_t pidx = (static_cast<int64_t>(pair) * p.max_splits + s) * g + row;
+          *reinterpret_cast<float4*>(p.part_o + pidx * kDecodeHeadDim + d0) = acc;
+          if (lane == 0) {
+            p.part_ml[pidx * 2 + 0] = M;
+            p.part_ml[pidx * 2 + 1] = L;
+          }
+        }
+      }
+      // The slot's contents are consumed: hand it back before the global
+      // hand-off so the consumers never wait on the split protocol.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&slot_empty[slot]));
+      if (nsplit > 1) {
+        // __syncwarp orders the lanes' partial stores before lane 0's
+        // gpu-scope release; the acquire half of the same atomic makes the
+        // other splits' partials visible to the last arriver (and, through
+        // the next __syncwarp, to all its lanes).
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          const unsigned int prev = atomic_add_acq_rel_gpu(&p.split_counters[pair], 1u);
+          last = (prev == static_cast<unsigned int>(nsplit - 1)) ? 1 : 0;
+          if (last) atomicExch(&p.split_counters[pair], 0u);
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        __syncwarp();
+        if (last) {
+          for (int row = 0; row < g; ++row) {
+            const int64_t base = static_cast<int64_t>(pair) * p.max_splits * g + row;
+            float M = NEG_INF;
+            for (int s2 = 0; s2 < nsplit; ++s2)
+              M = fmaxf(M, __ldcg(p.part_ml + (base + static_cast<int64_t>(s2) * g) * 2));
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s2 = 0; s2 < nsplit; ++s2) {
+              const int64_t pi = base + static_cast<int64_t>(s2) * g;
+              const float ms = __ldcg(p.part_ml + pi * 2);
+              const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
+              L += __ldcg(p.part_ml + pi * 2 + 1) * f;
+              const float4 po = __ldcg(reinterpret_cast<const float4*>(p.part_o + pi * kDecodeHeadDim + d0));
+              acc.x += po.x * f;
+              acc.y += po.y * f;
+              acc.z += po.z * f;
+              acc.w += po.w * f;
+            }
+            const float inv = (L > 0.f) ? 1.f / L : 0.f;
+            store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
+                             static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
+                         make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+          }
+        }
+      }
+      if (++slot == kSlots) {
+        slot = 0;
+        sphase ^= 1u;
+      }
+    }
+    return;
+  }
+
   // -------------------------------------------------------------- consumers
   const int cw = warp;
   const int gid = lane >> 2;
   const int tig = lane & 3;
-  const int ctid = threadIdx.x;  // 0..127
   const float scale_log2 = p.scale_log2;
-  const float NEG_INF = -INFINITY;
-
-  // Bounded barrier over the 128 consumer threads (an mbarrier with 128
-  // arrivals per phase): unlike bar.sync it cannot hang if a warp aborted.
-  uint32_t cons_phase = 0;
-  bool alive = true;
-  auto consumer_sync = [&]() {
-    mbar_arrive(smem_u32(cons_bar));
-    if (!mbar_wait_bounded(smem_u32(cons_bar), cons_phase)) {
-      flags[0] = 1;
-      alive = false;
-    }
-    cons_phase ^= 1u;
-  };
 
   float o[16][4];
   float m_run[2], l_run[2];
   uint32_t qa[8][4];
-  int cur_b = 0, cur_kvh = 0, cur_s = 0;
 
   int stage = 0;
   uint32_t phase = 0;
+  int cslot = 0;
+  uint32_t cphase = 0;
+  // Hands the warp states of one item (or the end marker, item < 0) to the
+  // merger through the next slot.
+  auto handoff = [&](int item, int nsplit) -> bool {
+    if (!mbar_wait_bounded(smem_u32(&slot_empty[cslot]), cphase ^ 1u)) {
+      flags[0] = 1;
+      return false;
+    }
+    if (item >= 0) {
+      constexpr int kRowSets = (G == 16) ? 2 : 1;
+      float* so = slot_o(cslot);
+#pragma unroll
+      for (int rs = 0; rs < kRowSets; ++rs) {
+        float l = l_run[rs];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        const int row = gid + 8 * rs;
+        if (row < g) {
+          if (tig == 0) {
+            slot_m(cslot)[cw * G + row] = m_run[rs];
+            slot_l(cslot)[cw * G + row] = l;
+          }
+          float* dst = so + (cw * G + row) * S::kORowStride;
+#pragma unroll
+          for (int n = 0; n < 16; ++n)
+            *reinterpret_cast<float2*>(dst + 8 * n + 2 * tig) =
+                make_float2(o[n][2 * rs], o[n][2 * rs + 1]);
+        }
+      }
+    }
+    if (threadIdx.x == 0) {
+      slot_hdr(cslot)[0] = item;
+      slot_hdr(cslot)[1] = nsplit;
+    }
+    mbar_arrive(smem_u32(&slot_full[cslot]));
+    if (++cslot == kSlots) {
+      cslot = 0;
+      cphase ^= 1u;
+    }
+    return true;
+  };
+
   while (true) {
     if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), phase)) {
       flags[0] = 1;
@@ -263,7 +427,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     }
     const int* m = meta + stage * kDecodeMetaInts;
     const int item = m[0];
-    if (item < 0) break;
+    if (item < 0) {
+      handoff(-1, 0);  // end marker for the merger
+      break;
+    }
     const int j = m[1];
     const int ntiles = m[2];
     const int nvalid = m[3];
@@ -271,10 +438,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     const uint8_t* sbase = stage_mem + stage * S::kStageBytes;
 
     if (j == 0) {
-      cur_kvh = item % Hk;
-      const int rest = item / Hk;
-      cur_b = rest % p.batch;
-      cur_s = rest / p.batch;
 #pragma unroll
       for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
       m_run[0] = m_run[1] = NEG_INF;
@@ -408,106 +571,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     }
 
     if (j + 1 < ntiles) continue;
-
-    // ---------------------------------------------------- item epilogue
-    constexpr int kRowSets = (G == 16) ? 2 : 1;
-#pragma unroll
-    for (int rs = 0; rs < kRowSets; ++rs) {
-      float l = l_run[rs];
-      l += __shfl_xor_sync(0xffffffffu, l, 1);
-      l += __shfl_xor_sync(0xffffffffu, l, 2);
-      l_run[rs] = l;
-      const int row = gid + 8 * rs;
-      if (tig == 0 && row < g) {
-        cm[cw * G + row] = m_run[rs];
-        cl[cw * G + row] = l;
-      }
-    }
-    consumer_sync();
-    if (!alive) break;
-#pragma unroll
-    for (int rs = 0; rs < kRowSets; ++rs) {
-      const int row = gid + 8 * rs;
-      if (row < g) {
-        float M = NEG_INF;
-#pragma unroll
-        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, cm[w * G + row]);
-        const float f = (m_run[rs] == NEG_INF) ? 0.f : fast_exp2(m_run[rs] - M);
-        float* dst = co + (cw * G + row) * S::kCoRowStride;
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          *reinterpret_cast<float2*>(dst + 8 * n + 2 * tig) =
-              make_float2(o[n][2 * rs] * f, o[n][2 * rs + 1] * f);
-        }
-      }
-    }
-    consumer_sync();
-    if (!alive) break;
-
-    const int pair = cur_b * Hk + cur_kvh;
-    for (int row = 0; row < g; ++row) {
-      float M = NEG_INF;
-#pragma unroll
-      for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, cm[w * G + row]);
-      float L = 0.f, acc = 0.f;
-#pragma unroll
-      for (int w = 0; w < kDecodeConsumerWarps; ++w) {
-        const float mw = cm[w * G + row];
-        const float f = (mw == NEG_INF) ? 0.f : fast_exp2(mw - M);
-        L += cl[w * G + row] * f;
-        acc += co[(w * G + row) * S::kCoRowStride + ctid];
-      }
-      if (nsplit == 1) {
-        const float v = (L > 0.f) ? acc / L : 0.f;
-        p.out[static_cast<int64_t>(cur_b) * p.out_stride_token +
-              static_cast<int64_t>(cur_kvh * g + row) * kDecodeHeadDim + ctid] =
-            __float2bfloat16_rn(v);
-      } else {
-        const int64_t pidx = (static_cast<int64_t>(pair) * p.max_splits + cur_s) * g + row;
-        p.part_o[pidx * kDecodeHeadDim + ctid] = acc;
-        if (ctid == 0) {
-          p.part_ml[pidx * 2 + 0] = M;
-          p.part_ml[pidx * 2 + 1] = L;
-        }
-      }
-    }
-    if (nsplit > 1) {
-      // Hand-off between the CTAs of a row: the CTA barrier orders every
-      // thread's partial stores before thread 0's gpu-scope release; the
-      // acquire half of the same atomic makes the other splits' partials
-      // visible to the last arriver, and the next barrier to its threads.
-      consumer_sync();
-      if (!alive) break;
-      if (ctid == 0) {
-        const unsigned int prev = atomic_add_acq_rel_gpu(&p.split_counters[pair], 1u);
-        const int last = (prev == static_cast<unsigned int>(nsplit - 1)) ? 1 : 0;
-        if (last) atomicExch(&p.split_counters[pair], 0u);
-        flags[1] = last;
-      }
-      consumer_sync();
-      if (!alive) break;
-      if (flags[1]) {
-        for (int row = 0; row < g; ++row) {
-          const int64_t base = static_cast<int64_t>(pair) * p.max_splits * g + row;
-          float M = NEG_INF;
-          for (int s2 = 0; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(p.part_ml + (base + s2 * g) * 2));
-          float L = 0.f, acc = 0.f;
-          for (int s2 = 0; s2 < nsplit; ++s2) {
-            const int64_t pi = base + static_cast<int64_t>(s2) * g;
-            const float ms = __ldcg(p.part_ml + pi * 2);
-            const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
-            L += __ldcg(p.part_ml + pi * 2 + 1) * f;
-            acc += __ldcg(p.part_o + pi * kDecodeHeadDim + ctid) * f;
-          }
-          const float v = (L > 0.f) ? acc / L : 0.f;
-          p.out[static_cast<int64_t>(cur_b) * p.out_stride_token +
-                static_cast<int64_t>(cur_kvh * g + row) * kDecodeHeadDim + ctid] =
-              __float2bfloat16_rn(v);
-        }
-      }
-    }
-    consumer_sync();
-    if (!alive) break;
+    if (!handoff(item, nsplit)) break;
   }
   // Consumers leave only after the producer's end marker (or an abort), so
   // every TMA transaction they waited on has completed.
