@@ -102,6 +102,10 @@ constexpr int kMaxDecodePairs = 1 << 16;
 #ifndef NKV_DECODE_MAX_SPLIT_TOKENS
 #define NKV_DECODE_MAX_SPLIT_TOKENS 4096
 #endif
+// Work items aimed for per SM (of a 148-SM part) when every row is full.
+#ifndef NKV_DECODE_TARGET_ITEMS_PER_SM
+#define NKV_DECODE_TARGET_ITEMS_PER_SM 7
+#endif
 
 // Split size depends only on the shapes (not on the device or the lengths), so
 // the workspace query and the launch always agree.
@@ -109,13 +113,13 @@ DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block
   DecodePlan pl{};
   pl.g = hq / hk;
   pl.pairs = batch * hk;
-  // Splits as long as possible (every item ends in a cross-warp merge and,
-  // when split, a cross-CTA combine; at 1 KiB-token splits that costs ~13 %
-  // of the bandwidth on B200) while still giving ~2 items per SM of a
-  // 148-SM part when every row is full, so the dynamic scheduler can balance
-  // ragged lengths: 1 block .. NKV_DECODE_MAX_SPLIT_TOKENS.
+  // Long splits amortise each item's fixed costs (grab, first-tile latency,
+  // merge); short ones let the dynamic scheduler balance ragged lengths and
+  // shrink the tail. Measured on B200: 4 K-token splits are best for a full
+  // TP1 launch, ~2 K for the small launches of a TP8 shard; aiming at ~7
+  // items per SM when every row is full gives both. 1 block .. the maximum.
   const int64_t block_units = static_cast<int64_t>(pl.pairs) * std::max(max_blocks, 1);
-  const int64_t target_items = 2 * 148;
+  const int64_t target_items = NKV_DECODE_TARGET_ITEMS_PER_SM * 148;
   int cb = static_cast<int>(block_units / target_items);
   const int max_cb = std::max(1, NKV_DECODE_MAX_SPLIT_TOKENS / block_size);
   pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
@@ -151,8 +155,17 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMa
     attr_set[dev] = true;
   }
   const int grid = std::max(1, std::min(sm_count(dev), p.total_items));
-  nkv::paged_decode_kernel<G><<<grid, nkv::kDecodeThreads, S::kSmemBytes, stream>>>(tk, tv, tq, p);
-  return launch_status();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(nkv::kDecodeThreads, 1, 1);
+  cfg.dynamicSmemBytes = S::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::paged_decode_kernel<G>, tk, tv, tq, p));
 }
 
 int padded_group(int g) {

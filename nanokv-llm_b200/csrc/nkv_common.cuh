@@ -152,6 +152,18 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while its predecessor runs; grid_dependency_wait()
+// blocks until the predecessor has completed and its writes are visible, and
+// allow_dependent_launch() lets the next kernel in the stream start early.
+// Both are no-ops when no such dependency exists.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier over `count` threads (id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -150,6 +150,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     prefetch_tmap(&tm_q);
   }
   __syncthreads();
+  // Launched with programmatic stream serialisation: everything above
+  // overlapped the previous kernel (typically the slot write of this layer);
+  // from here on its writes to the cache are visible.
+  grid_dependency_wait();
 
   const int Hk = p.num_kv_heads;
   const int g = p.g;

@@ -19,6 +19,9 @@ store_kvcache_kernel(const uint4* __restrict__ key, int64_t key_stride_vec,
                      uint4* __restrict__ k_cache, uint4* __restrict__ v_cache, int64_t num_slots,
                      const int32_t* __restrict__ slot_mapping, int32_t num_tokens,
                      int32_t row_vecs) {
+  // The decode kernel that follows in the stream may be launched now; it
+  // waits for this grid's completion before it reads the cache.
+  allow_dependent_launch();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int token = blockIdx.x * kStoreWarpsPerBlock + warp;
