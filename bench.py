@@ -147,15 +147,17 @@ def build_state(rank: int, world: int, dev: torch.device):
                 kv=kv, resident=resident, layer_bytes=layer_bytes)
 
 
-def algorithmic_decode_bytes(lens, hk, hq) -> int:
-    """Bytes one decode launch must move: every live K and V row of the kv
-    heads once, q in and o out, the block-table entries it follows and the
-    context lengths."""
+def algorithmic_decode_bytes(lens, hk, hq, with_store: bool = True) -> int:
+    """Bytes one decode-step launch must move: every live K and V row of the
+    kv heads once, q in and o out, the block-table entries it follows and the
+    context lengths -- plus, for the fused step, the new K/V rows read and
+    written into the cache and the slot indices."""
     b = len(lens)
     kv = sum(lens) * hk * D * 2 * 2
     qo = b * hq * D * 2 * 2
     tables = sum((L + BLOCK - 1) // BLOCK for L in lens) * 4 + b * 4
-    return kv + qo + tables
+    store = b * (hk * D * 2 * 2 * 2 + 4) if with_store else 0
+    return kv + qo + tables + store
 
 
 def run_gpu(args, rank, world, dev):
@@ -186,17 +188,18 @@ def run_gpu(args, rank, world, dev):
         for layer in range(LAYERS):
             c = layer % R
             q, k, v = layer_views(layer, src)
-            ops.store_kvcache(k, v, kv[0, c], kv[1, c], sm)
-            # the decode launches of every 6th layer are bracketed by events
-            # (the roofline's per-launch time); fewer events keep their own
-            # cost out of the step time
-            record = record and layer % 6 == 0
-            if record:
+            # the launches of every 6th layer are bracketed by events (the
+            # roofline's per-launch time); fewer events keep their own cost
+            # out of the step time
+            rec = record and layer % 6 == 0
+            if rec:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record()
-            ops.paged_decode(q, kv[0, c], kv[1, c], bt, cl, scale, out=out[layer], workspace=ws)
-            if record:
+            # one launch: slot write of the new K/V rows + paged decode
+            ops.decode_step(q, k, v, kv[0, c], kv[1, c], sm, bt, cl, scale, out=out[layer],
+                            workspace=ws)
+            if rec:
                 e1.record()
                 dec_events.append((e0, e1))
 
@@ -374,12 +377,13 @@ def measure_kvchat(dev, world):
     ws = ops.decode_workspace(dev, 1, hq, hk, D, nb, BLOCK)
 
     def step():
+        # one launch per layer: slot write + query-window append + decode
         for layer in range(L):
             q, k, v = qkv[layer].split([hq * D, hk * D, hk * D], dim=-1)
             q, k, v = q.view(1, hq, D), k.view(1, hk, D), v.view(1, hk, D)
-            ops.store_kvcache(k, v, kc[layer], vc[layer], sm)
-            ops.query_window_append(q, ring, layer, zero, zero, zero)
-            ops.paged_decode(q, kc[layer], vc[layer], bt, cl, D ** -0.5, out=out[layer], workspace=ws)
+            ops.decode_step(q, k, v, kc[layer], vc[layer], sm, bt, cl, D ** -0.5,
+                            out=out[layer], ring=ring, layer_id=layer, ring_slot_of_row=zero,
+                            ring_pos_of_row=zero, workspace=ws)
 
     step()
     torch.cuda.synchronize(dev)
@@ -446,8 +450,7 @@ def measure_config4(dev, world):
 
     def layer(i):
         kc, vc = caches[i % 2]
-        ops.store_kvcache(k, v, kc, vc, sm)
-        ops.paged_decode(q, kc, vc, bt, cl, D ** -0.5, out=out, workspace=ws)
+        ops.decode_step(q, k, v, kc, vc, sm, bt, cl, D ** -0.5, out=out, workspace=ws)
 
     for i in range(4):
         layer(i)
@@ -557,8 +560,9 @@ def read_traffic_bytes_per_launch(world: int):
 
 def run_profile_case(kind: str) -> None:
     """Small, self-contained launches for ncu captures (a few GB on the
-    device, inputs larger than L2): `decode` runs store + paged decode on one
-    layer of the first 64 config-2 sequences (Qwen3-8B shapes) 4 times;
+    device, inputs larger than L2): `decode` runs the fused decode step (slot
+    write + paged decode) on one layer of the first 64 config-2 sequences
+    (Qwen3-8B shapes) 4 times;
     `compress` runs one config-3 window-compression event 4 times."""
     from nanokv_b200 import ops
 
@@ -587,8 +591,8 @@ def run_profile_case(kind: str) -> None:
     qkv = torch.randn(64, (HQ + 2 * HK) * D, device=dev).to(torch.bfloat16)
     q, k, v = qkv.split([HQ * D, HK * D, HK * D], dim=-1)
     for _ in range(4):
-        ops.store_kvcache(k.view(64, HK, D), v.view(64, HK, D), kc, vc, sm)
-        ops.paged_decode(q.view(64, HQ, D), kc, vc, bt, cl, D ** -0.5)
+        ops.decode_step(q.view(64, HQ, D), k.view(64, HK, D), v.view(64, HK, D), kc, vc, sm, bt,
+                        cl, D ** -0.5)
     torch.cuda.synchronize()
     print(json.dumps({"profile": kind, "kv_tokens": sum(lens),
                       "alg_bytes": algorithmic_decode_bytes(lens, HK, HQ)}))
@@ -651,14 +655,15 @@ def main():
                     "path": "nanokv_b200.layers.attention.Attention.forward per layer; every "
                             "step copies all layers' q/k/v from pinned host memory (copy stream, "
                             "overlapped with compute) and copies every output back"},
-            "roofline": {"kernel": "nkv paged_decode_kernel", "bound": "hbm",
+            "roofline": {"kernel": "nkv paged_decode_kernel (fused decode step: slot write + "
+                                   "paged decode)", "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} hbm_gbs",
                          "traffic": traffic, "alg_bytes_per_launch": r["alg_bytes"],
                          "avg_launch_us": round(r["dec_avg_ms"] * 1e3, 2)},
             "cpu_baseline": cpu,
             "clocks": r["clocks"],
-            "gpu_launches": args.steps * LAYERS * 2,
+            "gpu_launches": args.steps * LAYERS,
             "compress": r["compress"],
             **r["extra"],
         }

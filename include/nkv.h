@@ -114,6 +114,39 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* 2b. Fused decode step: slot write + optional query-window append + decode */
+/* Replaces, in one launch, the decode-step sequence of                      */
+/*   nanokvllm/layers/attention.py:72-73 (store_kvcache) and :104-107        */
+/*   (flash_attn_with_kvcache), and for KvChat also the query-window append  */
+/*   of KvChat/layers/attention.py:80-87.                                    */
+/* Same result as nkv_store_kvcache(key, value, slot_mapping) [then          */
+/* nkv_query_window_append] then nkv_paged_decode, for a decode step: one   */
+/* new token per batch row, whose slot_mapping[b] is -1 or the slot of       */
+/* position context_lens[b]-1 (how the reference's decode step builds it,    */
+/* nanokvllm/engine/model_runner.py:194 and :279). Rows violating that are   */
+/* not written and flag NKV_DEVERR_STORE_SLOT. The producer warp writes each */
+/* kv head's new row just before the TMA that reads that tile, so no second  */
+/* launch or cross-CTA ordering is needed.                                   */
+/* ring may be NULL (no query window). Otherwise it is the KvChat ring       */
+/* [num_ring_slots, num_layers, window_size, num_q_heads, head_dim]; row b   */
+/* appends q[b] to ring[ring_slot_of_row[b], layer_id, ring_pos_of_row[b]]   */
+/* when ring_slot_of_row[b] >= 0; q heads must then be contiguous            */
+/* (q_stride_head == head_dim).                                              */
+int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                    const void* key, int64_t key_stride, const void* value, int64_t value_stride,
+                    const int32_t* slot_mapping,
+                    void* k_cache, void* v_cache, int64_t num_blocks,
+                    const int32_t* block_tables, int32_t max_blocks,
+                    const int32_t* context_lens,
+                    void* ring, int32_t num_ring_slots, int32_t num_layers,
+                    int32_t window_size, int32_t layer_id,
+                    const int32_t* ring_slot_of_row, const int32_t* ring_pos_of_row,
+                    void* out, int64_t out_stride_token,
+                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t block_size, float softmax_scale,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* 3a. Periodic window compression (one layer, all selected sequences)       */
 /* Replaces: MyCompressCompact, nanokvllm/layers/compress_utils.py:100-263,  */
 /*   with get_tail_window_and_tail_slots (:9-72), gather_kv_by_slots (:75-97) */

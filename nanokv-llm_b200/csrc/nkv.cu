@@ -292,12 +292,30 @@ size_t nkv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32
   return make_decode_plan(batch, num_q_heads, num_kv_heads, max_blocks, block_size).total;
 }
 
-int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
-                     const void* k_cache, const void* v_cache, int64_t num_blocks,
-                     const int32_t* block_tables, int32_t max_blocks, const int32_t* context_lens,
-                     void* out, int64_t out_stride_token, int32_t batch, int32_t num_q_heads,
-                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
-                     float softmax_scale, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The new-row and query-window inputs of a fused decode step.
+struct FusedStep {
+  const void* key = nullptr;
+  int64_t key_stride = 0;
+  const void* value = nullptr;
+  int64_t value_stride = 0;
+  const int32_t* slot_mapping = nullptr;
+  void* ring = nullptr;
+  int32_t num_ring_slots = 0, num_layers = 0, window_size = 0, layer_id = 0;
+  const int32_t* ring_slot_of_row = nullptr;
+  const int32_t* ring_pos_of_row = nullptr;
+};
+
+int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                      const void* k_cache, const void* v_cache, int64_t num_blocks,
+                      const int32_t* block_tables, int32_t max_blocks, const int32_t* context_lens,
+                      void* out, int64_t out_stride_token, int32_t batch, int32_t num_q_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                      float softmax_scale, void* workspace, size_t workspace_bytes, void* stream,
+                      const FusedStep* fused) {
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_blocks < 0 || num_blocks < 0)
     return NKV_ERR_INVALID_ARGUMENT;
   if (batch == 0) return NKV_OK;
@@ -354,6 +372,40 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
   p.chunk_tokens = pl.chunk_tokens;
   p.max_splits = pl.max_splits;
   p.total_items = pl.pairs * pl.max_splits;
+  if (fused != nullptr) {
+    const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+    if (!fused->key || !fused->value || !fused->slot_mapping) return NKV_ERR_INVALID_ARGUMENT;
+    if (!aligned16(fused->key) || !aligned16(fused->value) || (fused->key_stride % 8) ||
+        (fused->value_stride % 8))
+      return NKV_ERR_ALIGNMENT;
+    if (fused->key_stride < row || fused->value_stride < row) return NKV_ERR_INVALID_ARGUMENT;
+    p.new_k = static_cast<const uint4*>(fused->key);
+    p.new_v = static_cast<const uint4*>(fused->value);
+    p.new_k_stride_vec = fused->key_stride / 8;
+    p.new_v_stride_vec = fused->value_stride / 8;
+    p.slot_mapping = fused->slot_mapping;
+    p.k_cache_vec = static_cast<uint4*>(const_cast<void*>(k_cache));
+    p.v_cache_vec = static_cast<uint4*>(const_cast<void*>(v_cache));
+    if (fused->ring != nullptr) {
+      if (!fused->ring_slot_of_row || !fused->ring_pos_of_row || fused->num_ring_slots <= 0 ||
+          fused->num_layers <= 0 || fused->window_size <= 0 || fused->layer_id < 0 ||
+          fused->layer_id >= fused->num_layers)
+        return NKV_ERR_INVALID_ARGUMENT;
+      if (q_stride_head != head_dim || !aligned16(fused->ring)) return NKV_ERR_ALIGNMENT;
+      const int64_t per_pos = static_cast<int64_t>(num_q_heads) * head_dim / 8;
+      p.q_vec = static_cast<const uint4*>(q);
+      p.q_stride_token_vec = q_stride_token / 8;
+      p.ring_vec = static_cast<uint4*>(fused->ring);
+      p.ring_slot_of_row = fused->ring_slot_of_row;
+      p.ring_pos_of_row = fused->ring_pos_of_row;
+      p.ring_window = fused->window_size;
+      p.ring_slots = fused->num_ring_slots;
+      p.num_q_heads = num_q_heads;
+      p.ring_layer_base_vec = static_cast<int64_t>(fused->layer_id) * fused->window_size * per_pos;
+      p.ring_slot_stride_vec =
+          static_cast<int64_t>(fused->num_layers) * fused->window_size * per_pos;
+    }
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (G) {
     case 1: return launch_decode<1>(tk, tv, tq, p, s);
@@ -362,6 +414,51 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
     case 8: return launch_decode<8>(tk, tv, tq, p, s);
     default: return launch_decode<16>(tk, tv, tq, p, s);
   }
+}
+
+}  // namespace
+
+extern "C" {
+
+int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks,
+                     const int32_t* block_tables, int32_t max_blocks, const int32_t* context_lens,
+                     void* out, int64_t out_stride_token, int32_t batch, int32_t num_q_heads,
+                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                     float softmax_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  return paged_decode_impl(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks,
+                           block_tables, max_blocks, context_lens, out, out_stride_token, batch,
+                           num_q_heads, num_kv_heads, head_dim, block_size, softmax_scale,
+                           workspace, workspace_bytes, stream, nullptr);
+}
+
+int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* key,
+                    int64_t key_stride, const void* value, int64_t value_stride,
+                    const int32_t* slot_mapping, void* k_cache, void* v_cache, int64_t num_blocks,
+                    const int32_t* block_tables, int32_t max_blocks, const int32_t* context_lens,
+                    void* ring, int32_t num_ring_slots, int32_t num_layers, int32_t window_size,
+                    int32_t layer_id, const int32_t* ring_slot_of_row,
+                    const int32_t* ring_pos_of_row, void* out, int64_t out_stride_token,
+                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                    int32_t block_size, float softmax_scale, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  FusedStep f;
+  f.key = key;
+  f.key_stride = key_stride;
+  f.value = value;
+  f.value_stride = value_stride;
+  f.slot_mapping = slot_mapping;
+  f.ring = ring;
+  f.num_ring_slots = num_ring_slots;
+  f.num_layers = num_layers;
+  f.window_size = window_size;
+  f.layer_id = layer_id;
+  f.ring_slot_of_row = ring_slot_of_row;
+  f.ring_pos_of_row = ring_pos_of_row;
+  return paged_decode_impl(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks,
+                           block_tables, max_blocks, context_lens, out, out_stride_token, batch,
+                           num_q_heads, num_kv_heads, head_dim, block_size, softmax_scale,
+                           workspace, workspace_bytes, stream, &f);
 }
 
 // ------------------------------------------------------------------ window compress

@@ -87,6 +87,26 @@ struct DecodeParams {
   int chunk_tokens;
   int max_splits;
   int total_items;
+  // Fused decode step (optional, null when unused): the step's new K/V rows,
+  // written by the producer warp right before the TMA that reads them, and
+  // the KvChat query-window ring append.
+  const uint4* new_k;           // [batch] rows of num_kv_heads*128 bf16
+  const uint4* new_v;
+  int64_t new_k_stride_vec;     // row strides in 16-byte units
+  int64_t new_v_stride_vec;
+  const int32_t* slot_mapping;  // [batch]
+  uint4* k_cache_vec;           // the caches as 16-byte units (for the write)
+  uint4* v_cache_vec;
+  const uint4* q_vec;           // q rows for the ring append
+  int64_t q_stride_token_vec;
+  uint4* ring_vec;              // [slots, layers, W, Hq, 128] bf16, or null
+  const int32_t* ring_slot_of_row;  // [batch], -1 = row not in a query window
+  const int32_t* ring_pos_of_row;   // [batch]
+  int64_t ring_layer_base_vec;      // offset of ring[0, layer_id] in 16-byte units
+  int64_t ring_slot_stride_vec;     // ring[s] -> ring[s + 1]
+  int ring_slots;
+  int ring_window;
+  int num_q_heads;
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -161,10 +181,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
 
   if (warp == kDecodeProducerWarp) {
     // ------------------------------------------------------------ producer
-    if (lane != 0) return;
+    // The whole warp walks the loop; lane 0 grabs items and issues the TMA,
+    // all lanes share the fused step's row copies.
+    const bool leader = lane == 0;
     const uint64_t pol_stream = l2_policy_evict_first();
     const uint64_t pol_q = l2_policy_evict_last();
     const uint32_t q_bytes = static_cast<uint32_t>(2 * g * 128);
+    const int row_vecs = Hk * (kDecodeHeadDim / 8);  // 16-byte units of one cache row
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -177,7 +200,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     // first tile: claiming the next item early lets a busy CTA hold work an
     // idle one could have taken, which lengthens the tail (measured slower).
     while (ok) {
-      const int item = static_cast<int>(atomicAdd(&p.counters[0], 1u));
+      int item = 0;
+      if (leader) item = static_cast<int>(atomicAdd(&p.counters[0], 1u));
+      item = __shfl_sync(0xffffffffu, item, 0);
       if (item >= p.total_items) break;
       const int kvh = item % Hk;
       const int rest = item / Hk;
@@ -189,47 +214,96 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       const int t0 = s * p.chunk_tokens;
       const int t1 = min(t0 + p.chunk_tokens, len);
       const int ntiles = len > 0 ? (t1 - t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
+      // KvChat: this step's query rows of the group join the row's window.
+      if (p.ring_vec != nullptr && s == 0) {
+        const int rs = __ldg(p.ring_slot_of_row + b);
+        if (rs >= 0) {
+          const int pos = __ldg(p.ring_pos_of_row + b);
+          if (rs < p.ring_slots && pos >= 0 && pos < p.ring_window) {
+            const int n = g * (kDecodeHeadDim / 8);  // the group's q rows, 16-byte units
+            const uint4* src = p.q_vec + static_cast<int64_t>(b) * p.q_stride_token_vec +
+                               static_cast<int64_t>(kvh) * n;
+            uint4* dst = p.ring_vec + p.ring_layer_base_vec + rs * p.ring_slot_stride_vec +
+                         static_cast<int64_t>(pos) * p.num_q_heads * (kDecodeHeadDim / 8) +
+                         static_cast<int64_t>(kvh) * n;
+            for (int i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
+          } else if (leader) {
+            raise_error(NKV_DEVERR_RING_RANGE);
+          }
+        }
+      }
       int j = 0;
       do {
-        if (flags[0] || !mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) {
+        bool waited = true;
+        if (leader) {
+          waited = !flags[0] && mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u);
+          if (!waited) flags[0] = 1;
+        }
+        if (!__shfl_sync(0xffffffffu, waited ? 1 : 0, 0)) {
           ok = false;
-          flags[0] = 1;
           break;
         }
         armed[stage] = 0;
-        int* m = meta + stage * kDecodeMetaInts;
         const int tok = t0 + j * kDecodeTileTokens;
-        m[0] = item;
-        m[1] = j;
-        m[2] = ntiles;
-        m[3] = ntiles > 0 ? min(kDecodeTileTokens, t1 - tok) : 0;
-        m[4] = nsplit;
+        if (leader) {
+          int* m = meta + stage * kDecodeMetaInts;
+          m[0] = item;
+          m[1] = j;
+          m[2] = ntiles;
+          m[3] = ntiles > 0 ? min(kDecodeTileTokens, t1 - tok) : 0;
+          m[4] = nsplit;
+        }
         const uint32_t fb = smem_u32(&full_bar[stage]);
         if (ntiles == 0) {
-          mbar_arrive(fb);
+          if (leader) mbar_arrive(fb);
         } else {
-          int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
-                          tok / p.block_size);
-          int slot;
-          if (blk < 0 || static_cast<int64_t>(blk) >= p.num_blocks) {
-            raise_error(NKV_DEVERR_DECODE_BLOCK);
-            slot = -2 * kDecodeTileTokens;  // fully out of range: TMA fills zeros
-          } else {
-            slot = blk * p.block_size + (tok % p.block_size);
+          const int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
+                                tok / p.block_size);
+          const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
+          // fully out of range: TMA fills zeros
+          const int slot = blk_ok ? blk * p.block_size + (tok % p.block_size) : -2 * kDecodeTileTokens;
+          if (!blk_ok && leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
+          // Fused slot write: the current token (position len - 1) lives in
+          // this sequence's last tile; its K/V head slice is written here,
+          // made visible to the async proxy, then the tile is loaded.
+          if (p.new_k != nullptr && s == nsplit - 1 && j == ntiles - 1) {
+            const int32_t sm = __ldg(p.slot_mapping + b);
+            const int64_t want = blk_ok ? static_cast<int64_t>(blk) * p.block_size +
+                                              (len - 1) % p.block_size
+                                        : -1;
+            if (sm >= 0 && sm == want) {
+              // a 128-dim head row is 16 x 16 B: lanes 0-15 copy K, 16-31 V
+              constexpr int kHeadVecs = kDecodeHeadDim / 8;
+              const int u = lane & (kHeadVecs - 1);
+              const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + u;
+              if (lane < kHeadVecs) {
+                p.k_cache_vec[static_cast<int64_t>(sm) * row_vecs + col] =
+                    __ldg(p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col);
+              } else {
+                p.v_cache_vec[static_cast<int64_t>(sm) * row_vecs + col] =
+                    __ldg(p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
+              }
+              fence_proxy_async_global();
+            } else if (sm != -1 && leader) {
+              raise_error(NKV_DEVERR_STORE_SLOT);
+            }
+            __syncwarp();
           }
-          const uint32_t bytes = 4u * kHalfTileBytes + (j == 0 ? q_bytes : 0u);
-          mbar_arrive_expect_tx(fb, bytes);
+          if (leader) {
+            const uint32_t bytes = 4u * kHalfTileBytes + (j == 0 ? q_bytes : 0u);
+            mbar_arrive_expect_tx(fb, bytes);
+            const uint32_t base = smem_u32(stage_mem + stage * S::kStageBytes);
+            tma_load_3d(base + 0 * kHalfTileBytes, &tm_k, fb, 0, kvh, slot, pol_stream);
+            tma_load_3d(base + 1 * kHalfTileBytes, &tm_k, fb, 64, kvh, slot, pol_stream);
+            tma_load_3d(base + 2 * kHalfTileBytes, &tm_v, fb, 0, kvh, slot, pol_stream);
+            tma_load_3d(base + 3 * kHalfTileBytes, &tm_v, fb, 64, kvh, slot, pol_stream);
+            if (j == 0) {
+              const uint32_t qb = base + 4 * kHalfTileBytes;
+              tma_load_3d(qb, &tm_q, fb, 0, kvh * g, b, pol_q);
+              tma_load_3d(qb + S::kQHalfBytes, &tm_q, fb, 64, kvh * g, b, pol_q);
+            }
+          }
           armed[stage] = phase + 1u;
-          const uint32_t base = smem_u32(stage_mem + stage * S::kStageBytes);
-          tma_load_3d(base + 0 * kHalfTileBytes, &tm_k, fb, 0, kvh, slot, pol_stream);
-          tma_load_3d(base + 1 * kHalfTileBytes, &tm_k, fb, 64, kvh, slot, pol_stream);
-          tma_load_3d(base + 2 * kHalfTileBytes, &tm_v, fb, 0, kvh, slot, pol_stream);
-          tma_load_3d(base + 3 * kHalfTileBytes, &tm_v, fb, 64, kvh, slot, pol_stream);
-          if (j == 0) {
-            const uint32_t qb = base + 4 * kHalfTileBytes;
-            tma_load_3d(qb, &tm_q, fb, 0, kvh * g, b, pol_q);
-            tma_load_3d(qb + S::kQHalfBytes, &tm_q, fb, 64, kvh * g, b, pol_q);
-          }
         }
         if (++stage == kStages) {
           stage = 0;
@@ -237,28 +311,30 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         }
       } while (++j < ntiles);
     }
-    if (ok) {
-      // End-of-work marker for the consumers.
-      if (mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) {
-        armed[stage] = 0;  // released: its last transaction has completed
-        meta[stage * kDecodeMetaInts + 0] = -1;
-        mbar_arrive(smem_u32(&full_bar[stage]));
-      } else {
-        flags[0] = 1;
+    if (leader) {
+      if (ok) {
+        // End-of-work marker for the consumers.
+        if (mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) {
+          armed[stage] = 0;  // released: its last transaction has completed
+          meta[stage * kDecodeMetaInts + 0] = -1;
+          mbar_arrive(smem_u32(&full_bar[stage]));
+        } else {
+          flags[0] = 1;
+        }
       }
-    }
-    // Drain: never leave the CTA with a bulk copy still writing its shared
-    // memory (only matters after an abort; normally these return at once).
+      // Drain: never leave the CTA with a bulk copy still writing its shared
+      // memory (only matters after an abort; normally these return at once).
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) {
-      if (armed[s]) mbar_wait_bounded(smem_u32(&full_bar[s]), armed[s] - 1u);
-    }
-    // The last CTA out resets the scheduler counters for the next call.
-    __threadfence();
-    const unsigned int prev = atomicAdd(&p.counters[1], 1u);
-    if (prev == gridDim.x - 1) {
-      atomicExch(&p.counters[0], 0u);
-      atomicExch(&p.counters[1], 0u);
+      for (int s = 0; s < kStages; ++s) {
+        if (armed[s]) mbar_wait_bounded(smem_u32(&full_bar[s]), armed[s] - 1u);
+      }
+      // The last CTA out resets the scheduler counters for the next call.
+      __threadfence();
+      const unsigned int prev = atomicAdd(&p.counters[1], 1u);
+      if (prev == gridDim.x - 1) {
+        atomicExch(&p.counters[0], 0u);
+        atomicExch(&p.counters[1], 0u);
+      }
     }
     return;
   }

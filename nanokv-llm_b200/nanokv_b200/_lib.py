@@ -54,6 +54,12 @@ SIGNATURES: dict[str, tuple] = {
         [_P, c_int64, c_int64, _P, _P, c_int64, _I32P, c_int32, _I32P, _P, c_int64,
          c_int32, c_int32, c_int32, c_int32, c_int32, c_float, _P, c_size_t, _P],
     ),
+    "nkv_decode_step": (
+        c_int,
+        [_P, c_int64, c_int64, _P, c_int64, _P, c_int64, _I32P, _P, _P, c_int64, _I32P, c_int32,
+         _I32P, _P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _P, c_int64,
+         c_int32, c_int32, c_int32, c_int32, c_int32, c_float, _P, c_size_t, _P],
+    ),
     "nkv_window_compress": (
         c_int,
         [_P, c_int64, _P, _P, c_int64, _I32P, c_int32, _I32P, _I32P, _I32P, c_int32,

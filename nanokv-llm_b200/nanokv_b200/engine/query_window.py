@@ -58,6 +58,26 @@ class QueryWindowManager:
         t = torch.tensor([batch_index, slots, pos], dtype=torch.int32).to(self.device, non_blocking=True)
         return t[0], t[1], t[2]
 
+    def row_indices(self, seq_ids: list[int], batch_index: list[int], batch: int):
+        """Per batch row (ring slot or -1, write position) as device tensors,
+        for the fused decode step that appends inside the decode launch."""
+        slot = [-1] * batch
+        pos = [0] * batch
+        for sid, b in zip(seq_ids, batch_index):
+            slot[b], pos[b] = self.buffers[sid][0], self.buffers[sid][1]
+        t = torch.tensor([slot, pos], dtype=torch.int32).to(self.device, non_blocking=True)
+        return t[0], t[1]
+
+    def advance(self, seq_ids: list[int], layer_id: int) -> None:
+        """Bookkeeping of an append done elsewhere (the fused decode step):
+        write positions move on after the last layer, as in append()."""
+        if layer_id == self.num_layers - 1:
+            for s in seq_ids:
+                buf = self.buffers[s]
+                buf[1] = (buf[1] + 1) % self.window_size
+                if buf[2] < self.window_size:
+                    buf[2] += 1
+
     def append(self, seq_ids: list[int], layer_id: int, q: torch.Tensor,
                indices=None) -> None:
         """ring[slot(seq), layer_id, write_pos(seq)] = q[row]. `q` holds one
@@ -69,12 +89,7 @@ class QueryWindowManager:
             indices = self.step_indices(seq_ids)
         bidx, slots, pos = indices
         ops.query_window_append(q, self.ring, layer_id, bidx, slots, pos)
-        if layer_id == self.num_layers - 1:
-            for s in seq_ids:
-                buf = self.buffers[s]
-                buf[1] = (buf[1] + 1) % self.window_size
-                if buf[2] < self.window_size:
-                    buf[2] += 1
+        self.advance(seq_ids, layer_id)
 
     def gather(self, seq_ids: list[int], layer_id: int) -> torch.Tensor:
         """[m, Hq, W, D] in the reference's order (window starting at write_pos)."""

@@ -9,6 +9,10 @@ nanokvllm/layers/attention.py:42-108, same order of work per layer:
   3. decode attention over the paged cache     -> nkv_paged_decode
      (flash_attn_with_kvcache in the reference)
 
+On a decode step that does not compress, 1 and 3 run as one launch
+(nkv_decode_step), which writes each kv head's new row right before reading
+that tile.
+
 Prefill / mixed batches (use_decode_kernel False) are outside this path and
 keep the reference's flash_attn_varlen_func call unchanged.
 """
@@ -43,11 +47,19 @@ class Attention(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Layer):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
+        compressing = (context.use_decode_kernel and self.kv_compress_enabled
+                       and context.is_compress_step
+                       and bool(context.compress_selected_batch_indices))
+        if (context.use_decode_kernel and not compressing and k_cache.numel()
+                and q.size(0) == context.block_tables.size(0)):
+            # decode step without compression: slot write + decode in one launch
+            o = ops.decode_step(q, k, v, k_cache, v_cache, context.slot_mapping,
+                                context.block_tables, context.context_lens, self.scale)
+            return o.unsqueeze(1)
         if k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
 
-        if (context.use_decode_kernel and self.kv_compress_enabled and context.is_compress_step
-                and context.compress_selected_batch_indices):
+        if compressing:
             MyCompressCompact(q_current=q, k_cache=k_cache, v_cache=v_cache, layer_id=Layer,
                               block_size=k_cache.size(1),
                               window_blocks=self.kv_compress_window_blocks,

@@ -88,6 +88,26 @@ class Attention(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Layer):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
+        qwm = getattr(self, "query_window_manager", None)
+        if (not context.is_prefill and not context.compress_any and k_cache.numel()
+                and q.size(0) == context.block_tables.size(0)):
+            # decode step without compression: slot write, query-window append
+            # and decode in one launch
+            ring_args = {}
+            if self.kv_compress_enabled and qwm is not None and context.q_window_active_indices:
+                if context.q_window_row_slot_t is None:
+                    context.q_window_row_slot_t, context.q_window_row_pos_t = qwm.row_indices(
+                        context.q_window_active_seq_ids, context.q_window_active_indices,
+                        q.size(0))
+                ring_args = dict(ring=qwm.ring, layer_id=Layer,
+                                 ring_slot_of_row=context.q_window_row_slot_t,
+                                 ring_pos_of_row=context.q_window_row_pos_t)
+            o = ops.decode_step(q, k, v, k_cache, v_cache, context.slot_mapping,
+                                context.block_tables, context.context_lens, self.scale,
+                                **ring_args)
+            if ring_args:
+                qwm.advance(context.q_window_active_seq_ids, Layer)
+            return o.unsqueeze(1)
         if k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
         if not context.is_prefill and self.kv_compress_enabled:

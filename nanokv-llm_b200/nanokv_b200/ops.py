@@ -20,6 +20,7 @@ __all__ = [
     "store_kvcache",
     "flash_decode_with_kvcache",
     "paged_decode",
+    "decode_step",
     "decode_workspace",
     "window_compress",
     "query_window_append",
@@ -143,6 +144,54 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         block_tables.data_ptr(), max_blocks, context_lens.data_ptr(), out.data_ptr(), out.stride(0),
         B, Hq, Hk, D, block_size, float(softmax_scale), workspace.data_ptr(),
         workspace.numel() * workspace.element_size(), _stream(q.device)))
+    return out
+
+
+def decode_step(q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                v_cache: torch.Tensor, slot_mapping: torch.Tensor, block_tables: torch.Tensor,
+                context_lens: torch.Tensor, softmax_scale: float, out: torch.Tensor | None = None,
+                ring: torch.Tensor | None = None, layer_id: int = 0,
+                ring_slot_of_row: torch.Tensor | None = None,
+                ring_pos_of_row: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One fused launch of store_kvcache(key, value, slot_mapping) [+ the
+    KvChat query-window append] + paged_decode for a decode step (one new
+    token per row, slot_mapping[b] = -1 or the slot of position
+    context_lens[b] - 1)."""
+    _require_cuda("decode_step", q, key, value, k_cache, v_cache, slot_mapping, block_tables,
+                  context_lens)
+    B, Hq, D = q.shape
+    num_blocks, block_size, Hk, Dk = k_cache.shape
+    assert Dk == D and v_cache.shape == k_cache.shape
+    assert key.shape == (B, Hk, D) and value.shape == (B, Hk, D)
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == D and value.stride(1) == D
+    assert q.stride(-1) == 1 and k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.numel() == B
+    assert block_tables.dtype == torch.int32 and context_lens.dtype == torch.int32
+    max_blocks = block_tables.size(1)
+    if block_tables.stride(0) != max_blocks:
+        block_tables = block_tables.contiguous()
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=q.device)
+    if B == 0:
+        return out
+    if workspace is None:
+        workspace = decode_workspace(q.device, B, Hq, Hk, D, max_blocks, block_size)
+    if ring is not None:
+        slots, layers, W, Hr, Dr = ring.shape
+        assert Hr == Hq and Dr == D and ring.is_contiguous()
+        ring_args = (ring.data_ptr(), slots, layers, W, layer_id, ring_slot_of_row.data_ptr(),
+                     ring_pos_of_row.data_ptr())
+    else:
+        ring_args = (None, 0, 0, 0, 0, None, None)
+    lib = _lib.load()
+    _lib.check("nkv_decode_step", lib.nkv_decode_step(
+        q.data_ptr(), q.stride(0), q.stride(1), key.data_ptr(), key.stride(0), value.data_ptr(),
+        value.stride(0), slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        num_blocks, block_tables.data_ptr(), max_blocks, context_lens.data_ptr(), *ring_args,
+        out.data_ptr(), out.stride(0), B, Hq, Hk, D, block_size, float(softmax_scale),
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream(q.device)))
     return out
 
 

@@ -15,6 +15,8 @@ Additions, all optional and defaulting to "not provided":
                              device->host sync
   compress_ring_slots_t / q_window_*_t
                              device index tensors of the KvChat query window
+                             (per active row, and per batch row for the fused
+                             decode step)
 """
 
 from __future__ import annotations
@@ -60,6 +62,8 @@ class Context:
     q_window_batch_t: torch.Tensor | None = None
     q_window_slot_t: torch.Tensor | None = None
     q_window_pos_t: torch.Tensor | None = None
+    q_window_row_slot_t: torch.Tensor | None = None
+    q_window_row_pos_t: torch.Tensor | None = None
 
 
 _CONTEXT = Context()
