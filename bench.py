@@ -470,6 +470,100 @@ def measure_config4(dev, world):
             "tok_per_s": round(B / (t * layers), 1)}
 
 
+def prefill_flops(q_lens, k_lens, hq, causal=True) -> int:
+    """Algorithmic FLOPs of varlen attention: 2 x D per (query, key, head)
+    pair for Q K^T plus the same for P V, over the pairs the causal mask
+    admits (query i of a sequence sees Lk - Lq + i + 1 keys)."""
+    pairs = 0
+    for lq, lk in zip(q_lens, k_lens):
+        if causal:
+            first = lk - lq + 1
+            pairs += sum(max(0, min(lk, first + i)) for i in range(lq))
+        else:
+            pairs += lq * lk
+    return 4 * D * hq * pairs
+
+
+def measure_prefill(dev, world, compare_flash_attn: bool = True):
+    """Config 4's chunked prefill through nkv_paged_prefill (the replacement
+    of flash_attn_varlen_func at nanokvllm/layers/attention.py:96-102) on
+    Qwen3-32B attention shapes (64 q / 8 kv heads per TP1 layer): 16
+    sequences filled to 32,768 tokens in 2,048-token chunks, i.e. 16 steps
+    whose chunk c attends 2,048 causal queries per sequence to the
+    (c + 1) * 2,048 cached keys through the block tables. One layer's 16
+    steps (slot write + prefill attention) are timed with CUDA events and
+    scaled to 64 layers; the attention launches alone give the TFLOP/s. The
+    same attention calls through flash-attn (the reference's kernel, library
+    code) are timed beside them on the same inputs."""
+    from nanokv_b200 import ops
+
+    hq, hk, B, Lctx, chunk = 64 // world, 8 // world, 16, 32768, 2048
+    nsteps = Lctx // chunk
+    nb = B * Lctx // BLOCK
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(5)).view(B, -1)
+    bt = perm.to(torch.int32).to(dev)
+    kc = torch.empty(nb, BLOCK, hk, D, dtype=torch.bfloat16, device=dev).normal_()
+    vc = torch.empty_like(kc).normal_()
+    qkv = torch.randn(B * chunk, (hq + 2 * hk) * D, device=dev).to(torch.bfloat16)
+    q, k, v = qkv.split([hq * D, hk * D, hk * D], dim=-1)
+    q, k, v = q.view(-1, hq, D), k.view(-1, hk, D), v.view(-1, hk, D)
+    cu_q = (torch.arange(B + 1, dtype=torch.int32) * chunk).to(dev)
+    cu_k, sms = [], []
+    pos = torch.arange(chunk)
+    for c in range(nsteps):
+        cu_k.append((torch.arange(B + 1, dtype=torch.int32) * (c + 1) * chunk).to(dev))
+        p = c * chunk + pos
+        sm = (perm[:, (p // BLOCK)] * BLOCK + (p % BLOCK)).reshape(-1).to(torch.int32)
+        sms.append(sm.to(dev))
+    out = torch.empty(B * chunk, hq, D, dtype=torch.bfloat16, device=dev)
+    scale = D ** -0.5
+
+    def attn(c):
+        ops.paged_prefill(q, kc, vc, cu_q, cu_k[c], chunk, scale, block_table=bt, out=out)
+
+    def step(c):
+        ops.store_kvcache(k, v, kc, vc, sms[c])
+        attn(c)
+
+    def timed(fn, reps=2):
+        for c in range(nsteps):
+            fn(c)
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            for c in range(nsteps):
+                fn(c)
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) * 1e-3 / reps
+
+    t_step = timed(step)
+    t_attn = timed(attn)
+    flops = sum(prefill_flops([chunk] * B, [(c + 1) * chunk] * B, hq) for c in range(nsteps))
+    res = {"workload": "config4 chunked prefill: Qwen3-32B attention shapes (64 q / 8 kv heads), "
+                       "16 seqs x 32768 tokens in 2048-token chunks (16 steps: slot write + "
+                       "paged causal prefill attention); one layer timed, scaled x64",
+           "layer_ms_all_chunks": round(t_step * 1e3, 3),
+           "prefill_tok_per_s": round(B * Lctx / (t_step * 64), 1),
+           "attn_TFLOPs": round(flops / t_attn / 1e12, 1)}
+    if compare_flash_attn:
+        try:
+            from flash_attn import flash_attn_varlen_func
+        except Exception as e:  # library not importable: report without it
+            res["flash_attn"] = f"unavailable: {type(e).__name__}"
+            return res
+
+        def fa(c):
+            flash_attn_varlen_func(q, kc, vc, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k[c],
+                                   max_seqlen_q=chunk, max_seqlen_k=(c + 1) * chunk,
+                                   softmax_scale=scale, causal=True, block_table=bt)
+        t_fa = timed(fa)
+        res["flash_attn_TFLOPs"] = round(flops / t_fa / 1e12, 1)
+        res["attn_speedup_vs_flash_attn"] = round(t_fa / t_attn, 3)
+    return res
+
+
 # ---------------------------------------------------------------------- CPU arms
 def cpu_decode_sample(seconds: float, hq: int, hk: int):
     """Times the CPU oracle (fp32 torch restatement of the reference's paged

@@ -53,6 +53,7 @@ typedef enum nkv_status {
 #define NKV_DEVERR_WAIT_TIMEOUT    0x4u  /* a bounded mbarrier / cluster wait gave up */
 #define NKV_DEVERR_COMPRESS_RANGE  0x8u  /* compression window or slot outside the cache */
 #define NKV_DEVERR_RING_RANGE      0x10u /* query-window ring slot / position out of range */
+#define NKV_DEVERR_PREFILL_RANGE   0x20u /* cu_seqlens / max_seqlen_q outside the tensors or the grid */
 
 /* Human-readable name of a status code (static string). */
 const char* nkv_status_string(int status);
@@ -145,6 +146,40 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
                     int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                     int32_t head_dim, int32_t block_size, float softmax_scale,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 2c. Prefill / mixed-batch attention (variable-length, causal)            */
+/* Replaces: flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k,     */
+/*   max_seqlen_q, max_seqlen_k, softmax_scale, causal=True, block_table)    */
+/*   at nanokvllm/layers/attention.py:96-102 and KvChat/layers/attention.py: */
+/*   105-111 (metadata: nanokvllm/engine/model_runner.py:160-220).           */
+/* Sequence b has Lq = cu_seqlens_q[b+1]-cu_seqlens_q[b] query rows (q/out   */
+/* rows cu_seqlens_q[b] ..) and Lk = cu_seqlens_k[b+1]-cu_seqlens_k[b] keys.  */
+/* out[t, h] = softmax(scale * q[t, h] K^T) V over the keys of kv head       */
+/* h / g that query i (= t - cu_seqlens_q[b]) may see: all Lk keys, or with  */
+/* causal != 0 keys j <= Lk - Lq + i (bottom-right aligned mask, as          */
+/* flash-attn >= 2.1). A row that sees no key gets zeros.                    */
+/* Keys: with block_tables (the paged cache [num_blocks, block_size, Hk, D], */
+/* k_stride_token = v_stride_token = Hk*D, num_kv_rows = num_blocks *        */
+/* block_size) key j of sequence b is row block_tables[b, j / block_size] *  */
+/* block_size + j % block_size; with block_tables == NULL (prefill without a */
+/* cached prefix) it is row cu_seqlens_k[b] + j of k / v [num_kv_rows, Hk, D].*/
+/* max_seqlen_q sizes the grid and must be >= every Lq (rows violating it,   */
+/* or cu_seqlens outside num_q_tokens / num_kv_rows / the block table, are   */
+/* skipped and flag NKV_DEVERR_PREFILL_RANGE).                               */
+/* Supported: head_dim 128, g = num_q_heads / num_kv_heads in [1, 128],      */
+/* block_size a multiple of 64, heads of k / v / out contiguous (stride D).  */
+/* No workspace; nothing is allocated.                                       */
+int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                      int64_t num_q_tokens,
+                      const void* k, int64_t k_stride_token,
+                      const void* v, int64_t v_stride_token, int64_t num_kv_rows,
+                      const int32_t* block_tables, int32_t max_blocks, int32_t block_size,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                      int32_t batch, int32_t max_seqlen_q, int32_t causal,
+                      void* out, int64_t out_stride_token,
+                      int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                      float softmax_scale, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 3a. Periodic window compression (one layer, all selected sequences)       */

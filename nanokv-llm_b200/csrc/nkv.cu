@@ -14,6 +14,7 @@
 
 #include "nkv_common.cuh"
 #include "paged_decode.cuh"
+#include "paged_prefill.cuh"
 #include "store_kvcache.cuh"
 #include "threshold_compress.cuh"
 #include "window_compress.cuh"
@@ -459,6 +460,92 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
                            block_tables, max_blocks, context_lens, out, out_stride_token, batch,
                            num_q_heads, num_kv_heads, head_dim, block_size, softmax_scale,
                            workspace, workspace_bytes, stream, &f);
+}
+
+// ---------------------------------------------------------------- prefill
+int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                      int64_t num_q_tokens, const void* k, int64_t k_stride_token, const void* v,
+                      int64_t v_stride_token, int64_t num_kv_rows, const int32_t* block_tables,
+                      int32_t max_blocks, int32_t block_size, const int32_t* cu_seqlens_q,
+                      const int32_t* cu_seqlens_k, int32_t batch, int32_t max_seqlen_q,
+                      int32_t causal, void* out, int64_t out_stride_token, int32_t num_q_heads,
+                      int32_t num_kv_heads, int32_t head_dim, float softmax_scale, void* stream) {
+  if (batch < 0 || max_seqlen_q < 0 || num_q_tokens < 0 || num_kv_rows < 0 || num_q_heads <= 0 ||
+      num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || max_seqlen_q == 0 || num_q_tokens == 0) return NKV_OK;
+  if (!q || !k || !v || !cu_seqlens_q || !cu_seqlens_k || !out) return NKV_ERR_INVALID_ARGUMENT;
+  if (!std::isfinite(softmax_scale)) return NKV_ERR_INVALID_ARGUMENT;
+  const int g = num_q_heads / num_kv_heads;
+  if (head_dim != 128 || g > nkv::kPrefillRows || batch > 65535) return NKV_ERR_UNSUPPORTED;
+  if (block_tables != nullptr && (block_size <= 0 || block_size % nkv::kPrefillKeyTile != 0 ||
+                                  max_blocks <= 0))
+    return NKV_ERR_UNSUPPORTED;
+  const int qt = nkv::kPrefillRows / g;
+  const int64_t qtiles = (static_cast<int64_t>(max_seqlen_q) + qt - 1) / qt;
+  if (qtiles > 65535) return NKV_ERR_UNSUPPORTED;
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (k_stride_token < row || v_stride_token < row ||
+      out_stride_token < static_cast<int64_t>(num_q_heads) * head_dim ||
+      q_stride_head < head_dim || q_stride_token < q_stride_head * (num_q_heads - 1) + head_dim)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (q_stride_token % 8) ||
+      (q_stride_head % 8) || (k_stride_token % 8) || (v_stride_token % 8) ||
+      (reinterpret_cast<uintptr_t>(out) & 3u) || (out_stride_token % 2))
+    return NKV_ERR_ALIGNMENT;
+  const uint64_t kv_rows = static_cast<uint64_t>(std::max<int64_t>(num_kv_rows, 1));
+  CUtensorMap tk, tv, tq;
+  int st;
+  if ((st = encode_3d(&tk, k, head_dim, num_kv_heads, kv_rows, head_dim * 2, k_stride_token * 2, 1,
+                      nkv::kPrefillKeyTile, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
+    return st;
+  if ((st = encode_3d(&tv, v, head_dim, num_kv_heads, kv_rows, head_dim * 2, v_stride_token * 2, 1,
+                      nkv::kPrefillKeyTile, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
+    return st;
+  if ((st = encode_3d(&tq, q, head_dim, num_q_heads, num_q_tokens, q_stride_head * 2,
+                      q_stride_token * 2, g, qt, CU_TENSOR_MAP_L2_PROMOTION_NONE)) != NKV_OK)
+    return st;
+
+  nkv::PrefillParams p{};
+  p.block_tables = block_tables;
+  p.cu_q = cu_seqlens_q;
+  p.cu_k = cu_seqlens_k;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_token = out_stride_token;
+  p.num_blocks = block_tables ? num_kv_rows / block_size : 0;
+  p.num_q_tokens = num_q_tokens;
+  p.num_kv_rows = num_kv_rows;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.max_blocks = max_blocks;
+  p.batch = batch;
+  p.num_kv_heads = num_kv_heads;
+  p.g = g;
+  p.qt = qt;
+  p.block_size = block_size;
+  p.causal = causal ? 1 : 0;
+  p.qtiles = static_cast<int>(qtiles);
+
+  static bool attr_set[kMaxDevices] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nkv::paged_prefill_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         nkv::kPrefillSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_kv_heads, batch, static_cast<unsigned>(qtiles));
+  cfg.blockDim = dim3(nkv::kPrefillThreads, 1, 1);
+  cfg.dynamicSmemBytes = nkv::kPrefillSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::paged_prefill_kernel, tk, tv, tq, p));
 }
 
 // ------------------------------------------------------------------ window compress

@@ -183,6 +183,13 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// 2^x with the PTX approximate instruction (flush-to-zero; 2^-inf = +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Byte offset of (row, 16-byte chunk) inside a tile written by TMA with
 // CU_TENSOR_MAP_SWIZZLE_128B and 128-byte rows: chunk index XOR (row mod 8).
 __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {

@@ -109,12 +109,6 @@ struct DecodeParams {
   int num_q_heads;
 };
 
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, float4 v) {
   uint2 u;
   u.x = pack_bf16x2(v.x, v.y);

@@ -28,6 +28,7 @@ DEVERR_DECODE_BLOCK = 0x2
 DEVERR_WAIT_TIMEOUT = 0x4
 DEVERR_COMPRESS_RANGE = 0x8
 DEVERR_RING_RANGE = 0x10
+DEVERR_PREFILL_RANGE = 0x20
 
 # Size of the library's fixed decode scratch (NKV_STATIC_SCRATCH_BYTES, nkv.h).
 STATIC_SCRATCH_BYTES = 16 << 20
@@ -59,6 +60,12 @@ SIGNATURES: dict[str, tuple] = {
         [_P, c_int64, c_int64, _P, c_int64, _P, c_int64, _I32P, _P, _P, c_int64, _I32P, c_int32,
          _I32P, _P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _P, c_int64,
          c_int32, c_int32, c_int32, c_int32, c_int32, c_float, _P, c_size_t, _P],
+    ),
+    "nkv_paged_prefill": (
+        c_int,
+        [_P, c_int64, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int64, _I32P, c_int32,
+         c_int32, _I32P, _I32P, c_int32, c_int32, c_int32, _P, c_int64, c_int32, c_int32,
+         c_int32, c_float, _P],
     ),
     "nkv_window_compress": (
         c_int,

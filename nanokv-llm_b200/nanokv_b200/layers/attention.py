@@ -7,14 +7,14 @@ nanokvllm/layers/attention.py:42-108, same order of work per layer:
   2. periodic window compression when the Context asks for it
                                                -> nkv_window_compress (MyCompressCompact)
   3. decode attention over the paged cache     -> nkv_paged_decode
-     (flash_attn_with_kvcache in the reference)
+     (flash_attn_with_kvcache in the reference), or, on prefill / mixed
+     steps (use_decode_kernel False), variable-length causal attention
+                                               -> nkv_paged_prefill
+     (flash_attn_varlen_func in the reference, :96-102)
 
 On a decode step that does not compress, 1 and 3 run as one launch
 (nkv_decode_step), which writes each kv head's new row right before reading
 that tile.
-
-Prefill / mixed batches (use_decode_kernel False) are outside this path and
-keep the reference's flash_attn_varlen_func call unchanged.
 """
 
 from __future__ import annotations
@@ -68,15 +68,14 @@ class Attention(nn.Module):
                               num_layers=self.num_layers, context=context)
 
         if not context.use_decode_kernel:
-            from flash_attn import flash_attn_varlen_func  # prefill: not part of this path
-            if context.block_tables is not None:
+            if context.block_tables is not None:  # keys come from the paged cache
                 k, v = k_cache, v_cache
-            return flash_attn_varlen_func(q, k, v, max_seqlen_q=context.max_seqlen_q,
-                                          cu_seqlens_q=context.cu_seqlens_q,
-                                          max_seqlen_k=context.max_seqlen_k,
-                                          cu_seqlens_k=context.cu_seqlens_k,
-                                          softmax_scale=self.scale, causal=True,
-                                          block_table=context.block_tables)
+            return ops.flash_attn_varlen_func(q, k, v, max_seqlen_q=context.max_seqlen_q,
+                                              cu_seqlens_q=context.cu_seqlens_q,
+                                              max_seqlen_k=context.max_seqlen_k,
+                                              cu_seqlens_k=context.cu_seqlens_k,
+                                              softmax_scale=self.scale, causal=True,
+                                              block_table=context.block_tables)
         return ops.flash_decode_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
                                              cache_seqlens=context.context_lens,
                                              block_table=context.block_tables,

@@ -6,7 +6,8 @@ Per layer: store (nkv_store_kvcache), append the active sequences' queries to
 the device query ring (nkv_query_window_append), compress the sequences whose
 length reached S (nkv_threshold_compress: gather, SnapKV over the W-query
 window, top-k and in-place compaction to positions [0, R) in one launch), then
-decode (nkv_paged_decode).
+decode (nkv_paged_decode). Prefill steps run nkv_paged_prefill where the
+reference calls flash_attn_varlen_func (KvChat/layers/attention.py:105-111).
 """
 
 from __future__ import annotations
@@ -129,15 +130,14 @@ class Attention(nn.Module):
                                   query_window_size=self.query_window_size, context=context,
                                   num_layers=self.num_layers)
         if context.is_prefill:
-            from flash_attn import flash_attn_varlen_func  # prefill: not part of this path
-            if context.block_tables is not None:
+            if context.block_tables is not None:  # keys come from the paged cache
                 k, v = k_cache, v_cache
-            return flash_attn_varlen_func(q, k, v, max_seqlen_q=context.max_seqlen_q,
-                                          cu_seqlens_q=context.cu_seqlens_q,
-                                          max_seqlen_k=context.max_seqlen_k,
-                                          cu_seqlens_k=context.cu_seqlens_k,
-                                          softmax_scale=self.scale, causal=True,
-                                          block_table=context.block_tables)
+            return ops.flash_attn_varlen_func(q, k, v, max_seqlen_q=context.max_seqlen_q,
+                                              cu_seqlens_q=context.cu_seqlens_q,
+                                              max_seqlen_k=context.max_seqlen_k,
+                                              cu_seqlens_k=context.cu_seqlens_k,
+                                              softmax_scale=self.scale, causal=True,
+                                              block_table=context.block_tables)
         return ops.flash_decode_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
                                              cache_seqlens=context.context_lens,
                                              block_table=context.block_tables,

@@ -22,6 +22,8 @@ __all__ = [
     "paged_decode",
     "decode_step",
     "decode_workspace",
+    "paged_prefill",
+    "flash_attn_varlen_func",
     "window_compress",
     "query_window_append",
     "threshold_compress",
@@ -208,6 +210,75 @@ def flash_decode_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     o = paged_decode(q[:, 0], k_cache, v_cache, block_table, cache_seqlens, softmax_scale,
                      out=None if out is None else out[:, 0])
     return o.unsqueeze(1)
+
+
+# ---------------------------------------------------------------- prefill
+def paged_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                  cu_seqlens_k: torch.Tensor, max_seqlen_q: int, softmax_scale: float,
+                  causal: bool = True, block_table: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Variable-length attention of a prefill / mixed batch (nkv_paged_prefill).
+
+    q: [T, Hq, D] bf16. With block_table ([B, max_blocks] int32) k / v are the
+    paged caches [num_blocks, block_size, Hk, D]; without it they are the
+    step's rows [Tk, Hk, D] addressed through cu_seqlens_k. cu_seqlens_* are
+    int32 [B + 1] device tensors; causal masks bottom-right aligned.
+    Returns out [T, Hq, D] bf16.
+    """
+    _require_cuda("paged_prefill", q, k, v, cu_seqlens_q, cu_seqlens_k, block_table)
+    T, Hq, D = q.shape
+    assert q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+    assert q.stride(-1) == 1 and k.stride(-1) == 1 and v.stride(-1) == 1
+    assert cu_seqlens_q.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32
+    assert cu_seqlens_q.is_contiguous() and cu_seqlens_k.is_contiguous()
+    B = cu_seqlens_q.numel() - 1
+    assert cu_seqlens_k.numel() == B + 1
+    if block_table is not None:
+        num_blocks, block_size, Hk, Dk = k.shape
+        assert k.is_contiguous() and v.is_contiguous() and v.shape == k.shape
+        assert block_table.dtype == torch.int32 and block_table.dim() == 2
+        assert block_table.size(0) >= B
+        if not block_table.is_contiguous():
+            block_table = block_table.contiguous()
+        rows, k_stride, v_stride = num_blocks * block_size, Hk * D, Hk * D
+        max_blocks = block_table.size(1)
+        bt_ptr = block_table.data_ptr()
+    else:
+        rows, Hk, Dk = k.shape
+        assert v.shape == k.shape and k.stride(1) == D and v.stride(1) == D
+        k_stride, v_stride = k.stride(0), v.stride(0)
+        block_size = max_blocks = 0
+        bt_ptr = None
+    assert Dk == D
+    if out is None:
+        out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=q.device)
+    assert out.stride(-1) == 1 and out.stride(1) == D and out.size(0) >= T
+    if B <= 0 or T == 0 or max_seqlen_q <= 0:
+        return out
+    lib = _lib.load()
+    _lib.check("nkv_paged_prefill", lib.nkv_paged_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1), T, k.data_ptr(), k_stride, v.data_ptr(), v_stride,
+        rows, bt_ptr, max_blocks, block_size, cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), B,
+        int(max_seqlen_q), 1 if causal else 0, out.data_ptr(), out.stride(0), Hq, Hk, D,
+        float(softmax_scale), _stream(q.device)))
+    return out
+
+
+def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor,
+                           max_seqlen_q: int, max_seqlen_k: int,
+                           softmax_scale: float | None = None, causal: bool = False,
+                           block_table: torch.Tensor | None = None) -> torch.Tensor:
+    """Drop-in for the reference's prefill / mixed-batch call of
+    flash_attn_varlen_func (nanokvllm/layers/attention.py:96-102), with the
+    keyword names and defaults of flash-attn's function. max_seqlen_k is
+    accepted for the signature; the kernel reads each length from cu_seqlens_k.
+    """
+    del max_seqlen_k
+    if softmax_scale is None:
+        softmax_scale = q.size(-1) ** -0.5
+    return paged_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale,
+                         causal=causal, block_table=block_table)
 
 
 # ---------------------------------------------------------------- window compression

@@ -6,6 +6,8 @@ reference computes on the path that libnkv replaces:
   * store_kvcache slot writes        (nanokvllm/layers/attention.py:10-40)
   * paged decode attention           (flash_attn_with_kvcache semantics at
                                       nanokvllm/layers/attention.py:104-107)
+  * prefill / mixed-batch attention  (flash_attn_varlen_func semantics at
+                                      nanokvllm/layers/attention.py:96-102)
   * SnapKV scoring + top-k           (nanokvllm/layers/CompressMethod.py:4-58,
                                       KvChat/layers/CompressMethod.py:4-58)
   * periodic window compression      (nanokvllm/layers/compress_utils.py:9-290)

@@ -56,3 +56,21 @@ def threshold_inputs(seed: int, P: int, Hq: int, Hk: int, W: int, S_cfg: int, L:
     rng = np.random.default_rng(seed + 1000)
     qsteps = bf16(rng.standard_normal((W, L, 1, Hq, 128), dtype=np.float32))
     return pb, qsteps
+
+
+# Prefill / mixed-batch attention (flash_attn_varlen_func at
+# nanokvllm/layers/attention.py:96-102): (name, make_varlen_batch kwargs).
+# Covers prefill without a cached prefix (contiguous K/V), prefix-cached
+# prefill, chunked-prefill mixed batches with decode rows (Lq = 1), GQA
+# widths 1/2/3/4/8, empty sequences and queries longer than their keys.
+VARLEN_CASES = [
+    ("prefill_nocache_g2", dict(seed=41, q_lens=[1, 77, 300, 1024], k_lens=[1, 77, 300, 1024],
+                                Hq=16, Hk=8, paged=False)),
+    ("prefix_paged_g4", dict(seed=42, q_lens=[200, 64, 513], k_lens=[456, 1000, 769],
+                             Hq=32, Hk=8)),
+    ("mixed_chunked_g4", dict(seed=43, q_lens=[1, 1, 300, 1, 130], k_lens=[700, 1, 2300, 4097, 130],
+                              Hq=32, Hk=8)),
+    ("g8_paged", dict(seed=44, q_lens=[129, 3], k_lens=[129, 2000], Hq=64, Hk=8)),
+    ("mha_empty_rows", dict(seed=45, q_lens=[0, 5, 17, 0], k_lens=[0, 5, 17, 40], Hq=8, Hk=8)),
+    ("g3_nocache", dict(seed=46, q_lens=[50, 400], k_lens=[50, 400], Hq=24, Hk=8, paged=False)),
+]

@@ -91,3 +91,59 @@ CONFIG1_COMPRESS = dict(selected=[3], window_blocks=4, keep_blocks=2, keep_extra
 
 def make_config1() -> PagedBatch:
     return make_paged_batch(**CONFIG1)
+
+
+@dataclass
+class VarlenBatch:
+    q: torch.Tensor             # [T, Hq, D] bf16: the step's query rows
+    k_new: torch.Tensor         # [T, Hk, D] bf16: the step's key rows
+    v_new: torch.Tensor
+    k_cache: torch.Tensor | None  # [num_blocks, block_size, Hk, D] (paged) or None
+    v_cache: torch.Tensor | None
+    block_tables: torch.Tensor | None  # [B, max_blocks] int32, -1 padded
+    slot_mapping: torch.Tensor  # [T] int32: cache slot of each step row (paged)
+    cu_seqlens_q: torch.Tensor  # [B + 1] int32
+    cu_seqlens_k: torch.Tensor  # [B + 1] int32
+    max_seqlen_q: int
+    max_seqlen_k: int
+
+
+def make_varlen_batch(seed: int, q_lens: list[int], k_lens: list[int], Hq: int, Hk: int,
+                      D: int = 128, block_size: int = 256, paged: bool = True) -> VarlenBatch:
+    """A prefill / mixed batch as the reference's prepare_step builds it
+    (nanokvllm/engine/model_runner.py:160-220): sequence b advances q_lens[b]
+    tokens and then holds k_lens[b] >= q_lens[b] tokens, so its step rows are
+    positions k_lens[b] - q_lens[b] .. k_lens[b] - 1. Paged: the cache holds
+    every sequence's k_lens[b] tokens in randomly permuted blocks, the step's
+    rows included (as after store_kvcache). Unpaged (no cached prefix,
+    k_lens == q_lens): keys are the step's rows themselves."""
+    rng = np.random.default_rng(seed)
+    assert len(q_lens) == len(k_lens)
+    T = sum(q_lens)
+    cu_q = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    cu_k = np.concatenate([[0], np.cumsum(k_lens)]).astype(np.int32)
+    q = bf16(rng.standard_normal((T, Hq, D), dtype=np.float32))
+    if not paged:
+        assert list(q_lens) == list(k_lens)
+        kn = bf16(rng.standard_normal((T, Hk, D), dtype=np.float32))
+        vn = bf16(rng.standard_normal((T, Hk, D), dtype=np.float32))
+        return VarlenBatch(q=q, k_new=kn, v_new=vn, k_cache=None, v_cache=None,
+                           block_tables=None, slot_mapping=torch.full((T,), -1, dtype=torch.int32),
+                           cu_seqlens_q=torch.from_numpy(cu_q), cu_seqlens_k=torch.from_numpy(cu_k),
+                           max_seqlen_q=max(q_lens, default=0), max_seqlen_k=max(k_lens, default=0))
+    pb = make_paged_batch(seed + 1000, list(k_lens), Hq, Hk, D, block_size)
+    slots = []
+    for b, (lq, lk) in enumerate(zip(q_lens, k_lens)):
+        assert lk >= lq
+        t = pb.block_tables[b].tolist()
+        for pos in range(lk - lq, lk):
+            slots.append(t[pos // block_size] * block_size + pos % block_size)
+    sm = torch.tensor(slots, dtype=torch.int32)
+    flat_k = pb.k_cache.view(-1, Hk, D)
+    flat_v = pb.v_cache.view(-1, Hk, D)
+    kn = flat_k[sm.long()].clone() if T else torch.zeros(0, Hk, D, dtype=torch.bfloat16)
+    vn = flat_v[sm.long()].clone() if T else torch.zeros(0, Hk, D, dtype=torch.bfloat16)
+    return VarlenBatch(q=q, k_new=kn, v_new=vn, k_cache=pb.k_cache, v_cache=pb.v_cache,
+                       block_tables=pb.block_tables, slot_mapping=sm,
+                       cu_seqlens_q=torch.from_numpy(cu_q), cu_seqlens_k=torch.from_numpy(cu_k),
+                       max_seqlen_q=max(q_lens, default=0), max_seqlen_k=max(k_lens, default=0))

@@ -57,3 +57,26 @@ def test_argument_errors_need_no_gpu():
     # obs_window other than 1 is not the reference's periodic path
     assert lib.nkv_window_compress(16, 4096, 16, 16, 10, 16, 8, 16, 16, 16, 1, 4, 513, 2, 32, 8,
                                    128, 256, 0.1, None, None, None) == 2
+
+
+def test_prefill_argument_errors_need_no_gpu():
+    """nkv_paged_prefill validates shapes, strides and alignment on the host."""
+    from nanokv_b200 import _lib
+
+    lib = _lib.load()
+    base = dict(q=16, qst=4096, qsh=128, nq=100, k=16, kst=1024, v=16, vst=1024, rows=1000,
+                bt=16, mb=8, bs=256, cuq=16, cuk=16, b=2, mq=64, causal=1, out=16, ost=4096,
+                hq=32, hk=8, d=128, scale=0.1, stream=None)
+
+    def call(**over):
+        a = dict(base, **over)
+        return lib.nkv_paged_prefill(*a.values())
+
+    assert call(d=64) == 2                      # head_dim 128 only
+    assert call(bs=100) == 2                    # paged block size multiple of 64
+    assert call(q=18) == 4                      # misaligned q
+    assert call(kst=1028) == 4                  # row stride not a 16-byte multiple
+    assert call(hq=30) == 1                     # Hq % Hk != 0
+    assert call(ost=2048) == 1                  # out rows too short for Hq heads
+    assert call(b=0) == 0 and call(mq=0) == 0   # empty batch is a no-op
+    assert call(scale=float("inf")) == 1
