@@ -168,7 +168,8 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
 /* or cu_seqlens outside num_q_tokens / num_kv_rows / the block table, are   */
 /* skipped and flag NKV_DEVERR_PREFILL_RANGE).                               */
 /* Supported: head_dim 128, g = num_q_heads / num_kv_heads in [1, 128],      */
-/* block_size a multiple of 64, heads of k / v / out contiguous (stride D).  */
+/* block_size 64 or a multiple of 128, heads of k / v / out contiguous       */
+/* (stride D), out 16-byte aligned with out_stride_token a multiple of 8.    */
 /* No workspace; nothing is allocated.                                       */
 int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                       int64_t num_q_tokens,

@@ -478,8 +478,10 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
   if (!std::isfinite(softmax_scale)) return NKV_ERR_INVALID_ARGUMENT;
   const int g = num_q_heads / num_kv_heads;
   if (head_dim != 128 || g > nkv::kPrefillRows || batch > 65535) return NKV_ERR_UNSUPPORTED;
-  if (block_tables != nullptr && (block_size <= 0 || block_size % nkv::kPrefillKeyTile != 0 ||
-                                  max_blocks <= 0))
+  // A 128-key tile spans whole cache blocks (64-token blocks: two per tile)
+  // or lies inside one (multiples of 128).
+  if (block_tables != nullptr &&
+      (max_blocks <= 0 || !(block_size == 64 || (block_size > 0 && block_size % 128 == 0))))
     return NKV_ERR_UNSUPPORTED;
   const int qt = nkv::kPrefillRows / g;
   const int64_t qtiles = (static_cast<int64_t>(max_seqlen_q) + qt - 1) / qt;
@@ -491,16 +493,18 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
     return NKV_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (q_stride_token % 8) ||
       (q_stride_head % 8) || (k_stride_token % 8) || (v_stride_token % 8) ||
-      (reinterpret_cast<uintptr_t>(out) & 3u) || (out_stride_token % 2))
+      !aligned16(out) || (out_stride_token % 8))
     return NKV_ERR_ALIGNMENT;
   const uint64_t kv_rows = static_cast<uint64_t>(std::max<int64_t>(num_kv_rows, 1));
+  const int rows_per_load = block_tables ? std::min(block_size, nkv::kPrefillKeyTile)
+                                         : nkv::kPrefillKeyTile;
   CUtensorMap tk, tv, tq;
   int st;
   if ((st = encode_3d(&tk, k, head_dim, num_kv_heads, kv_rows, head_dim * 2, k_stride_token * 2, 1,
-                      nkv::kPrefillKeyTile, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
+                      rows_per_load, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
     return st;
   if ((st = encode_3d(&tv, v, head_dim, num_kv_heads, kv_rows, head_dim * 2, v_stride_token * 2, 1,
-                      nkv::kPrefillKeyTile, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
+                      rows_per_load, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) != NKV_OK)
     return st;
   if ((st = encode_3d(&tq, q, head_dim, num_q_heads, num_q_tokens, q_stride_head * 2,
                       q_stride_token * 2, g, qt, CU_TENSOR_MAP_L2_PROMOTION_NONE)) != NKV_OK)
@@ -522,6 +526,7 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
   p.g = g;
   p.qt = qt;
   p.block_size = block_size;
+  p.rows_per_load = rows_per_load;
   p.causal = causal ? 1 : 0;
   p.qtiles = static_cast<int>(qtiles);
 

@@ -10,35 +10,56 @@
 // cache (block_tables) or, without a block table, in rows cu_k[b] + j of
 // contiguous K/V tensors.
 //
-// One CTA per (kv head, sequence, q-tile). A q-tile is up to 128 rows:
-// QT = floor(128/g) query positions x the g query heads of the kv head's GQA
-// group (row = i*g + r), so every K/V tile is read once for the whole group.
-// q-tiles run longest-first (grid z reversed) to shorten the causal tail.
-//   * warp 8, the producer: TMA-loads the q-tile (one transaction) and then
-//     streams 64-key K and V tiles (128B swizzle, no multicast) through a
-//     4-stage full/empty mbarrier ring; a tile never crosses a cache block.
-//   * warps 0-7, the consumers: 16 rows each; S = Q K^T and O += P V with
-//     mma.sync m16n8k16 (bf16 in, fp32 accumulate), online softmax in the
-//     exp2 domain, causal and length masks by select on the diagonal tiles;
-//     P is re-packed from the S accumulators as the A operand.
-//   * epilogue: O / l in bf16 to the query rows that exist (Lq may end inside
-//     the tile). Rows with no admissible key (Lk = 0) get zeros.
+// One CTA per (kv head, sequence, q-tile); q-tiles run longest-first (grid z
+// reversed) to shorten the causal tail. A q-tile is the 128-row M side of
+// the tensor-core tiles: QT = floor(128/g) query positions x the g query
+// heads of the kv head's GQA group (row = i*g + r), so every K/V tile is
+// read once for the whole group.
+//
+// Fifth-generation tensor cores (tcgen05), all accumulators in TMEM:
+//   * warp 9, producer: TMA-loads the q-tile, then 128-key K and V tiles
+//     (128-byte swizzle, no multicast) into a 3-deep K ring and a 2-deep V
+//     ring; a tile is cut at cache-block boundaries when blocks hold < 128.
+//   * warp 8, MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
+//     S buffers (8 x UMMA 128x128x16, A and B from shared memory), then
+//     O += P_{j-1} V_{j-1} (A = P from TMEM, B = V MN-major from shared
+//     memory) once the softmax warps have written P_{j-1}: the tensor core
+//     computes S_j while the softmax of tile j-1 runs.
+//   * warps 0-7, softmax: row t = TMEM lane t belongs to warps t/32 and
+//     t/32 + 4, which take key columns [0,64) and [64,128) of S (and dims
+//     [0,64) / [64,128) of O). Per tile: S half-row from TMEM, causal /
+//     length masks on diagonal and tail tiles, the two partial row maxima
+//     exchanged through shared memory (an mbarrier of the 8 warps), online
+//     softmax in the exp2 domain with a lazily moved maximum (O in TMEM is
+//     rescaled only when the row maximum grows by more than 2^8, so
+//     stale-maximum probabilities stay <= 256), P packed to bf16 into TMEM;
+//     row sums stay per half until the epilogue O / l -> bf16 -> the query
+//     rows that exist.
+// TMEM columns: S0 [0,128), S1 [128,256), O [256,384), P [384,448).
 #pragma once
 #include "nkv_common.cuh"
+#include "tcgen05.cuh"
 
 namespace nkv {
 
-constexpr int kPrefillRows = 128;          // rows (query x head) per CTA
-constexpr int kPrefillKeyTile = 64;        // keys per pipeline stage
-constexpr int kPrefillConsumerWarps = 8;
-constexpr int kPrefillThreads = (kPrefillConsumerWarps + 1) * 32;
-constexpr int kPrefillStages = 4;
-constexpr int kPrefillHalfKV = kPrefillKeyTile * 128;     // 64 rows x 64 dims x 2 B
-constexpr int kPrefillStageBytes = 4 * kPrefillHalfKV;    // K lo/hi, V lo/hi
-constexpr int kPrefillQHalf = kPrefillRows * 128;         // 128 rows x 64 dims x 2 B
-constexpr int kPrefillSmemBytes =
-    2 * kPrefillQHalf + kPrefillStages * kPrefillStageBytes + (2 * kPrefillStages + 1) * 8 + 64 +
-    1024 /* alignment */;
+constexpr int kPrefillRows = 128;      // M: rows (query x head) per CTA
+constexpr int kPrefillKeyTile = 128;   // N of S / K of PV: keys per tile
+constexpr int kPrefillKStages = 3;
+constexpr int kPrefillVStages = 2;
+constexpr int kPrefillThreads = 320;   // 8 softmax warps, MMA warp, producer warp
+constexpr int kPrefillMmaWarp = 8;
+constexpr int kPrefillProducerWarp = 9;
+constexpr int kPrefillHalf = kPrefillKeyTile * 128;   // 64 dims x 128 keys x 2 B
+constexpr int kPrefillTileBytes = 2 * kPrefillHalf;   // one K or V tile, 32 KB
+constexpr int kPrefillQHalf = kPrefillRows * 128;
+constexpr int kPrefillNumBars = 20;
+constexpr int kPrefillRedBytes = 2 * 2 * kPrefillRows * 4;  // [parity][half][row] floats
+constexpr int kPrefillSmemBytes = 2 * kPrefillQHalf +
+                                  (kPrefillKStages + kPrefillVStages) * kPrefillTileBytes + 256 +
+                                  kPrefillRedBytes + 1024 /* alignment */;
+constexpr uint32_t kPrefillTmemCols = 512;
+constexpr uint32_t kTmemS0 = 0, kTmemO = 256, kTmemP = 384;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
   const int32_t* block_tables;  // null: contiguous K/V rows cu_k[b] + j
@@ -53,31 +74,68 @@ struct PrefillParams {
   int max_blocks;
   int batch;
   int num_kv_heads;
-  int g;            // query heads per kv head
-  int qt;           // query positions per CTA, floor(128 / g)
+  int g;              // query heads per kv head
+  int qt;             // query positions per CTA, floor(128 / g)
   int block_size;
+  int rows_per_load;  // keys per TMA box: min(block_size, 128) paged, 128 contiguous
   int causal;
-  int qtiles;   // q-tiles per sequence slot of the grid
+  int qtiles;         // q-tiles per sequence slot of the grid
 };
+
+// 3-D tiled TMA load with the default L2 policy (K/V tiles are re-read by
+// every q-tile of the sequence, so they should stay in L2).
+__device__ __forceinline__ void tma_load_3d_nohint(uint32_t dst, const CUtensorMap* map,
+                                                   uint32_t bar, int32_t c0, int32_t c1,
+                                                   int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Publishes `v` for (row, half) and returns the other half's value, through
+// shared-memory slots and an mbarrier of 8 warp arrivals (bounded wait).
+__device__ __forceinline__ float exchange_half(float* red, uint64_t* red_bar, int step, int half,
+                                               int row, int lane, float v) {
+  float* slot = red + ((step & 1) * 2) * kPrefillRows;
+  slot[half * kPrefillRows + row] = v;
+  __syncwarp();
+  const uint32_t bar = smem_u32(&red_bar[step & 1]);
+  if (lane == 0) mbar_arrive(bar);
+  mbar_wait_bounded(bar, (step >> 1) & 1);
+  return slot[(half ^ 1) * kPrefillRows + row];
+}
 
 __global__ void __launch_bounds__(kPrefillThreads, 1)
 paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_q, const PrefillParams p) {
-  const int G = p.g;
-  const int QT = p.qt;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* q_mem = smem;                                  // Q lo, Q hi
-  uint8_t* stage_mem = smem + 2 * kPrefillQHalf;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_mem + kPrefillStages * kPrefillStageBytes);
-  uint64_t* empty_bar = full_bar + kPrefillStages;
-  uint64_t* q_bar = empty_bar + kPrefillStages;
+  uint8_t* q_mem = smem;  // Q lo, Q hi
+  uint8_t* k_mem = smem + 2 * kPrefillQHalf;
+  uint8_t* v_mem = k_mem + kPrefillKStages * kPrefillTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(v_mem + kPrefillVStages * kPrefillTileBytes);
+  uint64_t* q_full = bars;                       // 1
+  uint64_t* k_full = bars + 1;                   // 3
+  uint64_t* k_empty = k_full + kPrefillKStages;  // 3
+  uint64_t* v_full = k_empty + kPrefillKStages;  // 2
+  uint64_t* v_empty = v_full + kPrefillVStages;  // 2
+  uint64_t* s_full = v_empty + kPrefillVStages;  // 2
+  uint64_t* s_free = s_full + 2;                 // 2
+  uint64_t* p_full = s_free + 2;                 // 1
+  uint64_t* pv_done = p_full + 1;                // 1
+  uint64_t* mma_done = pv_done + 1;              // 1
+  uint64_t* red_bar = mma_done + 1;              // 2: half-row exchange, by tile parity
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kPrefillNumBars);
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Longest q-tiles (most keys under the causal mask) first.
+  const int G = p.g;
+  const int QT = p.qt;
   const int qtile = p.qtiles - 1 - static_cast<int>(blockIdx.z);
   const int kvh = blockIdx.x;
   const int b = blockIdx.y;
@@ -103,237 +161,323 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
   const int ntiles = (kend + kPrefillKeyTile - 1) / kPrefillKeyTile;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPrefillStages; ++s) {
-      mbar_init(smem_u32(&full_bar[s]), 1);
-      mbar_init(smem_u32(&empty_bar[s]), kPrefillConsumerWarps);
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < kPrefillKStages; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
     }
-    mbar_init(smem_u32(q_bar), 1);
+    for (int s = 0; s < kPrefillVStages; ++s) {
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&s_full[s]), 1);
+      mbar_init(smem_u32(&s_free[s]), 8);
+    }
+    mbar_init(smem_u32(p_full), 8);
+    mbar_init(smem_u32(pv_done), 1);
+    mbar_init(smem_u32(mma_done), 1);
+    mbar_init(smem_u32(&red_bar[0]), 8);
+    mbar_init(smem_u32(&red_bar[1]), 8);
     fence_barrier_init();
   }
+  if (warp == kPrefillMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), kPrefillTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
   grid_dependency_wait();
 
-  if (warp == kPrefillConsumerWarps) {
+  if (warp == kPrefillProducerWarp) {
     // ------------------------------------------------------------ producer
-    if (lane != 0) return;
-    const uint64_t pol_stream = l2_policy_evict_first();
-    const uint64_t pol_q = l2_policy_evict_first();
-    prefetch_tmap(&tm_k);
-    prefetch_tmap(&tm_v);
-    prefetch_tmap(&tm_q);
-    {
+    if (lane == 0) {
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      prefetch_tmap(&tm_q);
       const uint32_t qb = smem_u32(q_mem);
-      mbar_arrive_expect_tx(smem_u32(q_bar), 2u * QT * G * 128);
-      tma_load_3d(qb, &tm_q, smem_u32(q_bar), 0, kvh * G, q0 + qs, pol_q);
-      tma_load_3d(qb + kPrefillQHalf, &tm_q, smem_u32(q_bar), 64, kvh * G, q0 + qs, pol_q);
-    }
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t armed[kPrefillStages];
-#pragma unroll
-    for (int s = 0; s < kPrefillStages; ++s) armed[s] = 0;
-    for (int t = 0; t < ntiles; ++t) {
-      if (!mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u)) break;
-      armed[stage] = 0;
-      const int tok = t * kPrefillKeyTile;
-      int row;
-      if (p.block_tables != nullptr) {
-        const int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
-                              tok / p.block_size);
-        if (blk < 0 || static_cast<int64_t>(blk) >= p.num_blocks) {
-          raise_error(NKV_DEVERR_DECODE_BLOCK);
-          row = -2 * kPrefillKeyTile;  // fully out of range: zeros
-        } else {
-          row = blk * p.block_size + (tok % p.block_size);
-        }
-      } else {
-        row = k0 + tok;
-      }
-      const uint32_t fb = smem_u32(&full_bar[stage]);
-      mbar_arrive_expect_tx(fb, 4u * kPrefillHalfKV);
-      armed[stage] = phase + 1u;
-      const uint32_t base = smem_u32(stage_mem + stage * kPrefillStageBytes);
-      tma_load_3d(base + 0 * kPrefillHalfKV, &tm_k, fb, 0, kvh, row, pol_stream);
-      tma_load_3d(base + 1 * kPrefillHalfKV, &tm_k, fb, 64, kvh, row, pol_stream);
-      tma_load_3d(base + 2 * kPrefillHalfKV, &tm_v, fb, 0, kvh, row, pol_stream);
-      tma_load_3d(base + 3 * kPrefillHalfKV, &tm_v, fb, 64, kvh, row, pol_stream);
-      if (++stage == kPrefillStages) {
-        stage = 0;
-        phase ^= 1u;
-      }
-    }
-    // Drain outstanding transactions before leaving (only after an abort).
-#pragma unroll
-    for (int s = 0; s < kPrefillStages; ++s)
-      if (armed[s]) mbar_wait_bounded(smem_u32(&full_bar[s]), armed[s] - 1u);
-    mbar_wait_bounded(smem_u32(q_bar), 0);
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
-  const int cw = warp;
-  const int gid = lane >> 2;
-  const int tig = lane & 3;
-  const float NEG_INF = -INFINITY;
-  const float scale_log2 = p.scale_log2;
-  // This thread's two rows of the warp's m-tile: rho = 16*cw + gid (+8).
-  const int rho0 = 16 * cw + gid;
-  const int rho1 = rho0 + 8;
-  const int qi0 = rho0 / G, qi1 = rho1 / G;  // query positions within the tile
-  const int lim0 = shift + qs + qi0;         // last admissible key (causal)
-  const int lim1 = shift + qs + qi1;
-
-  float o[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
-
-  // Q fragments (A operand) of the warp's 16 rows, from the swizzled q-tile.
-  uint32_t qa[8][4];
-  const bool q_ok = mbar_wait_bounded(smem_u32(q_bar), 0);
-  {
-    const uint8_t* qlo = q_mem;
-    const uint8_t* qhi = q_mem + kPrefillQHalf;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint8_t* qh = (kk < 4) ? qlo : qhi;
-      const uint32_t c = 2u * (kk & 3);
-      qa[kk][0] = *reinterpret_cast<const uint32_t*>(qh + swz128(rho0, c) + 4 * tig);
-      qa[kk][1] = *reinterpret_cast<const uint32_t*>(qh + swz128(rho1, c) + 4 * tig);
-      qa[kk][2] = *reinterpret_cast<const uint32_t*>(qh + swz128(rho0, c + 1) + 4 * tig);
-      qa[kk][3] = *reinterpret_cast<const uint32_t*>(qh + swz128(rho1, c + 1) + 4 * tig);
-    }
-  }
-
-  int stage = 0;
-  uint32_t phase = 0;
-  for (int t = 0; t < ntiles && q_ok; ++t) {
-    if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), phase)) break;
-    const uint32_t sK0 = smem_u32(stage_mem + stage * kPrefillStageBytes);
-    const uint32_t sK1 = sK0 + kPrefillHalfKV;
-    const uint32_t sV0 = sK0 + 2 * kPrefillHalfKV;
-    const uint32_t sV1 = sK0 + 3 * kPrefillHalfKV;
-    const int tok0 = t * kPrefillKeyTile;
-
-    float sacc[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-#pragma unroll
-    for (int kp = 0; kp < 4; ++kp) {
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const uint32_t r = nt * 8 + (lane & 7);
-        const uint32_t c16 = kp * 4 + (lane >> 3);
-        const uint32_t addr = ((c16 < 8) ? sK0 : sK1) + swz128(r, c16 & 7u);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(addr, b0, b1, b2, b3);
-        mma_bf16_16816(sacc[nt], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0,
-                       b1);
-        mma_bf16_16816(sacc[nt], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2],
-                       qa[2 * kp + 1][3], b2, b3);
-      }
-    }
-    // masks: keys past Lk (last tile) and, with causal, past each row's limit
-    const bool need_mask =
-        (tok0 + kPrefillKeyTile > Lk) ||
-        (p.causal && tok0 + kPrefillKeyTile - 1 > shift + qs);
-    float pr[8][4];
-#pragma unroll
-    for (int rs = 0; rs < 2; ++rs) {
-      const int lim = rs ? lim1 : lim0;
-      float mx = NEG_INF;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float v = sacc[nt][2 * rs + e] * scale_log2;
-          if (need_mask) {
-            const int key = tok0 + nt * 8 + 2 * tig + e;
-            if (key >= Lk || (p.causal && key > lim)) v = NEG_INF;
+      mbar_arrive_expect_tx(smem_u32(q_full), 2u * QT * G * 128);
+      const uint64_t pol_q = l2_policy_evict_first();
+      tma_load_3d(qb, &tm_q, smem_u32(q_full), 0, kvh * G, q0 + qs, pol_q);
+      tma_load_3d(qb + kPrefillQHalf, &tm_q, smem_u32(q_full), 64, kvh * G, q0 + qs, pol_q);
+      const int sub = p.rows_per_load;
+      // per ring (0 = K, 1 = V): bit s set while stage s has a fill in
+      // flight, and the parity of that fill's full-barrier phase
+      uint32_t armed[2] = {0u, 0u}, parity[2] = {0u, 0u};
+      bool ok = true;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        for (int kv = 0; kv < 2; ++kv) {
+          const int stages = kv ? kPrefillVStages : kPrefillKStages;
+          const int s = t % stages;
+          const uint32_t ph = (t / stages) & 1;
+          uint64_t* emp = kv ? v_empty : k_empty;
+          uint64_t* ful = kv ? v_full : k_full;
+          if (!mbar_wait_bounded(smem_u32(&emp[s]), ph ^ 1u)) {
+            ok = false;
+            break;
           }
-          sacc[nt][2 * rs + e] = v;
-          mx = fmaxf(mx, v);
+          armed[kv] &= ~(1u << s);  // the stage's previous fill was consumed
+          const uint32_t fb = smem_u32(&ful[s]);
+          mbar_arrive_expect_tx(fb, kPrefillTileBytes);
+          armed[kv] |= 1u << s;
+          parity[kv] = (parity[kv] & ~(1u << s)) | (ph << s);
+          const uint32_t base = smem_u32((kv ? v_mem : k_mem) + s * kPrefillTileBytes);
+          const CUtensorMap* map = kv ? &tm_v : &tm_k;
+          for (int part = 0; part < kPrefillKeyTile; part += sub) {
+            const int tok = t * kPrefillKeyTile + part;
+            int row;
+            if (p.block_tables != nullptr) {
+              if (tok >= Lk) {
+                row = -2 * sub;  // wholly past the sequence: zero fill
+              } else {
+                const int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
+                                      tok / p.block_size);
+                if (blk < 0 || static_cast<int64_t>(blk) >= p.num_blocks) {
+                  raise_error(NKV_DEVERR_DECODE_BLOCK);
+                  row = -2 * sub;
+                } else {
+                  row = blk * p.block_size + (tok % p.block_size);
+                }
+              }
+            } else {
+              row = k0 + tok;
+            }
+            tma_load_3d_nohint(base + part * 128, map, fb, 0, kvh, row);
+            tma_load_3d_nohint(base + kPrefillHalf + part * 128, map, fb, 64, kvh, row);
+          }
         }
       }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run[rs], mx);
-      const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
-      const float alpha = fast_exp2(m_run[rs] - m_use);
-      m_run[rs] = m_new;
-      float rsum = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float pv = fast_exp2(sacc[nt][2 * rs + e] - m_use);
-          pr[nt][2 * rs + e] = pv;
-          rsum += pv;
+      // Fills still in flight (only after an abort) complete before exit.
+      for (int kv = 0; kv < 2; ++kv) {
+        uint64_t* ful = kv ? v_full : k_full;
+        for (int s = 0; s < kPrefillKStages; ++s)
+          if (armed[kv] & (1u << s)) mbar_wait_bounded(smem_u32(&ful[s]), (parity[kv] >> s) & 1u);
+      }
+      mbar_wait_bounded(smem_u32(q_full), 0);
+    }
+  } else if (warp == kPrefillMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = umma_idesc_bf16(128, kPrefillKeyTile, 0);
+    constexpr uint32_t idesc_o = umma_idesc_bf16(128, 128, 1);
+    const uint32_t q_base = smem_u32(q_mem);
+    bool ok = mbar_wait_bounded(smem_u32(q_full), 0);
+    for (int j = 0; j <= ntiles && ok; ++j) {
+      if (j < ntiles) {
+        const int ks = j % kPrefillKStages;
+        if (!mbar_wait_bounded(smem_u32(&k_full[ks]), (j / kPrefillKStages) & 1) ||
+            !mbar_wait_bounded(smem_u32(&s_free[j & 1]), ((j >> 1) & 1) ^ 1u)) {
+          ok = false;
+          break;
         }
-      }
-      l_run[rs] = l_run[rs] * alpha + rsum;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t kb = smem_u32(k_mem + ks * kPrefillTileBytes);
+          const uint32_t d = tmem + kTmemS0 + (j & 1) * kPrefillKeyTile;
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][2 * rs] *= alpha;
-        o[n][2 * rs + 1] *= alpha;
+          for (int kk = 0; kk < 8; ++kk) {
+            // K-major A (Q) and B (K): 16 dims per step, 32 bytes into the
+            // 128-byte swizzled rows of the half holding them; 8-row groups
+            // 1024 B apart (SBO).
+            const uint32_t qoff = (kk >> 2) * kPrefillQHalf + (kk & 3) * 32;
+            const uint32_t koff = (kk >> 2) * kPrefillHalf + (kk & 3) * 32;
+            umma_ss(d, umma_desc_sw128(q_base + qoff, 16, 1024),
+                    umma_desc_sw128(kb + koff, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&s_full[j & 1]));
+          umma_commit(smem_u32(&k_empty[ks]));
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        const int t = j - 1;
+        const int vs = t % kPrefillVStages;
+        if (!mbar_wait_bounded(smem_u32(p_full), t & 1) ||
+            !mbar_wait_bounded(smem_u32(&v_full[vs]), (t / kPrefillVStages) & 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* vt = v_mem + vs * kPrefillTileBytes;
+        const int valid = Lk - t * kPrefillKeyTile;
+        if (valid < kPrefillKeyTile) {
+          // V rows past the sequence may hold any bits (NaN included); their
+          // P is 0, so zero them rather than let 0 * NaN reach O.
+          const int nz = (kPrefillKeyTile - valid) * 8;  // 16-byte chunks per half
+          for (int c = lane; c < 2 * nz; c += 32) {
+            const int half = c / nz;
+            const int idx = c - half * nz;
+            *reinterpret_cast<uint4*>(vt + half * kPrefillHalf + valid * 128 + idx * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t vb = smem_u32(vt);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // B = V (K = keys, N = dims, MN-major): 16 keys per step, the
+            // dims 64..127 atom one half-tile further (LBO), 8-key groups
+            // 1024 B apart (SBO).
+            umma_ts(tmem + kTmemO, tmem + kTmemP + kk * 8,
+                    umma_desc_sw128(vb + kk * 2048, kPrefillHalf, 1024), idesc_o,
+                    (t > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&v_empty[vs]));
+          umma_commit(smem_u32(pv_done));
+        }
+        __syncwarp();
       }
     }
-    // O += P V over the tile's four 16-key k-steps. V rows past Lk are zeroed
-    // in registers so uninitialised cache bytes never meet a zero weight.
-    const bool tail = tok0 + kPrefillKeyTile > Lk;
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const uint32_t a0 = pack_bf16x2(pr[2 * jj][0], pr[2 * jj][1]);
-      const uint32_t a1 = pack_bf16x2(pr[2 * jj][2], pr[2 * jj][3]);
-      const uint32_t a2 = pack_bf16x2(pr[2 * jj + 1][0], pr[2 * jj + 1][1]);
-      const uint32_t a3 = pack_bf16x2(pr[2 * jj + 1][2], pr[2 * jj + 1][3]);
-      uint32_t mask_lo = 0xffffffffu, mask_hi = 0xffffffffu;
-      if (tail) {
-        const int ta = tok0 + 16 * jj + 2 * tig;
-        mask_lo = (ta < Lk ? 0x0000ffffu : 0u) | (ta + 1 < Lk ? 0xffff0000u : 0u);
-        mask_hi = (ta + 8 < Lk ? 0x0000ffffu : 0u) | (ta + 9 < Lk ? 0xffff0000u : 0u);
-      }
-      const int mi = lane >> 3;
-      const uint32_t r = 16 * jj + (mi & 1) * 8 + (lane & 7);
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        const uint32_t c16 = 2 * dp + (mi >> 1);
-        const uint32_t addr = ((c16 < 8) ? sV0 : sV1) + swz128(r, c16 & 7u);
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_trans(addr, v0, v1, v2, v3);
-        v0 &= mask_lo;
-        v2 &= mask_lo;
-        v1 &= mask_hi;
-        v3 &= mask_hi;
-        mma_bf16_16816(o[2 * dp], a0, a1, a2, a3, v0, v1);
-        mma_bf16_16816(o[2 * dp + 1], a0, a1, a2, a3, v2, v3);
-      }
-    }
+    // Every MMA this thread issued completes before the TMEM is released.
+    if (lane == 0) umma_commit(smem_u32(mma_done));
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&empty_bar[stage]));
-    if (++stage == kPrefillStages) {
-      stage = 0;
-      phase ^= 1u;
+    mbar_wait_bounded(smem_u32(mma_done), 0);
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int half = warp >> 2;                      // key / dim columns [64*half, +64)
+    const int row = quarter * 32 + lane;             // TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int qi = row / G;
+    const int r = row - qi * G;
+    const int lim = shift + qs + qi;
+    const float scale_log2 = p.scale_log2;
+    float m_used = -INFINITY;
+    float l_half = 0.f;  // row sum over this half's columns
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait_bounded(smem_u32(&s_full[j & 1]), (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[2][32];
+      const uint32_t sbase = tmem + lane_base + kTmemS0 + (j & 1) * kPrefillKeyTile + half * 64;
+      tmem_ld32(sbase, sv[0]);
+      tmem_ld32(sbase + 32, sv[1]);
+      tmem_ld_wait(sv[0]);
+      tmem_ld_wait(sv[1]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s_free[j & 1]));
+
+      const int tok0 = j * kPrefillKeyTile + half * 64;
+      const bool masked = (j * kPrefillKeyTile + kPrefillKeyTile > Lk) ||
+                          (p.causal && j * kPrefillKeyTile + kPrefillKeyTile - 1 > shift + qs);
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float v = __uint_as_float(sv[c][e]) * scale_log2;
+          if (masked) {
+            const int key = tok0 + 32 * c + e;
+            if (key >= Lk || (p.causal && key > lim)) v = -INFINITY;
+          }
+          sv[c][e] = __float_as_uint(v);
+          mx8[e & 7] = fmaxf(mx8[e & 7], v);
+        }
+      }
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      // exchange the half-row maxima (slots and barriers by tile parity; a
+      // slot is rewritten two tiles later, after its reader has arrived on
+      // the next tile's barrier)
+      mx = fmaxf(mx, exchange_half(red, red_bar, j, half, row, lane, mx));
+      const float m_new = fmaxf(m_used, mx);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m_used == -INFINITY) {
+        m_used = m_new;  // nothing accumulated yet (O and l are zero)
+      } else if (m_new > m_used + kRescaleThreshold) {
+        alpha = fast_exp2(m_used - m_new);
+        m_used = m_new;
+        rescale = true;
+      }
+      const float m_sub = (m_used == -INFINITY) ? 0.f : m_used;
+      uint32_t pk[32];
+      float rs8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = fast_exp2(__uint_as_float(sv[c][2 * e]) - m_sub);
+          const float p1 = fast_exp2(__uint_as_float(sv[c][2 * e + 1]) - m_sub);
+          rs8[e & 7] += p0 + p1;
+          pk[c * 16 + e] = pack_bf16x2(p0, p1);
+        }
+      }
+      const float rsum = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      l_half = l_half * alpha + rsum;
+      // P buffer free and O current once the previous PV has completed.
+      if (j > 0 && !mbar_wait_bounded(smem_u32(pv_done), (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t ov[32];
+          const uint32_t oa = tmem + lane_base + kTmemO + half * 64 + 32 * c;
+          tmem_ld32(oa, ov);
+          tmem_ld_wait(ov);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(oa, ov);
+        }
+      }
+      tmem_st32(tmem + lane_base + kTmemP + half * 32, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(p_full));
+    }
+    // ---------------------------------------------------------- epilogue
+    // whole-row sum from the two halves (slot parity of tile ntiles is free:
+    // its last readers passed the barrier of tile ntiles - 1)
+    const float l_run = l_half + exchange_half(red, red_bar, ntiles, half, row, lane, l_half);
+    const bool row_out = qi < qn;
+    __nv_bfloat16* dst = p.out + static_cast<int64_t>(q0 + qs + qi) * p.out_stride_token +
+                         static_cast<int64_t>(kvh * G + r) * 128 + half * 64;
+    if (ntiles == 0) {
+      if (row_out)
+        for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0u, 0u, 0u, 0u);
+    } else if (ok && mbar_wait_bounded(smem_u32(pv_done), (ntiles - 1) & 1)) {
+      tc_fence_after();
+      const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t ov[32];
+        tmem_ld32(tmem + lane_base + kTmemO + half * 64 + 32 * c, ov);
+        tmem_ld_wait(ov);
+        uint32_t pkd[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pkd[e] = pack_bf16x2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv);
+        if (row_out) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            d4[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2], pkd[4 * e + 3]);
+        }
+      }
     }
   }
 
-  // ---------------------------------------------------------------- epilogue
-#pragma unroll
-  for (int rs = 0; rs < 2; ++rs) {
-    float l = l_run[rs];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    const int qi = rs ? qi1 : qi0;
-    const int r = (rs ? rho1 : rho0) % G;
-    if (qi < qn) {
-      const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = p.out + static_cast<int64_t>(q0 + qs + qi) * p.out_stride_token +
-                           static_cast<int64_t>(kvh * G + r) * 128;
-#pragma unroll
-      for (int n = 0; n < 16; ++n)
-        *reinterpret_cast<uint32_t*>(dst + 8 * n + 2 * tig) =
-            pack_bf16x2(o[n][2 * rs] * inv, o[n][2 * rs + 1] * inv);
-    }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kPrefillMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPrefillTmemCols);
   }
 }
 
