@@ -657,7 +657,9 @@ def run_profile_case(kind: str) -> None:
     device, inputs larger than L2): `decode` runs the fused decode step (slot
     write + paged decode) on one layer of the first 64 config-2 sequences
     (Qwen3-8B shapes) 4 times;
-    `compress` runs one config-3 window-compression event 4 times."""
+    `compress` runs one config-3 window-compression event 4 times;
+    `prefill` runs one chunked-prefill attention launch (Qwen3-32B shapes,
+    4 x 2,048 queries over 10,240 keys) 4 times."""
     from nanokv_b200 import ops
 
     dev = torch.device("cuda", 0)
@@ -666,6 +668,24 @@ def run_profile_case(kind: str) -> None:
         for _ in range(4):
             measure_compress(dev, HQ, HK)
         torch.cuda.synchronize()
+        return
+    if kind == "prefill":
+        # 4 sequences of Qwen3-32B attention shapes: a 2,048-token causal
+        # chunk over an 8,192-token cached prefix (cache 168 MB, > L2)
+        hq, hk, B, chunk, prefix = 64, 8, 4, 2048, 8192
+        L = prefix + chunk
+        nb = B * L // BLOCK
+        perm = torch.randperm(nb, generator=torch.Generator().manual_seed(6)).view(B, -1)
+        bt = perm.to(torch.int32).to(dev)
+        kc = torch.empty(nb, BLOCK, hk, D, dtype=torch.bfloat16, device=dev).normal_()
+        vc = torch.empty_like(kc).normal_()
+        q = torch.randn(B * chunk, hq, D, device=dev).to(torch.bfloat16)
+        cu_q = (torch.arange(B + 1, dtype=torch.int32) * chunk).to(dev)
+        cu_k = (torch.arange(B + 1, dtype=torch.int32) * L).to(dev)
+        for _ in range(4):
+            ops.paged_prefill(q, kc, vc, cu_q, cu_k, chunk, D ** -0.5, block_table=bt)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": kind, "flops": prefill_flops([chunk] * B, [L] * B, hq)}))
         return
     lens = workload_lens()[:64]
     nblk = [(L + BLOCK - 1) // BLOCK for L in lens]
@@ -698,7 +718,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
-    ap.add_argument("--profile", choices=["decode", "compress"], default=None,
+    ap.add_argument("--profile", choices=["decode", "compress", "prefill"], default=None,
                     help="run a small case for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile:

@@ -170,6 +170,7 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
 /* Supported: head_dim 128, g = num_q_heads / num_kv_heads in [1, 128],      */
 /* block_size 64 or a multiple of 128, heads of k / v / out contiguous       */
 /* (stride D), out 16-byte aligned with out_stride_token a multiple of 8.    */
+/* softmax_scale must be finite and > 0.                                     */
 /* No workspace; nothing is allocated.                                       */
 int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                       int64_t num_q_tokens,

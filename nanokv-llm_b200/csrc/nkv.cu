@@ -475,9 +475,10 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
     return NKV_ERR_INVALID_ARGUMENT;
   if (batch == 0 || max_seqlen_q == 0 || num_q_tokens == 0) return NKV_OK;
   if (!q || !k || !v || !cu_seqlens_q || !cu_seqlens_k || !out) return NKV_ERR_INVALID_ARGUMENT;
-  if (!std::isfinite(softmax_scale)) return NKV_ERR_INVALID_ARGUMENT;
+  if (!std::isfinite(softmax_scale) || !(softmax_scale > 0.f)) return NKV_ERR_INVALID_ARGUMENT;
   const int g = num_q_heads / num_kv_heads;
-  if (head_dim != 128 || g > nkv::kPrefillRows || batch > 65535) return NKV_ERR_UNSUPPORTED;
+  if (head_dim != 128 || g > nkv::kPrefillRows || batch > 65535 || num_kv_heads > 65535)
+    return NKV_ERR_UNSUPPORTED;
   // A 128-key tile spans whole cache blocks (64-token blocks: two per tile)
   // or lies inside one (multiples of 128).
   if (block_tables != nullptr &&
@@ -485,7 +486,7 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
     return NKV_ERR_UNSUPPORTED;
   const int qt = nkv::kPrefillRows / g;
   const int64_t qtiles = (static_cast<int64_t>(max_seqlen_q) + qt - 1) / qt;
-  if (qtiles > 65535) return NKV_ERR_UNSUPPORTED;
+  if (qtiles > (1ll << 31) - 1) return NKV_ERR_UNSUPPORTED;
   const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
   if (k_stride_token < row || v_stride_token < row ||
       out_stride_token < static_cast<int64_t>(num_q_heads) * head_dim ||
@@ -541,7 +542,7 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_kv_heads, batch, static_cast<unsigned>(qtiles));
+  cfg.gridDim = dim3(static_cast<unsigned>(qtiles), num_kv_heads, batch);
   cfg.blockDim = dim3(nkv::kPrefillThreads, 1, 1);
   cfg.dynamicSmemBytes = nkv::kPrefillSmemBytes;
   cfg.stream = static_cast<cudaStream_t>(stream);

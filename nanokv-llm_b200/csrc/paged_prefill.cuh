@@ -10,8 +10,9 @@
 // cache (block_tables) or, without a block table, in rows cu_k[b] + j of
 // contiguous K/V tensors.
 //
-// One CTA per (kv head, sequence, q-tile); q-tiles run longest-first (grid z
-// reversed) to shorten the causal tail. A q-tile is the 128-row M side of
+// One CTA per (q-tile, kv head, sequence), q-tiles innermost so that the
+// CTAs resident at once share one sequence's K/V stream in L2, longest-first
+// (grid x reversed) to shorten the causal tail. A q-tile is the 128-row M side of
 // the tensor-core tiles: QT = floor(128/g) query positions x the g query
 // heads of the kv head's GQA group (row = i*g + r), so every K/V tile is
 // read once for the whole group.
@@ -136,9 +137,9 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
   const int lane = threadIdx.x & 31;
   const int G = p.g;
   const int QT = p.qt;
-  const int qtile = p.qtiles - 1 - static_cast<int>(blockIdx.z);
-  const int kvh = blockIdx.x;
-  const int b = blockIdx.y;
+  const int qtile = p.qtiles - 1 - static_cast<int>(blockIdx.x);
+  const int kvh = blockIdx.y;
+  const int b = blockIdx.z;
   const int q0 = __ldg(p.cu_q + b);
   const int Lq = __ldg(p.cu_q + b + 1) - q0;
   const int k0 = __ldg(p.cu_k + b);
@@ -149,7 +150,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
       (p.block_tables == nullptr ? (k0 < 0 || static_cast<int64_t>(k0) + Lk > p.num_kv_rows)
                                  : (static_cast<int64_t>(Lk) >
                                     static_cast<int64_t>(p.max_blocks) * p.block_size))) {
-    if (threadIdx.x == 0 && blockIdx.z == 0) raise_error(NKV_DEVERR_PREFILL_RANGE);
+    if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(NKV_DEVERR_PREFILL_RANGE);
     return;
   }
   const int qs = qtile * QT;  // first query position of this CTA
@@ -367,20 +368,26 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
       const int tok0 = j * kPrefillKeyTile + half * 64;
       const bool masked = (j * kPrefillKeyTile + kPrefillKeyTile > Lk) ||
                           (p.causal && j * kPrefillKeyTile + kPrefillKeyTile - 1 > shift + qs);
+      // Row maximum of the raw scores (the scale is positive): only diagonal
+      // and tail tiles take the masking path.
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+      if (masked) {
+        const int kmax = p.causal ? min(Lk - 1, lim) : Lk - 1;  // last admissible key
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 2; ++c) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float v = __uint_as_float(sv[c][e]) * scale_log2;
-          if (masked) {
-            const int key = tok0 + 32 * c + e;
-            if (key >= Lk || (p.causal && key > lim)) v = -INFINITY;
+          for (int e = 0; e < 32; ++e) {
+            if (tok0 + 32 * c + e > kmax) sv[c][e] = __float_as_uint(-INFINITY);
+            mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sv[c][e]));
           }
-          sv[c][e] = __float_as_uint(v);
-          mx8[e & 7] = fmaxf(mx8[e & 7], v);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sv[c][e]));
         }
       }
       float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
@@ -389,7 +396,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
       // slot is rewritten two tiles later, after its reader has arrived on
       // the next tile's barrier)
       mx = fmaxf(mx, exchange_half(red, red_bar, j, half, row, lane, mx));
-      const float m_new = fmaxf(m_used, mx);
+      const float m_new = fmaxf(m_used, mx * scale_log2);  // log2 units
       float alpha = 1.f;
       bool rescale = false;
       if (m_used == -INFINITY) {
@@ -399,7 +406,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
         m_used = m_new;
         rescale = true;
       }
-      const float m_sub = (m_used == -INFINITY) ? 0.f : m_used;
+      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
       uint32_t pk[32];
       float rs8[8];
 #pragma unroll
@@ -408,8 +415,8 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(__uint_as_float(sv[c][2 * e]) - m_sub);
-          const float p1 = fast_exp2(__uint_as_float(sv[c][2 * e + 1]) - m_sub);
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][2 * e]), scale_log2, neg_m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][2 * e + 1]), scale_log2, neg_m));
           rs8[e & 7] += p0 + p1;
           pk[c * 16 + e] = pack_bf16x2(p0, p1);
         }

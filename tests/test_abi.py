@@ -80,3 +80,4 @@ def test_prefill_argument_errors_need_no_gpu():
     assert call(ost=2048) == 1                  # out rows too short for Hq heads
     assert call(b=0) == 0 and call(mq=0) == 0   # empty batch is a no-op
     assert call(scale=float("inf")) == 1
+    assert call(scale=-0.1) == 1
