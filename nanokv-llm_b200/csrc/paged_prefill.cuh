@@ -18,9 +18,11 @@
 // read once for the whole group.
 //
 // Fifth-generation tensor cores (tcgen05), all accumulators in TMEM:
-//   * warp 9, producer: TMA-loads the q-tile, then 128-key K and V tiles
-//     (128-byte swizzle, no multicast) into a 3-deep K ring and a 2-deep V
-//     ring; a tile is cut at cache-block boundaries when blocks hold < 128.
+//   * warps 9 and 10, producers: TMA-load the q-tile and the 128-key K
+//     tiles (warp 9) and the V tiles (warp 10), 128-byte swizzle, no
+//     multicast, into a 3-deep K ring and a 2-deep V ring; the two rings
+//     refill independently (K as soon as its S MMA is done, V after its PV
+//     MMA). A tile is cut at cache-block boundaries when blocks hold < 128.
 //   * warp 8, MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
 //     S buffers (8 x UMMA 128x128x16, A and B from shared memory), then
 //     O += P_{j-1} V_{j-1} (A = P from TMEM, B = V MN-major from shared
@@ -47,9 +49,9 @@ constexpr int kPrefillRows = 128;      // M: rows (query x head) per CTA
 constexpr int kPrefillKeyTile = 128;   // N of S / K of PV: keys per tile
 constexpr int kPrefillKStages = 3;
 constexpr int kPrefillVStages = 2;
-constexpr int kPrefillThreads = 320;   // 8 softmax warps, MMA warp, producer warp
+constexpr int kPrefillThreads = 352;   // 8 softmax warps, MMA warp, K and V producer warps
 constexpr int kPrefillMmaWarp = 8;
-constexpr int kPrefillProducerWarp = 9;
+constexpr int kPrefillProducerWarp = 9;  // Q and K; warp 10 loads V
 constexpr int kPrefillHalf = kPrefillKeyTile * 128;   // 64 dims x 128 keys x 2 B
 constexpr int kPrefillTileBytes = 2 * kPrefillHalf;   // one K or V tile, 32 KB
 constexpr int kPrefillQHalf = kPrefillRows * 128;
@@ -192,71 +194,65 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
   const uint32_t tmem = *tmem_slot;
   grid_dependency_wait();
 
-  if (warp == kPrefillProducerWarp) {
-    // ------------------------------------------------------------ producer
+  if (warp >= kPrefillProducerWarp) {
+    // ------------------------------------------------------------ producers
+    const int kv = warp - kPrefillProducerWarp;  // 0: Q + K, 1: V
     if (lane == 0) {
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
-      prefetch_tmap(&tm_q);
-      const uint32_t qb = smem_u32(q_mem);
-      mbar_arrive_expect_tx(smem_u32(q_full), 2u * QT * G * 128);
-      const uint64_t pol_q = l2_policy_evict_first();
-      tma_load_3d(qb, &tm_q, smem_u32(q_full), 0, kvh * G, q0 + qs, pol_q);
-      tma_load_3d(qb + kPrefillQHalf, &tm_q, smem_u32(q_full), 64, kvh * G, q0 + qs, pol_q);
+      const CUtensorMap* map = kv ? &tm_v : &tm_k;
+      prefetch_tmap(map);
+      if (kv == 0) {
+        prefetch_tmap(&tm_q);
+        const uint32_t qb = smem_u32(q_mem);
+        mbar_arrive_expect_tx(smem_u32(q_full), 2u * QT * G * 128);
+        const uint64_t pol_q = l2_policy_evict_first();
+        tma_load_3d(qb, &tm_q, smem_u32(q_full), 0, kvh * G, q0 + qs, pol_q);
+        tma_load_3d(qb + kPrefillQHalf, &tm_q, smem_u32(q_full), 64, kvh * G, q0 + qs, pol_q);
+      }
       const int sub = p.rows_per_load;
-      // per ring (0 = K, 1 = V): bit s set while stage s has a fill in
-      // flight, and the parity of that fill's full-barrier phase
-      uint32_t armed[2] = {0u, 0u}, parity[2] = {0u, 0u};
-      bool ok = true;
-      for (int t = 0; t < ntiles && ok; ++t) {
-        for (int kv = 0; kv < 2; ++kv) {
-          const int stages = kv ? kPrefillVStages : kPrefillKStages;
-          const int s = t % stages;
-          const uint32_t ph = (t / stages) & 1;
-          uint64_t* emp = kv ? v_empty : k_empty;
-          uint64_t* ful = kv ? v_full : k_full;
-          if (!mbar_wait_bounded(smem_u32(&emp[s]), ph ^ 1u)) {
-            ok = false;
-            break;
-          }
-          armed[kv] &= ~(1u << s);  // the stage's previous fill was consumed
-          const uint32_t fb = smem_u32(&ful[s]);
-          mbar_arrive_expect_tx(fb, kPrefillTileBytes);
-          armed[kv] |= 1u << s;
-          parity[kv] = (parity[kv] & ~(1u << s)) | (ph << s);
-          const uint32_t base = smem_u32((kv ? v_mem : k_mem) + s * kPrefillTileBytes);
-          const CUtensorMap* map = kv ? &tm_v : &tm_k;
-          for (int part = 0; part < kPrefillKeyTile; part += sub) {
-            const int tok = t * kPrefillKeyTile + part;
-            int row;
-            if (p.block_tables != nullptr) {
-              if (tok >= Lk) {
-                row = -2 * sub;  // wholly past the sequence: zero fill
-              } else {
-                const int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
-                                      tok / p.block_size);
-                if (blk < 0 || static_cast<int64_t>(blk) >= p.num_blocks) {
-                  raise_error(NKV_DEVERR_DECODE_BLOCK);
-                  row = -2 * sub;
-                } else {
-                  row = blk * p.block_size + (tok % p.block_size);
-                }
-              }
+      const int stages = kv ? kPrefillVStages : kPrefillKStages;
+      uint64_t* emp = kv ? v_empty : k_empty;
+      uint64_t* ful = kv ? v_full : k_full;
+      uint8_t* ring = kv ? v_mem : k_mem;
+      // bit s set while stage s has a fill in flight, with that fill's
+      // full-barrier parity
+      uint32_t armed = 0u, parity = 0u;
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % stages;
+        const uint32_t ph = (t / stages) & 1;
+        if (!mbar_wait_bounded(smem_u32(&emp[s]), ph ^ 1u)) break;
+        armed &= ~(1u << s);  // the stage's previous fill was consumed
+        const uint32_t fb = smem_u32(&ful[s]);
+        mbar_arrive_expect_tx(fb, kPrefillTileBytes);
+        armed |= 1u << s;
+        parity = (parity & ~(1u << s)) | (ph << s);
+        const uint32_t base = smem_u32(ring + s * kPrefillTileBytes);
+        for (int part = 0; part < kPrefillKeyTile; part += sub) {
+          const int tok = t * kPrefillKeyTile + part;
+          int row;
+          if (p.block_tables != nullptr) {
+            if (tok >= Lk) {
+              row = -2 * sub;  // wholly past the sequence: zero fill
             } else {
-              row = k0 + tok;
+              const int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
+                                    tok / p.block_size);
+              if (blk < 0 || static_cast<int64_t>(blk) >= p.num_blocks) {
+                raise_error(NKV_DEVERR_DECODE_BLOCK);
+                row = -2 * sub;
+              } else {
+                row = blk * p.block_size + (tok % p.block_size);
+              }
             }
-            tma_load_3d_nohint(base + part * 128, map, fb, 0, kvh, row);
-            tma_load_3d_nohint(base + kPrefillHalf + part * 128, map, fb, 64, kvh, row);
+          } else {
+            row = k0 + tok;
           }
+          tma_load_3d_nohint(base + part * 128, map, fb, 0, kvh, row);
+          tma_load_3d_nohint(base + kPrefillHalf + part * 128, map, fb, 64, kvh, row);
         }
       }
       // Fills still in flight (only after an abort) complete before exit.
-      for (int kv = 0; kv < 2; ++kv) {
-        uint64_t* ful = kv ? v_full : k_full;
-        for (int s = 0; s < kPrefillKStages; ++s)
-          if (armed[kv] & (1u << s)) mbar_wait_bounded(smem_u32(&ful[s]), (parity[kv] >> s) & 1u);
-      }
-      mbar_wait_bounded(smem_u32(q_full), 0);
+      for (int s = 0; s < stages; ++s)
+        if (armed & (1u << s)) mbar_wait_bounded(smem_u32(&ful[s]), (parity >> s) & 1u);
+      if (kv == 0) mbar_wait_bounded(smem_u32(q_full), 0);
     }
   } else if (warp == kPrefillMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
