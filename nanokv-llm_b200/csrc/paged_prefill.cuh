@@ -38,7 +38,12 @@
 //     stale-maximum probabilities stay <= 256), P packed to bf16 into TMEM;
 //     row sums stay per half until the epilogue O / l -> bf16 -> the query
 //     rows that exist.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,384), P [384,448).
+//   The q-tile is moved once from shared memory into TMEM (bf16 pairs, as
+//   P), so the S MMAs take A from TMEM and shared memory only feeds K and V
+//   to the tensor core (with A and B both in shared memory the S MMA would
+//   be bound by shared-memory bandwidth).
+// TMEM columns: S0 [0,128), S1 [128,256), O [256,384), P [384,448),
+// Q [448,512).
 #pragma once
 #include "nkv_common.cuh"
 #include "tcgen05.cuh"
@@ -55,13 +60,13 @@ constexpr int kPrefillProducerWarp = 9;  // Q and K; warp 10 loads V
 constexpr int kPrefillHalf = kPrefillKeyTile * 128;   // 64 dims x 128 keys x 2 B
 constexpr int kPrefillTileBytes = 2 * kPrefillHalf;   // one K or V tile, 32 KB
 constexpr int kPrefillQHalf = kPrefillRows * 128;
-constexpr int kPrefillNumBars = 20;
+constexpr int kPrefillNumBars = 21;
 constexpr int kPrefillRedBytes = 2 * 2 * kPrefillRows * 4;  // [parity][half][row] floats
 constexpr int kPrefillSmemBytes = 2 * kPrefillQHalf +
                                   (kPrefillKStages + kPrefillVStages) * kPrefillTileBytes + 256 +
                                   kPrefillRedBytes + 1024 /* alignment */;
 constexpr uint32_t kPrefillTmemCols = 512;
-constexpr uint32_t kTmemS0 = 0, kTmemO = 256, kTmemP = 384;
+constexpr uint32_t kTmemS0 = 0, kTmemO = 256, kTmemP = 384, kTmemQ = 448;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
@@ -110,6 +115,32 @@ __device__ __forceinline__ float exchange_half(float* red, uint64_t* red_bar, in
   return slot[(half ^ 1) * kPrefillRows + row];
 }
 
+// ------------------------------------------------------------- paired fp32
+// sm_100 executes two fp32 lanes per instruction on .b64 register pairs.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __global__ void __launch_bounds__(kPrefillThreads, 1)
 paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
@@ -132,6 +163,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
   uint64_t* pv_done = p_full + 1;                // 1
   uint64_t* mma_done = pv_done + 1;              // 1
   uint64_t* red_bar = mma_done + 1;              // 2: half-row exchange, by tile parity
+  uint64_t* q_tmem = red_bar + 2;                // 1: q-tile copied into TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kPrefillNumBars);
   float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
@@ -182,6 +214,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
     mbar_init(smem_u32(mma_done), 1);
     mbar_init(smem_u32(&red_bar[0]), 8);
     mbar_init(smem_u32(&red_bar[1]), 8);
+    mbar_init(smem_u32(q_tmem), 8);
     fence_barrier_init();
   }
   if (warp == kPrefillMmaWarp) {
@@ -258,8 +291,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_s = umma_idesc_bf16(128, kPrefillKeyTile, 0);
     constexpr uint32_t idesc_o = umma_idesc_bf16(128, 128, 1);
-    const uint32_t q_base = smem_u32(q_mem);
-    bool ok = mbar_wait_bounded(smem_u32(q_full), 0);
+    bool ok = mbar_wait_bounded(smem_u32(q_tmem), 0);
     for (int j = 0; j <= ntiles && ok; ++j) {
       if (j < ntiles) {
         const int ks = j % kPrefillKStages;
@@ -274,13 +306,12 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
           const uint32_t d = tmem + kTmemS0 + (j & 1) * kPrefillKeyTile;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            // K-major A (Q) and B (K): 16 dims per step, 32 bytes into the
-            // 128-byte swizzled rows of the half holding them; 8-row groups
-            // 1024 B apart (SBO).
-            const uint32_t qoff = (kk >> 2) * kPrefillQHalf + (kk & 3) * 32;
+            // A = Q from TMEM (16 dims = 8 columns per step); B = K, K-major:
+            // 16 dims per step, 32 bytes into the 128-byte swizzled rows of
+            // the half holding them, 8-row groups 1024 B apart (SBO).
             const uint32_t koff = (kk >> 2) * kPrefillHalf + (kk & 3) * 32;
-            umma_ss(d, umma_desc_sw128(q_base + qoff, 16, 1024),
-                    umma_desc_sw128(kb + koff, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+            umma_ts(d, tmem + kTmemQ + kk * 8, umma_desc_sw128(kb + koff, 16, 1024), idesc_s,
+                    kk > 0 ? 1u : 0u);
           }
           umma_commit(smem_u32(&s_full[j & 1]));
           umma_commit(smem_u32(&k_empty[ks]));
@@ -344,8 +375,27 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
     const float scale_log2 = p.scale_log2;
     float m_used = -INFINITY;
     float l_half = 0.f;  // row sum over this half's columns
-    bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
+    // q-tile -> TMEM: this thread's row, dims [64*half, +64) from the
+    // swizzled shared-memory half, as 32 columns of bf16 pairs
+    bool ok = mbar_wait_bounded(smem_u32(q_full), 0);
+    {
+      uint32_t qv[32];
+      const uint8_t* qh = q_mem + half * kPrefillQHalf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(qh + swz128(row, c));
+        qv[4 * c] = v.x;
+        qv[4 * c + 1] = v.y;
+        qv[4 * c + 2] = v.z;
+        qv[4 * c + 3] = v.w;
+      }
+      tmem_st32(tmem + lane_base + kTmemQ + half * 32, qv);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(q_tmem));
+    }
+    for (int j = 0; j < ntiles && ok; ++j) {
       if (!mbar_wait_bounded(smem_u32(&s_full[j & 1]), (j >> 1) & 1)) {
         ok = false;
         break;
@@ -403,21 +453,31 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
         rescale = true;
       }
       const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t nm2 = f2_pack(neg_m, neg_m);
       uint32_t pk[32];
-      float rs8[8];
+      uint64_t rs2[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
+      for (int e = 0; e < 4; ++e) rs2[e] = 0ull;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][2 * e]), scale_log2, neg_m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][2 * e + 1]), scale_log2, neg_m));
-          rs8[e & 7] += p0 + p1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][2 * e]), __uint_as_float(sv[c][2 * e + 1])),
+                           sc2, nm2), x0, x1);
+          const float p0 = fast_exp2(x0);
+          const float p1 = fast_exp2(x1);
+          rs2[e & 3] = f2_add(rs2[e & 3], f2_pack(p0, p1));
           pk[c * 16 + e] = pack_bf16x2(p0, p1);
         }
       }
-      const float rsum = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      float r0, r1, r2, r3, r4, r5, r6, r7;
+      f2_unpack(rs2[0], r0, r1);
+      f2_unpack(rs2[1], r2, r3);
+      f2_unpack(rs2[2], r4, r5);
+      f2_unpack(rs2[3], r6, r7);
+      const float rsum = ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7));
       l_half = l_half * alpha + rsum;
       // P buffer free and O current once the previous PV has completed.
       if (j > 0 && !mbar_wait_bounded(smem_u32(pv_done), (j - 1) & 1)) {
