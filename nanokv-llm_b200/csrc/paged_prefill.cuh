@@ -20,7 +20,8 @@
 // Fifth-generation tensor cores (tcgen05), all accumulators in TMEM:
 //   * warps 9 and 10, producers: TMA-load the q-tile and the 128-key K
 //     tiles (warp 9) and the V tiles (warp 10), 128-byte swizzle, no
-//     multicast, into a 3-deep K ring and a 2-deep V ring; the two rings
+//     multicast, into a 4-deep K ring (its last stage is the q-tile buffer,
+//     reused once Q has moved to TMEM) and a 2-deep V ring; the two rings
 //     refill independently (K as soon as its S MMA is done, V after its PV
 //     MMA). A tile is cut at cache-block boundaries when blocks hold < 128.
 //   * warp 8, MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
@@ -52,7 +53,8 @@ namespace nkv {
 
 constexpr int kPrefillRows = 128;      // M: rows (query x head) per CTA
 constexpr int kPrefillKeyTile = 128;   // N of S / K of PV: keys per tile
-constexpr int kPrefillKStages = 3;
+constexpr int kPrefillKStages = 4;     // K ring depth; its last stage reuses the q-tile buffer
+constexpr int kPrefillKSmemStages = kPrefillKStages - 1;
 constexpr int kPrefillVStages = 2;
 constexpr int kPrefillThreads = 352;   // 8 softmax warps, MMA warp, K and V producer warps
 constexpr int kPrefillMmaWarp = 8;
@@ -60,10 +62,10 @@ constexpr int kPrefillProducerWarp = 9;  // Q and K; warp 10 loads V
 constexpr int kPrefillHalf = kPrefillKeyTile * 128;   // 64 dims x 128 keys x 2 B
 constexpr int kPrefillTileBytes = 2 * kPrefillHalf;   // one K or V tile, 32 KB
 constexpr int kPrefillQHalf = kPrefillRows * 128;
-constexpr int kPrefillNumBars = 21;
+constexpr int kPrefillNumBars = 23;
 constexpr int kPrefillRedBytes = 2 * 2 * kPrefillRows * 4;  // [parity][half][row] floats
 constexpr int kPrefillSmemBytes = 2 * kPrefillQHalf +
-                                  (kPrefillKStages + kPrefillVStages) * kPrefillTileBytes + 256 +
+                                  (kPrefillKSmemStages + kPrefillVStages) * kPrefillTileBytes + 256 +
                                   kPrefillRedBytes + 1024 /* alignment */;
 constexpr uint32_t kPrefillTmemCols = 512;
 constexpr uint32_t kTmemS0 = 0, kTmemO = 256, kTmemP = 384, kTmemQ = 448;
@@ -141,6 +143,11 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   return d;
 }
 
+// Shared-memory address of K stage s (the last one is the q-tile buffer).
+__device__ __forceinline__ uint8_t* k_stage(uint8_t* k_mem, uint8_t* q_mem, int s) {
+  return s < kPrefillKSmemStages ? k_mem + s * kPrefillTileBytes : q_mem;
+}
+
 __global__ void __launch_bounds__(kPrefillThreads, 1)
 paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
@@ -150,11 +157,11 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* q_mem = smem;  // Q lo, Q hi
   uint8_t* k_mem = smem + 2 * kPrefillQHalf;
-  uint8_t* v_mem = k_mem + kPrefillKStages * kPrefillTileBytes;
+  uint8_t* v_mem = k_mem + kPrefillKSmemStages * kPrefillTileBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(v_mem + kPrefillVStages * kPrefillTileBytes);
   uint64_t* q_full = bars;                       // 1
-  uint64_t* k_full = bars + 1;                   // 3
-  uint64_t* k_empty = k_full + kPrefillKStages;  // 3
+  uint64_t* k_full = bars + 1;                   // 4
+  uint64_t* k_empty = k_full + kPrefillKStages;  // 4
   uint64_t* v_full = k_empty + kPrefillKStages;  // 2
   uint64_t* v_empty = v_full + kPrefillVStages;  // 2
   uint64_t* s_full = v_empty + kPrefillVStages;  // 2
@@ -245,7 +252,6 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
       const int stages = kv ? kPrefillVStages : kPrefillKStages;
       uint64_t* emp = kv ? v_empty : k_empty;
       uint64_t* ful = kv ? v_full : k_full;
-      uint8_t* ring = kv ? v_mem : k_mem;
       // bit s set while stage s has a fill in flight, with that fill's
       // full-barrier parity
       uint32_t armed = 0u, parity = 0u;
@@ -253,12 +259,15 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
         const int s = t % stages;
         const uint32_t ph = (t / stages) & 1;
         if (!mbar_wait_bounded(smem_u32(&emp[s]), ph ^ 1u)) break;
+        // the last K stage is the q-tile buffer: free once Q is in TMEM
+        if (kv == 0 && t == kPrefillKSmemStages && !mbar_wait_bounded(smem_u32(q_tmem), 0)) break;
         armed &= ~(1u << s);  // the stage's previous fill was consumed
         const uint32_t fb = smem_u32(&ful[s]);
         mbar_arrive_expect_tx(fb, kPrefillTileBytes);
         armed |= 1u << s;
         parity = (parity & ~(1u << s)) | (ph << s);
-        const uint32_t base = smem_u32(ring + s * kPrefillTileBytes);
+        const uint32_t base =
+            smem_u32(kv ? v_mem + s * kPrefillTileBytes : k_stage(k_mem, q_mem, s));
         for (int part = 0; part < kPrefillKeyTile; part += sub) {
           const int tok = t * kPrefillKeyTile + part;
           int row;
@@ -302,7 +311,7 @@ paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_k,
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t kb = smem_u32(k_mem + ks * kPrefillTileBytes);
+          const uint32_t kb = smem_u32(k_stage(k_mem, q_mem, ks));
           const uint32_t d = tmem + kTmemS0 + (j & 1) * kPrefillKeyTile;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
