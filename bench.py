@@ -297,7 +297,8 @@ def run_gpu(args, rank, world, dev):
     lens = st["lens"]
     del kv, st, layers
     torch.cuda.empty_cache()
-    extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world)}
+    extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world),
+             "config4_prefill": measure_prefill(dev, world)}
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e_ms, statistics.mean(dec_ms)], dtype=torch.float64, device=dev)
@@ -547,6 +548,10 @@ def measure_prefill(dev, world, compare_flash_attn: bool = True):
            "layer_ms_all_chunks": round(t_step * 1e3, 3),
            "prefill_tok_per_s": round(B * Lctx / (t_step * 64), 1),
            "attn_TFLOPs": round(flops / t_attn / 1e12, 1)}
+    peak, src = read_bf16_peak()
+    res["roofline"] = {"bound": "tensor", "achieved": res["attn_TFLOPs"], "peak": peak,
+                       "unit": "TFLOP/s", "frac": round(res["attn_TFLOPs"] / peak, 4),
+                       "peak_source": f"{src} bf16_tflops (burst)"}
     if compare_flash_attn:
         try:
             from flash_attn import flash_attn_varlen_func
@@ -636,6 +641,14 @@ def read_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def read_bf16_peak():
+    """Dense bf16 TFLOP/s of this pool's B200s (cuBLAS burst), measured."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def read_traffic_bytes_per_launch(world: int):
