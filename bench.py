@@ -298,7 +298,8 @@ def run_gpu(args, rank, world, dev):
     del kv, st, layers
     torch.cuda.empty_cache()
     extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world),
-             "config4_prefill": measure_prefill(dev, world)}
+             "config4_prefill": measure_prefill(dev, world),
+             "qk_norm_rope_store": measure_norm_rope(dev, world)}
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e_ms, statistics.mean(dec_ms)], dtype=torch.float64, device=dev)
@@ -566,6 +567,67 @@ def measure_prefill(dev, world, compare_flash_attn: bool = True):
         t_fa = timed(fa)
         res["flash_attn_TFLOPs"] = round(flops / t_fa / 1e12, 1)
         res["attn_speedup_vs_flash_attn"] = round(t_fa / t_attn, 3)
+    return res
+
+
+def measure_norm_rope(dev, world):
+    """q/k RMSNorm + RoPE + slot write of one layer (nkv_qk_norm_rope_store)
+    against the same math as separate eager torch ops (the reference modules'
+    sequence, qwen3.py:109-113, then the slot write), on config 2's decode step (256
+    tokens of Qwen3-8B heads) and on a 2,048-token x 16 prefill chunk of
+    Qwen3-32B heads. HBM bytes = qkv read + q written + k, v slots written."""
+    from nanokv_b200 import ops
+
+    def rms_norm(x, w, eps):  # the reference module's ops (layernorm.py:16-25), eager
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)).to(x.dtype) * w
+
+    def rope(x, pos, cs):  # rotary_embedding.py:7-15, 37-45, eager
+        c, s_ = cs[pos].unsqueeze(1).chunk(2, dim=-1)
+        x1, x2 = torch.chunk(x.float(), 2, dim=-1)
+        return torch.cat((x1 * c - x2 * s_, x2 * c + x1 * s_), dim=-1).to(x.dtype)
+
+    res = {}
+    for name, T, hq, hk in (("decode_config2", 256, HQ // world, HK // world),
+                            ("prefill_config4", 16 * 2048, 64 // world, 8 // world)):
+        g = torch.Generator(device=dev).manual_seed(7)
+        qkv = torch.randn(T, (hq + 2 * hk) * D, device=dev, generator=g).to(torch.bfloat16)
+        pos = torch.randint(0, 32768, (T,), device=dev, generator=g)
+        cs = torch.randn(40960, D, device=dev, generator=g)
+        qw = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        kw = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        nslots = T * 2
+        kc = torch.empty(nslots // BLOCK, BLOCK, hk, D, device=dev, dtype=torch.bfloat16)
+        vc = torch.empty_like(kc)
+        sm = torch.randperm(nslots, device=dev, generator=g)[:T].to(torch.int32)
+        q_out = torch.empty(T, hq, D, device=dev, dtype=torch.bfloat16)
+
+        def fused():
+            ops.qk_norm_rope_store(qkv, pos, cs, qw, kw, 1e-6, hq, hk, k_cache=kc, v_cache=vc,
+                                   slot_mapping=sm, q_out=q_out)
+
+        def torch_ops():
+            q, k, v = qkv.split([hq * D, hk * D, hk * D], dim=-1)
+            q = rope(rms_norm(q.view(T, hq, D), qw, 1e-6), pos, cs)
+            k = rope(rms_norm(k.view(T, hk, D), kw, 1e-6), pos, cs)
+            ops.store_kvcache(k, v.view(T, hk, D), kc, vc, sm)
+
+        def timed(fn, n=20):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                fn()
+            b.record()
+            torch.cuda.synchronize(dev)
+            return a.elapsed_time(b) / n * 1e3
+
+        t_f, t_t = timed(fused), timed(torch_ops)
+        nbytes = T * (hq + 2 * hk) * D * 2 + T * hq * D * 2 + T * 2 * hk * D * 2
+        res[name] = {"tokens": T, "fused_us": round(t_f, 1), "torch_ops_us": round(t_t, 1),
+                     "speedup": round(t_t / t_f, 2), "fused_GBps": round(nbytes / t_f / 1e3, 1)}
     return res
 
 

@@ -54,6 +54,7 @@ typedef enum nkv_status {
 #define NKV_DEVERR_COMPRESS_RANGE  0x8u  /* compression window or slot outside the cache */
 #define NKV_DEVERR_RING_RANGE      0x10u /* query-window ring slot / position out of range */
 #define NKV_DEVERR_PREFILL_RANGE   0x20u /* cu_seqlens / max_seqlen_q outside the tensors or the grid */
+#define NKV_DEVERR_ROPE_POSITION   0x40u /* position outside the rotary cos/sin cache (clamped) */
 
 /* Human-readable name of a status code (static string). */
 const char* nkv_status_string(int status);
@@ -182,6 +183,37 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
                       void* out, int64_t out_stride_token,
                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                       float softmax_scale, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 2d. q/k RMSNorm + rotary embedding + slot write (one launch)             */
+/* Replaces the per-layer sequence q_norm / k_norm / rotary_emb of          */
+/*   nanokvllm/models/qwen3.py:109-113 and store_kvcache of                  */
+/*   nanokvllm/layers/attention.py:72-73.                                    */
+/* qkv: the qkv projection output [num_tokens, (Hq + 2 Hk) * head_dim] bf16 */
+/* (row stride qkv_stride_token). For token t and head h:                   */
+/*   q heads: q_out[t, h] = rope(rmsnorm(q[t, h]) * q_norm_weight)           */
+/*   k heads: k = rope(rmsnorm(k[t, h]) * k_norm_weight), written to          */
+/*            k_cache[slot_mapping[t], h] (and to k_out[t, h] if k_out is     */
+/*            not NULL); v[t, h] is copied to v_cache[slot_mapping[t], h].    */
+/* slot_mapping[t] == -1 skips the cache writes (graph padding); k_cache may */
+/* be NULL (no cache yet, as the reference's warm-up). RMSNorm: fp32 mean of */
+/* squares, bf16(x * rsqrt(var + eps)) * weight rounded to bf16 (the        */
+/* reference module's rounding points, layers/layernorm.py:16-25). RoPE:     */
+/* rotate-half with cos / sin from cos_sin_cache[positions[t]]               */
+/* ([max_positions, head_dim] fp32: cos then sin, rotary_embedding.py:7-45). */
+/* Positions outside the cache are clamped and flag NKV_DEVERR_ROPE_POSITION;*/
+/* slots >= num_slots are not written and flag NKV_DEVERR_STORE_SLOT.       */
+/* Supported: head_dim 128; bf16 rows 4-byte aligned with even strides.      */
+int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t num_tokens,
+                           const int64_t* positions, const float* cos_sin_cache,
+                           int64_t max_positions, const void* q_norm_weight,
+                           const void* k_norm_weight, float eps,
+                           void* q_out, int64_t q_out_stride_token,
+                           void* k_out, int64_t k_out_stride_token,
+                           void* k_cache, void* v_cache, int64_t num_slots,
+                           const int32_t* slot_mapping,
+                           int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                           void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 3a. Periodic window compression (one layer, all selected sequences)       */

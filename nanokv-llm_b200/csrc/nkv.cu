@@ -15,6 +15,7 @@
 #include "nkv_common.cuh"
 #include "paged_decode.cuh"
 #include "paged_prefill.cuh"
+#include "qk_norm_rope.cuh"
 #include "store_kvcache.cuh"
 #include "threshold_compress.cuh"
 #include "window_compress.cuh"
@@ -460,6 +461,62 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
                            block_tables, max_blocks, context_lens, out, out_stride_token, batch,
                            num_q_heads, num_kv_heads, head_dim, block_size, softmax_scale,
                            workspace, workspace_bytes, stream, &f);
+}
+
+// ---------------------------------------------------------------- q/k norm + RoPE + store
+int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t num_tokens,
+                           const int64_t* positions, const float* cos_sin_cache,
+                           int64_t max_positions, const void* q_norm_weight,
+                           const void* k_norm_weight, float eps, void* q_out,
+                           int64_t q_out_stride_token, void* k_out, int64_t k_out_stride_token,
+                           void* k_cache, void* v_cache, int64_t num_slots,
+                           const int32_t* slot_mapping, int32_t num_q_heads, int32_t num_kv_heads,
+                           int32_t head_dim, void* stream) {
+  if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_positions <= 0 ||
+      num_slots < 0)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return NKV_OK;
+  if (head_dim != 128) return NKV_ERR_UNSUPPORTED;
+  if (!qkv || !positions || !cos_sin_cache || !q_norm_weight || !k_norm_weight || !q_out)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (k_cache && (!v_cache || !slot_mapping)) return NKV_ERR_INVALID_ARGUMENT;
+  if (!(eps >= 0.f) || !std::isfinite(eps)) return NKV_ERR_INVALID_ARGUMENT;
+  const int64_t heads = static_cast<int64_t>(num_q_heads) + 2 * num_kv_heads;
+  if (qkv_stride_token < heads * head_dim || q_out_stride_token < int64_t(num_q_heads) * head_dim ||
+      (k_out && k_out_stride_token < int64_t(num_kv_heads) * head_dim))
+    return NKV_ERR_INVALID_ARGUMENT;
+  auto a4 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3u) == 0; };
+  if (!a4(qkv) || !a4(q_out) || !a4(q_norm_weight) || !a4(k_norm_weight) ||
+      (k_out && !a4(k_out)) || (k_cache && (!a4(k_cache) || !a4(v_cache))) ||
+      (reinterpret_cast<uintptr_t>(cos_sin_cache) & 7u) || (qkv_stride_token & 1) ||
+      (q_out_stride_token & 1) || (k_out && (k_out_stride_token & 1)))
+    return NKV_ERR_ALIGNMENT;
+  nkv::NormRopeParams p{};
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.qkv_stride = qkv_stride_token;
+  p.positions = positions;
+  p.cos_sin = cos_sin_cache;
+  p.max_positions = max_positions;
+  p.q_weight = static_cast<const __nv_bfloat16*>(q_norm_weight);
+  p.k_weight = static_cast<const __nv_bfloat16*>(k_norm_weight);
+  p.eps = eps;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.q_out_stride = q_out_stride_token;
+  p.k_out = static_cast<__nv_bfloat16*>(k_out);
+  p.k_out_stride = k_out_stride_token;
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.num_slots = num_slots;
+  p.slot_mapping = slot_mapping;
+  p.num_tokens = num_tokens;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  const int64_t items = static_cast<int64_t>(num_tokens) * heads;
+  const int64_t blocks = (items + nkv::kNormRopeWarps - 1) / nkv::kNormRopeWarps;
+  if (blocks > 0x7fffffff) return NKV_ERR_UNSUPPORTED;
+  nkv::qk_norm_rope_kernel<<<static_cast<unsigned>(blocks), nkv::kNormRopeWarps * 32, 0,
+                             static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
 }
 
 // ---------------------------------------------------------------- prefill

@@ -29,6 +29,7 @@ DEVERR_WAIT_TIMEOUT = 0x4
 DEVERR_COMPRESS_RANGE = 0x8
 DEVERR_RING_RANGE = 0x10
 DEVERR_PREFILL_RANGE = 0x20
+DEVERR_ROPE_POSITION = 0x40
 
 # Size of the library's fixed decode scratch (NKV_STATIC_SCRATCH_BYTES, nkv.h).
 STATIC_SCRATCH_BYTES = 16 << 20
@@ -60,6 +61,11 @@ SIGNATURES: dict[str, tuple] = {
         [_P, c_int64, c_int64, _P, c_int64, _P, c_int64, _I32P, _P, _P, c_int64, _I32P, c_int32,
          _I32P, _P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _P, c_int64,
          c_int32, c_int32, c_int32, c_int32, c_int32, c_float, _P, c_size_t, _P],
+    ),
+    "nkv_qk_norm_rope_store": (
+        c_int,
+        [_P, c_int64, c_int32, _P, _P, c_int64, _P, _P, c_float, _P, c_int64, _P, c_int64,
+         _P, _P, c_int64, _I32P, c_int32, c_int32, c_int32, _P],
     ),
     "nkv_paged_prefill": (
         c_int,

@@ -44,19 +44,43 @@ class Attention(nn.Module):
             self.kv_compress_keep_blocks = vllm_config.kv_compress_keep_blocks
             self.kv_compress_keep_extra_tokens = vllm_config.kv_compress_keep_extra_tokens
 
+    def forward_qkv(self, qkv: torch.Tensor, positions: torch.Tensor,
+                    q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor,
+                    cos_sin_cache: torch.Tensor, eps: float, Layer):
+        """The block of nanokvllm/models/qwen3.py:109-114 from the qkv
+        projection output: q/k RMSNorm + RoPE + the slot write in one launch
+        (nkv_qk_norm_rope_store), then this layer's attention (compression,
+        decode or prefill) on the stored cache. Same result as
+        q_norm / k_norm / rotary_emb followed by forward(q, k, v, Layer)."""
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        has_cache = bool(k_cache.numel() and v_cache.numel())
+        q, v, k = ops.qk_norm_rope_store(
+            qkv, positions, cos_sin_cache, q_norm_weight, k_norm_weight, eps, self.num_heads,
+            self.num_kv_heads, k_cache=k_cache if has_cache else None,
+            v_cache=v_cache if has_cache else None,
+            slot_mapping=context.slot_mapping if has_cache else None,
+            k_out=None if (has_cache and context.use_decode_kernel) else torch.empty(
+                qkv.size(0), self.num_kv_heads, self.head_dim, dtype=qkv.dtype,
+                device=qkv.device))
+        return self._attend(q, k, v, Layer, stored=has_cache)
+
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Layer):
+        return self._attend(q, k, v, Layer, stored=False)
+
+    def _attend(self, q, k, v, Layer, stored: bool):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
         compressing = (context.use_decode_kernel and self.kv_compress_enabled
                        and context.is_compress_step
                        and bool(context.compress_selected_batch_indices))
-        if (context.use_decode_kernel and not compressing and k_cache.numel()
+        if (not stored and context.use_decode_kernel and not compressing and k_cache.numel()
                 and q.size(0) == context.block_tables.size(0)):
             # decode step without compression: slot write + decode in one launch
             o = ops.decode_step(q, k, v, k_cache, v_cache, context.slot_mapping,
                                 context.block_tables, context.context_lens, self.scale)
             return o.unsqueeze(1)
-        if k_cache.numel() and v_cache.numel():
+        if not stored and k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
 
         if compressing:

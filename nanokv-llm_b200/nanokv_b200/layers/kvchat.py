@@ -86,11 +86,34 @@ class Attention(nn.Module):
             self.query_window_size = vllm_config.query_window_size
             self.num_layers = num_layers
 
+    def forward_qkv(self, qkv: torch.Tensor, positions: torch.Tensor,
+                    q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor,
+                    cos_sin_cache: torch.Tensor, eps: float, Layer):
+        """KvChat/models/qwen3.py's q/k norm + RoPE + this layer's attention,
+        from the qkv projection output: norm, RoPE and the slot write in one
+        launch (nkv_qk_norm_rope_store), then the query window, compression
+        and decode / prefill on the stored cache."""
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        has_cache = bool(k_cache.numel() and v_cache.numel())
+        q, v, k = ops.qk_norm_rope_store(
+            qkv, positions, cos_sin_cache, q_norm_weight, k_norm_weight, eps, self.num_heads,
+            self.num_kv_heads, k_cache=k_cache if has_cache else None,
+            v_cache=v_cache if has_cache else None,
+            slot_mapping=context.slot_mapping if has_cache else None,
+            k_out=None if (has_cache and not context.is_prefill) else torch.empty(
+                qkv.size(0), self.num_kv_heads, self.head_dim, dtype=qkv.dtype,
+                device=qkv.device))
+        return self._attend(q, k, v, Layer, stored=has_cache)
+
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, Layer):
+        return self._attend(q, k, v, Layer, stored=False)
+
+    def _attend(self, q, k, v, Layer, stored: bool):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
         qwm = getattr(self, "query_window_manager", None)
-        if (not context.is_prefill and not context.compress_any and k_cache.numel()
+        if (not stored and not context.is_prefill and not context.compress_any and k_cache.numel()
                 and q.size(0) == context.block_tables.size(0)):
             # decode step without compression: slot write, query-window append
             # and decode in one launch
@@ -109,7 +132,7 @@ class Attention(nn.Module):
             if ring_args:
                 qwm.advance(context.q_window_active_seq_ids, Layer)
             return o.unsqueeze(1)
-        if k_cache.numel() and v_cache.numel():
+        if not stored and k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
         if not context.is_prefill and self.kv_compress_enabled:
             qwm = self.query_window_manager

@@ -23,6 +23,7 @@ __all__ = [
     "decode_step",
     "decode_workspace",
     "paged_prefill",
+    "qk_norm_rope_store",
     "flash_attn_varlen_func",
     "window_compress",
     "query_window_append",
@@ -210,6 +211,58 @@ def flash_decode_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     o = paged_decode(q[:, 0], k_cache, v_cache, block_table, cache_seqlens, softmax_scale,
                      out=None if out is None else out[:, 0])
     return o.unsqueeze(1)
+
+
+# ---------------------------------------------------------------- q/k norm + RoPE + store
+def qk_norm_rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos_sin_cache: torch.Tensor,
+                       q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor, eps: float,
+                       num_q_heads: int, num_kv_heads: int, k_cache: torch.Tensor | None = None,
+                       v_cache: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None,
+                       q_out: torch.Tensor | None = None, k_out: torch.Tensor | None = None):
+    """q_norm / k_norm + rotary_emb + store_kvcache of one layer in one launch
+    (nkv_qk_norm_rope_store; the sequence at nanokvllm/models/qwen3.py:109-113
+    and nanokvllm/layers/attention.py:72-73).
+
+    qkv: [T, (Hq + 2 Hk) * 128] bf16 (the qkv projection output);
+    positions: [T] int64; cos_sin_cache: the RotaryEmbedding module's fp32
+    buffer ([max_pos, 1, 128] or [max_pos, 128]); norm weights [128] bf16.
+    Returns (q [T, Hq, 128], v view [T, Hk, 128], k_out or None); k and v
+    are written to the cache slots when k_cache is given.
+    """
+    _require_cuda("qk_norm_rope_store", qkv, positions, cos_sin_cache, q_norm_weight,
+                  k_norm_weight, k_cache, v_cache, slot_mapping)
+    T = qkv.size(0)
+    D = 128
+    assert qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1
+    assert qkv.size(-1) == (num_q_heads + 2 * num_kv_heads) * D
+    assert positions.dtype == torch.int64 and positions.is_contiguous() and positions.numel() == T
+    cs = cos_sin_cache.reshape(-1, D)
+    assert cs.dtype == torch.float32 and cs.is_contiguous()
+    assert q_norm_weight.dtype == torch.bfloat16 and k_norm_weight.dtype == torch.bfloat16
+    assert q_norm_weight.is_contiguous() and k_norm_weight.is_contiguous()
+    if q_out is None:
+        q_out = torch.empty(T, num_q_heads, D, dtype=torch.bfloat16, device=qkv.device)
+    assert q_out.stride(-1) == 1 and q_out.stride(1) == D
+    if k_out is not None:
+        assert k_out.stride(-1) == 1 and k_out.stride(1) == D
+    num_slots = 0
+    if k_cache is not None:
+        assert v_cache is not None and slot_mapping is not None
+        assert k_cache.is_contiguous() and v_cache.is_contiguous() and v_cache.shape == k_cache.shape
+        assert slot_mapping.dtype == torch.int32 and slot_mapping.numel() == T
+        num_slots = k_cache.numel() // (num_kv_heads * D)
+    v = qkv[:, (num_q_heads + num_kv_heads) * D:].view(T, num_kv_heads, D)
+    if T == 0:
+        return q_out, v, k_out
+    lib = _lib.load()
+    _lib.check("nkv_qk_norm_rope_store", lib.nkv_qk_norm_rope_store(
+        qkv.data_ptr(), qkv.stride(0), T, positions.data_ptr(), cs.data_ptr(), cs.size(0),
+        q_norm_weight.data_ptr(), k_norm_weight.data_ptr(), float(eps), q_out.data_ptr(),
+        q_out.stride(0), _ptr(k_out), 0 if k_out is None else k_out.stride(0), _ptr(k_cache),
+        _ptr(v_cache), num_slots, _ptr(slot_mapping), num_q_heads, num_kv_heads, D,
+        _stream(qkv.device)))
+    return q_out, v, k_out
 
 
 # ---------------------------------------------------------------- prefill

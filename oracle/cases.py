@@ -5,6 +5,7 @@
 from __future__ import annotations
 
 import numpy as np
+import torch
 
 from .inputs import CONFIG1, CONFIG1_COMPRESS, bf16, make_paged_batch
 
@@ -74,3 +75,29 @@ VARLEN_CASES = [
     ("mha_empty_rows", dict(seed=45, q_lens=[0, 5, 17, 0], k_lens=[0, 5, 17, 40], Hq=8, Hk=8)),
     ("g3_nocache", dict(seed=46, q_lens=[50, 400], k_lens=[50, 400], Hq=24, Hk=8, paged=False)),
 ]
+
+
+# q/k RMSNorm + RoPE + slot write (qwen3.py:109-113): (name, seed, tokens,
+# Hq, Hk, max_positions, rope base, eps). Qwen3-8B / 32B / 0.6B head shapes.
+NORM_ROPE_CASES = [
+    ("decode_8b", 61, 64, 32, 8, 16384, 1000000.0, 1e-6),
+    ("prefill_32b", 62, 48, 64, 8, 40960, 1000000.0, 1e-6),
+    ("small_06b", 63, 7, 16, 8, 2048, 10000.0, 1e-5),
+]
+
+
+def norm_rope_inputs(seed: int, T: int, Hq: int, Hk: int, max_pos: int):
+    """Seeded qkv rows ([T, (Hq + 2 Hk) * 128] bf16, N(0, 2^2) with a few
+    large channels as real activations have), positions in [0, max_pos),
+    norm weights N(1, 0.3^2) in bf16, and slots (every 5th token -1)."""
+    rng = np.random.default_rng(seed)
+    D = 128
+    x = rng.standard_normal((T, (Hq + 2 * Hk) * D), dtype=np.float32) * 2.0
+    x[:, rng.choice(x.shape[1], size=x.shape[1] // 64, replace=False)] *= 8.0
+    pos = rng.integers(0, max_pos, size=T).astype(np.int64)
+    pos[: min(T, 3)] = [0, 1, max_pos - 1][: min(T, 3)]
+    qw = rng.normal(1.0, 0.3, size=D).astype(np.float32)
+    kw = rng.normal(1.0, 0.3, size=D).astype(np.float32)
+    slots = rng.permutation(T * 4)[:T].astype(np.int32)
+    slots[::5] = -1
+    return (bf16(x), torch.from_numpy(pos), bf16(qw), bf16(kw), torch.from_numpy(slots))

@@ -81,3 +81,23 @@ def test_prefill_argument_errors_need_no_gpu():
     assert call(b=0) == 0 and call(mq=0) == 0   # empty batch is a no-op
     assert call(scale=float("inf")) == 1
     assert call(scale=-0.1) == 1
+
+
+def test_norm_rope_argument_errors_need_no_gpu():
+    from nanokv_b200 import _lib
+
+    lib = _lib.load()
+    base = dict(qkv=16, qst=6144, T=4, pos=16, cs=16, maxp=128, qw=16, kw=16, eps=1e-6, qo=16,
+                qost=4096, ko=None, kost=0, kc=None, vc=None, ns=0, sm=None, hq=32, hk=8, d=128,
+                stream=None)
+
+    def call(**over):
+        a = dict(base, **over)
+        return lib.nkv_qk_norm_rope_store(*a.values())
+
+    assert call(d=64) == 2                  # head_dim 128 only
+    assert call(qkv=18) == 4                # misaligned rows
+    assert call(qst=6000) == 1              # row shorter than (Hq + 2 Hk) * D
+    assert call(cs=20) == 4                 # cos/sin cache must be 8-byte aligned
+    assert call(kc=16) == 1                 # cache without v_cache / slot_mapping
+    assert call(T=0) == 0

@@ -199,3 +199,21 @@ def test_varlen_oracle_pinned_to_flash_attn(golden_dir):
         assert rel.item() <= 5e-3, f"{name}: rel {rel.item()}"
         # rows that see no key are all zeros in both
         assert torch.equal((ours == 0).all(-1), (ref == 0).all(-1))
+
+
+def test_norm_rope_oracle_matches_reference_modules(golden_dir):
+    """oracle.norm_rope restates q/k RMSNorm + RoPE; it must reproduce the
+    reference's own RMSNorm / RotaryEmbedding modules (run eagerly on the
+    CPU by tests/golden/make_golden_norm_rope.py) bit for bit."""
+    from oracle.cases import NORM_ROPE_CASES, norm_rope_inputs
+    from oracle.norm_rope import qk_norm_rope_store_ref, rope_cache
+
+    g = np.load(golden_dir / "norm_rope.npz")
+    for name, seed, T, Hq, Hk, max_pos, base, eps in NORM_ROPE_CASES:
+        qkv, pos, qw, kw, _ = norm_rope_inputs(seed, T, Hq, Hk, max_pos)
+        assert digest(qkv) == str(g[f"{name}/qkv_digest"])
+        cs = rope_cache(max_pos, base)
+        assert digest(cs.view(torch.int32)) == str(g[f"{name}/cos_sin_digest"])
+        q, k, _ = qk_norm_rope_store_ref(qkv, pos, cs, qw, kw, eps, Hq, Hk)
+        assert np.array_equal(q.view(torch.int16).numpy(), g[f"{name}/q_bits"]), name
+        assert np.array_equal(k.view(torch.int16).numpy(), g[f"{name}/k_bits"]), name
