@@ -572,8 +572,9 @@ def measure_prefill(dev, world, compare_flash_attn: bool = True):
 
 def measure_norm_rope(dev, world):
     """q/k RMSNorm + RoPE + slot write of one layer (nkv_qk_norm_rope_store)
-    against the same math as separate eager torch ops (the reference modules'
-    sequence, qwen3.py:109-113, then the slot write), on config 2's decode step (256
+    against the same math as separate torch ops (the reference modules'
+    sequence, qwen3.py:109-113, then the slot write), both replayed from CUDA
+    graphs, on config 2's decode step (256
     tokens of Qwen3-8B heads) and on a 2,048-token x 16 prefill chunk of
     Qwen3-32B heads. HBM bytes = qkv read + q written + k, v slots written."""
     from nanokv_b200 import ops
@@ -612,17 +613,29 @@ def measure_norm_rope(dev, world):
             k = rope(rms_norm(k.view(T, hk, D), kw, 1e-6), pos, cs)
             ops.store_kvcache(k, v.view(T, hk, D), kc, vc, sm)
 
-        def timed(fn, n=20):
-            for _ in range(3):
-                fn()
+        def timed(fn, n=20, reps=5):
+            # replayed from a CUDA graph, as decode steps run in the reference,
+            # so host launch overhead is not in the figure
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    fn()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(n):
+                    fn()
+            graph.replay()
             torch.cuda.synchronize(dev)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            for _ in range(n):
-                fn()
+            for _ in range(reps):
+                graph.replay()
             b.record()
             torch.cuda.synchronize(dev)
-            return a.elapsed_time(b) / n * 1e3
+            del graph
+            return a.elapsed_time(b) / (n * reps) * 1e3
 
         t_f, t_t = timed(fused), timed(torch_ops)
         nbytes = T * (hq + 2 * hk) * D * 2 + T * hq * D * 2 + T * 2 * hk * D * 2

@@ -203,7 +203,8 @@ int nkv_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_he
 /* ([max_positions, head_dim] fp32: cos then sin, rotary_embedding.py:7-45). */
 /* Positions outside the cache are clamped and flag NKV_DEVERR_ROPE_POSITION;*/
 /* slots >= num_slots are not written and flag NKV_DEVERR_STORE_SLOT.       */
-/* Supported: head_dim 128; bf16 rows 4-byte aligned with even strides.      */
+/* Supported: head_dim 128; all pointers 16-byte aligned, row strides       */
+/* multiples of 8 elements.                                                  */
 int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t num_tokens,
                            const int64_t* positions, const float* cos_sin_cache,
                            int64_t max_positions, const void* q_norm_weight,

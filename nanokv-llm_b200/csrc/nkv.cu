@@ -485,11 +485,10 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
   if (qkv_stride_token < heads * head_dim || q_out_stride_token < int64_t(num_q_heads) * head_dim ||
       (k_out && k_out_stride_token < int64_t(num_kv_heads) * head_dim))
     return NKV_ERR_INVALID_ARGUMENT;
-  auto a4 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3u) == 0; };
-  if (!a4(qkv) || !a4(q_out) || !a4(q_norm_weight) || !a4(k_norm_weight) ||
-      (k_out && !a4(k_out)) || (k_cache && (!a4(k_cache) || !a4(v_cache))) ||
-      (reinterpret_cast<uintptr_t>(cos_sin_cache) & 7u) || (qkv_stride_token & 1) ||
-      (q_out_stride_token & 1) || (k_out && (k_out_stride_token & 1)))
+  if (!aligned16(qkv) || !aligned16(q_out) || !aligned16(q_norm_weight) ||
+      !aligned16(k_norm_weight) || (k_out && !aligned16(k_out)) ||
+      (k_cache && (!aligned16(k_cache) || !aligned16(v_cache))) || !aligned16(cos_sin_cache) ||
+      (qkv_stride_token % 8) || (q_out_stride_token % 8) || (k_out && (k_out_stride_token % 8)))
     return NKV_ERR_ALIGNMENT;
   nkv::NormRopeParams p{};
   p.qkv = static_cast<const __nv_bfloat16*>(qkv);
@@ -511,8 +510,15 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
   p.num_tokens = num_tokens;
   p.num_q_heads = num_q_heads;
   p.num_kv_heads = num_kv_heads;
-  const int64_t items = static_cast<int64_t>(num_tokens) * heads;
-  const int64_t blocks = (items + nkv::kNormRopeWarps - 1) / nkv::kNormRopeWarps;
+  // 4-head groups; one warp per token when tokens are plenty, one group per
+  // warp for small (decode) batches
+  const int64_t groups = (heads + 3) / 4;
+  const int64_t gpw = std::min<int64_t>(
+      groups, std::max<int64_t>(1, (int64_t(num_tokens) * groups + 32767) / 32768));
+  p.groups_per_warp = static_cast<int>(gpw);
+  p.warps_per_token = static_cast<int>((groups + gpw - 1) / gpw);
+  const int64_t warps = static_cast<int64_t>(num_tokens) * p.warps_per_token;
+  const int64_t blocks = (warps + nkv::kNormRopeWarps - 1) / nkv::kNormRopeWarps;
   if (blocks > 0x7fffffff) return NKV_ERR_UNSUPPORTED;
   nkv::qk_norm_rope_kernel<<<static_cast<unsigned>(blocks), nkv::kNormRopeWarps * 32, 0,
                              static_cast<cudaStream_t>(stream)>>>(p);

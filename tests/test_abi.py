@@ -96,8 +96,8 @@ def test_norm_rope_argument_errors_need_no_gpu():
         return lib.nkv_qk_norm_rope_store(*a.values())
 
     assert call(d=64) == 2                  # head_dim 128 only
-    assert call(qkv=18) == 4                # misaligned rows
+    assert call(qkv=24) == 4                # rows not 16-byte aligned
     assert call(qst=6000) == 1              # row shorter than (Hq + 2 Hk) * D
-    assert call(cs=20) == 4                 # cos/sin cache must be 8-byte aligned
+    assert call(cs=24) == 4                 # cos/sin cache must be 16-byte aligned
     assert call(kc=16) == 1                 # cache without v_cache / slot_mapping
     assert call(T=0) == 0
