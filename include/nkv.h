@@ -233,6 +233,7 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
 /* out_keep_idx (optional, [num_selected, keep_tokens]) receives the window-  */
 /* relative kept indices; out_new_lens (optional, [num_selected]) the new     */
 /* lengths. Needs num_kv_heads <= 8 (one thread-block cluster per sequence). */
+/* Entries of selected_batch_indices equal to -1 are skipped.                */
 /* The caller guarantees what the reference asserts (full_blocks >=          */
 /* window_blocks); rows violating it are skipped and flag                    */
 /* NKV_DEVERR_COMPRESS_RANGE.                                                */
@@ -245,6 +246,23 @@ int nkv_window_compress(const void* q, int64_t q_stride_token,
                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                         int32_t block_size, float softmax_scale,
                         int32_t* out_keep_idx, int32_t* out_new_lens, void* stream);
+
+/* 3a'. Device-side selection of the rows a periodic compression step takes */
+/* (the reference's host loop in prepare_decode, nanokvllm/engine/          */
+/* model_runner.py:305-321), so the whole compression step can be captured  */
+/* in a CUDA graph and replayed: row b (length context_lens[b]) is skipped   */
+/* when its length mod block_size == block_size - 1, eligible when          */
+/* tail_uncompressed[b] >= window_blocks * block_size and                    */
+/* context_lens[b] / block_size >= window_blocks; the first topk eligible   */
+/* rows in batch order go to out_selected[0, count), the rest of            */
+/* out_selected[topk] is -1 (nkv_window_compress skips -1 entries, so it is  */
+/* called with num_selected = topk). out_count [1] and out_base_lens        */
+/* [batch] (a copy of context_lens: the base lengths nkv_window_compress    */
+/* reads) may be NULL.                                                       */
+int nkv_window_select(const int32_t* context_lens, const int32_t* tail_uncompressed,
+                      int32_t batch, int32_t block_size, int32_t window_blocks, int32_t topk,
+                      int32_t* out_selected, int32_t* out_count, int32_t* out_base_lens,
+                      void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 3b. KvChat query window: append this step's queries of active sequences  */

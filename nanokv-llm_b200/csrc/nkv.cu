@@ -680,6 +680,28 @@ int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, vo
   }
 }
 
+int nkv_window_select(const int32_t* context_lens, const int32_t* tail_uncompressed,
+                      int32_t batch, int32_t block_size, int32_t window_blocks, int32_t topk,
+                      int32_t* out_selected, int32_t* out_count, int32_t* out_base_lens,
+                      void* stream) {
+  if (batch < 0 || topk < 0 || block_size <= 0 || window_blocks <= 0) return NKV_ERR_INVALID_ARGUMENT;
+  if (topk == 0 && batch == 0) return NKV_OK;
+  if ((batch > 0 && (!context_lens || !tail_uncompressed)) || (topk > 0 && !out_selected))
+    return NKV_ERR_INVALID_ARGUMENT;
+  nkv::WindowSelectParams p{};
+  p.context_lens = context_lens;
+  p.tail_uncompressed = tail_uncompressed;
+  p.selected = out_selected;
+  p.count = out_count;
+  p.base_lens = out_base_lens;
+  p.batch = batch;
+  p.block_size = block_size;
+  p.window_blocks = window_blocks;
+  p.topk = topk;
+  nkv::window_select_kernel<<<1, nkv::kSelectThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
 // ------------------------------------------------------------------ KvChat
 int nkv_query_window_append(const void* q, int64_t q_stride_token, void* ring,
                             int32_t num_ring_slots, int32_t num_layers, int32_t window_size,

@@ -119,6 +119,10 @@ window_compress_kernel(const WindowCompressParams p) {
   __shared__ int s_tail_block;
 
   const int b = __ldg(p.selected + sel_i);
+  // -1: an unused entry of a fixed-size selection list (device-side
+  // selection, graph replay); uniform across the cluster, before any
+  // cluster barrier
+  if (b < 0) return;
   const int L0 = __ldg(p.base_lens + b);
   const int full_blocks = L0 / bs;
   const int tail_len = L0 % bs;
@@ -260,6 +264,53 @@ window_compress_kernel(const WindowCompressParams p) {
         p.out_keep_idx[static_cast<int64_t>(sel_i) * keep_tokens + i] = final_idx[i];
     }
   }
+}
+
+// Periodic-compression selection on the device, so a compression step can
+// be replayed from a CUDA graph: the rule of the reference's prepare_decode
+// (nanokvllm/engine/model_runner.py:305-321) -- row b (physical length L =
+// context_lens[b]) is skipped when L % block_size == block_size - 1 and is
+// eligible when tail_uncompressed[b] >= window_blocks * block_size and
+// L / block_size >= window_blocks; the FIRST topk eligible rows in batch
+// order are selected. One CTA; writes selected[0, topk) (-1 padded), the
+// count, and a copy of context_lens as the step's base lengths.
+constexpr int kSelectThreads = kCompressThreads;  // block_* helpers assume this size
+
+struct WindowSelectParams {
+  const int32_t* context_lens;
+  const int32_t* tail_uncompressed;
+  int32_t* selected;    // [topk]
+  int32_t* count;       // [1] or null
+  int32_t* base_lens;   // [batch] or null
+  int batch;
+  int block_size;
+  int window_blocks;
+  int topk;
+};
+
+__global__ void __launch_bounds__(kSelectThreads)
+window_select_kernel(const WindowSelectParams p) {
+  __shared__ int red[kCompressWarps];
+  const int window_tokens = p.window_blocks * p.block_size;
+  for (int i = threadIdx.x; i < p.topk; i += kSelectThreads) p.selected[i] = -1;
+  __syncthreads();
+  int taken = 0;  // eligible rows in earlier chunks
+  for (int base = 0; base < p.batch; base += kSelectThreads) {
+    const int b = base + threadIdx.x;
+    int elig = 0;
+    if (b < p.batch) {
+      const int L = __ldg(p.context_lens + b);
+      if (p.base_lens != nullptr) p.base_lens[b] = L;
+      if (L % p.block_size != p.block_size - 1 && __ldg(p.tail_uncompressed + b) >= window_tokens &&
+          L / p.block_size >= p.window_blocks)
+        elig = 1;
+    }
+    const int before = block_excl_scan(elig, red);
+    const int pos = taken + before;
+    if (elig && pos < p.topk) p.selected[pos] = b;
+    taken += block_sum_int(elig, red);
+  }
+  if (threadIdx.x == 0 && p.count != nullptr) p.count[0] = min(taken, p.topk);
 }
 
 }  // namespace nkv

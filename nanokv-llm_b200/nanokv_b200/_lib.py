@@ -79,6 +79,10 @@ SIGNATURES: dict[str, tuple] = {
          c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float,
          _I32P, _I32P, _P],
     ),
+    "nkv_window_select": (
+        c_int,
+        [_I32P, _I32P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _I32P, _P],
+    ),
     "nkv_query_window_append": (
         c_int,
         [_P, c_int64, _P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _I32P,

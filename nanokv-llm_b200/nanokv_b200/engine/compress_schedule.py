@@ -114,6 +114,71 @@ class PeriodicCompressScheduler:
         else:
             ctx.compress_base_context_lens = None
 
+    # ---------------------------------------------------------- device-side selection
+    def device_buffers(self, batch: int, device) -> dict:
+        """Static buffers of a graph-captured compression step (allocate once
+        per captured batch size)."""
+        pin = torch.cuda.is_available()
+        return {
+            "selected": torch.full((self.topk,), -1, dtype=torch.int32, device=device),
+            "base_lens": torch.zeros(batch, dtype=torch.int32, device=device),
+            "tail_uncompressed": torch.zeros(batch, dtype=torch.int32, device=device),
+            "selected_host": torch.full((self.topk,), -1, dtype=torch.int32).pin_memory()
+            if pin else torch.full((self.topk,), -1, dtype=torch.int32),
+        }
+
+    def fill_context_device(self, ctx: Context, seqs, buffers: dict) -> bool:
+        """Like fill_context, but leaves the choice of rows to the device
+        (nkv_window_select inside the step), so the compression step can be
+        replayed from a CUDA graph captured once: only the per-sequence
+        tail_uncompressed counters are uploaded. Returns is_compress_step;
+        on such a step the runner replays its compression graph (captured
+        with this context) instead of the plain decode graph, and calls
+        events_from_device after the step."""
+        self.decode_step_counter += 1
+        is_step = self.decode_step_counter % self.period == 0
+        ctx.compress_need_mask = None
+        ctx.compress_any = False
+        ctx.is_compress_step = is_step
+        ctx.compress_selected_batch_indices = []
+        ctx.compress_selected_seq_ids = []
+        ctx.compress_device_select = True
+        ctx.compress_topk = self.topk
+        ctx.compress_selected_t = buffers["selected"]
+        ctx.compress_base_context_lens = buffers["base_lens"][: len(seqs)]
+        tail = buffers["tail_uncompressed"]
+        if is_step:
+            host = torch.tensor([s.tail_uncompressed_len for s in seqs], dtype=torch.int32)
+            if tail.is_cuda and torch.cuda.is_available():
+                host = host.pin_memory()
+            tail[: len(seqs)].copy_(host, non_blocking=True)
+        ctx.compress_tail_uncompressed_t = tail[: len(seqs)]
+        ctx.compress_selected_host = buffers["selected_host"]
+        return is_step
+
+    def events_from_device(self, selected_host, base_lens_host, block_tables_host,
+                           keep_blocks: int, keep_extra_tokens: int,
+                           num_layers: int) -> list[dict]:
+        """The events of a device-selected compression step, built after the
+        step from the selection it copied back (the same events
+        MyCompressCompact builds on a host-selected step)."""
+        B = self.block_size
+        window_tokens = self.window_blocks * B
+        keep_tokens = keep_blocks * B + keep_extra_tokens
+        events = []
+        for b in [int(x) for x in selected_host if int(x) >= 0]:
+            new_len = int(base_lens_host[b]) - window_tokens + keep_tokens
+            keep_after = (new_len + B - 1) // B
+            events.append({
+                "batch_index": b,
+                "layer": num_layers - 1,
+                "new_context_len": new_len,
+                "keep_blocks": keep_after,
+                "freed_block_ids": [int(x) for x in block_tables_host[b][keep_after:] if int(x) >= 0],
+                "tail_uncompressed_len_after": 0,
+            })
+        return events
+
 
 def prepare_threshold_context(ctx: Context, seqs, config, query_window_manager) -> None:
     """KvChat's per-step trigger (KvChat/engine/model_runner.py:304-339): a

@@ -73,7 +73,8 @@ class Attention(nn.Module):
         k_cache, v_cache = self.k_cache, self.v_cache
         compressing = (context.use_decode_kernel and self.kv_compress_enabled
                        and context.is_compress_step
-                       and bool(context.compress_selected_batch_indices))
+                       and (context.compress_device_select
+                            or bool(context.compress_selected_batch_indices)))
         if (not stored and context.use_decode_kernel and not compressing and k_cache.numel()
                 and q.size(0) == context.block_tables.size(0)):
             # decode step without compression: slot write + decode in one launch

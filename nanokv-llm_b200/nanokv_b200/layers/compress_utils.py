@@ -39,6 +39,10 @@ def MyCompressCompact(q_current: torch.Tensor, k_cache: torch.Tensor, v_cache: t
         context = get_context()
     if (not context.use_decode_kernel) or context.context_lens is None or context.block_tables is None:
         return False
+    if context.compress_device_select:
+        return _compress_device_selected(q_current, k_cache, v_cache, layer_id, block_size,
+                                         window_blocks, keep_blocks, keep_extra_tokens,
+                                         num_layers, context)
     selected = context.compress_selected_batch_indices
     if not selected:
         return False
@@ -79,4 +83,35 @@ def MyCompressCompact(q_current: torch.Tensor, k_cache: torch.Tensor, v_cache: t
                 "freed_block_ids": freed,
                 "tail_uncompressed_len_after": 0,
             })
+    return True
+
+
+def _compress_device_selected(q_current, k_cache, v_cache, layer_id, block_size, window_blocks,
+                              keep_blocks, keep_extra_tokens, num_layers, context) -> bool:
+    """A compression step whose rows are chosen on the device, so that the
+    same kernel sequence serves every compression step of a batch size and
+    can be captured in a CUDA graph: layer 0 runs nkv_window_select (the
+    reference's selection rule) into the fixed-size compress_selected_t and
+    snapshots the base lengths; every layer compresses with the -1-padded
+    list; the last layer copies the list to pinned host memory, from which
+    the host builds the events once the step has finished
+    (PeriodicCompressScheduler.events_from_device). Nothing here depends on
+    this step's host-side values."""
+    B = block_size
+    window_tokens = window_blocks * B
+    keep_tokens = keep_blocks * B + keep_extra_tokens
+    num_keep = keep_tokens - 2
+    if window_tokens - 1 <= 0 or window_tokens <= num_keep + 1:
+        return False
+    sel = context.compress_selected_t
+    base = context.compress_base_context_lens
+    assert sel is not None and base is not None and context.compress_tail_uncompressed_t is not None
+    if layer_id == 0:
+        ops.window_select(context.context_lens, context.compress_tail_uncompressed_t, B,
+                          window_blocks, context.compress_topk, out_selected=sel,
+                          out_base_lens=base)
+    ops.window_compress(q_current, k_cache, v_cache, context.block_tables, base,
+                        context.context_lens, sel, window_blocks, keep_tokens, obs_window=1)
+    if layer_id + 1 >= num_layers and context.compress_selected_host is not None:
+        context.compress_selected_host.copy_(sel, non_blocking=True)
     return True

@@ -26,6 +26,7 @@ __all__ = [
     "qk_norm_rope_store",
     "flash_attn_varlen_func",
     "window_compress",
+    "window_select",
     "query_window_append",
     "threshold_compress",
 ]
@@ -332,6 +333,30 @@ def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         softmax_scale = q.size(-1) ** -0.5
     return paged_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale,
                          causal=causal, block_table=block_table)
+
+
+def window_select(context_lens: torch.Tensor, tail_uncompressed: torch.Tensor, block_size: int,
+                  window_blocks: int, topk: int, out_selected: torch.Tensor | None = None,
+                  out_count: torch.Tensor | None = None,
+                  out_base_lens: torch.Tensor | None = None) -> torch.Tensor:
+    """Device-side periodic-compression selection (nkv_window_select): the
+    first `topk` eligible rows by the reference's rule (model_runner.py:
+    305-321) into out_selected[topk], -1 padded. All tensors int32 on the
+    device; nothing is read back, so the call can sit inside a CUDA graph."""
+    _require_cuda("window_select", context_lens, tail_uncompressed, out_selected, out_count,
+                  out_base_lens)
+    B = context_lens.numel()
+    assert context_lens.dtype == torch.int32 and tail_uncompressed.dtype == torch.int32
+    assert context_lens.is_contiguous() and tail_uncompressed.is_contiguous()
+    assert tail_uncompressed.numel() >= B
+    if out_selected is None:
+        out_selected = torch.empty(topk, dtype=torch.int32, device=context_lens.device)
+    assert out_selected.dtype == torch.int32 and out_selected.numel() >= topk
+    lib = _lib.load()
+    _lib.check("nkv_window_select", lib.nkv_window_select(
+        context_lens.data_ptr(), tail_uncompressed.data_ptr(), B, block_size, window_blocks, topk,
+        out_selected.data_ptr(), _ptr(out_count), _ptr(out_base_lens), _stream(context_lens.device)))
+    return out_selected
 
 
 # ---------------------------------------------------------------- window compression

@@ -17,6 +17,10 @@ Additions, all optional and defaulting to "not provided":
                              device index tensors of the KvChat query window
                              (per active row, and per batch row for the fused
                              decode step)
+  compress_device_select, compress_topk, compress_tail_uncompressed_t,
+  compress_selected_host     selection of a periodic compression step on the
+                             device, so the step can be replayed from a CUDA
+                             graph (see compress_utils.MyCompressCompact)
 """
 
 from __future__ import annotations
@@ -64,6 +68,16 @@ class Context:
     q_window_pos_t: torch.Tensor | None = None
     q_window_row_slot_t: torch.Tensor | None = None
     q_window_row_pos_t: torch.Tensor | None = None
+
+    # device-side selection of a periodic compression step (graph-capturable):
+    # the layers select at layer 0 into compress_selected_t ([topk], -1
+    # padded) from context_lens and compress_tail_uncompressed_t, compress
+    # with that fixed-size list, and copy it to compress_selected_host (pinned)
+    # at the last layer; the host builds the events after the step.
+    compress_device_select: bool = False
+    compress_topk: int = 0
+    compress_tail_uncompressed_t: torch.Tensor | None = None
+    compress_selected_host: torch.Tensor | None = None
 
 
 _CONTEXT = Context()
