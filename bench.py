@@ -300,6 +300,8 @@ def run_gpu(args, rank, world, dev):
     extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world),
              "config4_prefill": measure_prefill(dev, world),
              "qk_norm_rope_store": measure_norm_rope(dev, world)}
+    if world > 1:
+        extra["oproj_allreduce"] = measure_oproj(dev, world)
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e_ms, statistics.mean(dec_ms)], dtype=torch.float64, device=dev)
@@ -642,6 +644,73 @@ def measure_norm_rope(dev, world):
         res[name] = {"tokens": T, "fused_us": round(t_f, 1), "torch_ops_us": round(t_t, 1),
                      "speedup": round(t_t / t_f, 2), "fused_GBps": round(nbytes / t_f / 1e3, 1)}
     return res
+
+
+def measure_oproj(dev, world):
+    """The attention block's o_proj with its TP all-reduce on config 2's
+    decode step (256 tokens, Qwen3-8B hidden 4096, k = 4096 / world per
+    rank): nkv_oproj_allreduce (one kernel, NVLink SHARP reduction) against
+    the reference's F.linear + dist.all_reduce (cuBLAS + NCCL). Collective:
+    every rank runs it. Time per call from CUDA events around 100 calls after
+    a barrier (rank 0's; the kernel itself synchronises the ranks), both
+    sides replayed from CUDA graphs."""
+    import torch.nn.functional as F
+    from nanokv_b200.layers.linear import OProjAllReduce
+
+    T, N, K = 256, 4096, 4096 // world
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    try:
+        op = OProjAllReduce(N, 512, device=dev)
+    except RuntimeError as e:  # no NVLS on this group
+        return {"unavailable": str(e)}
+    y = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
+
+    def fused():
+        op(x, w, out=y)
+
+    def reference():
+        r = F.linear(x, w)
+        torch.distributed.all_reduce(r)
+
+    def timed(fn, n=20, reps=5):
+        # replayed from a CUDA graph (decode steps run from graphs), so the
+        # host's launch rate is not in the figure; all ranks capture and
+        # replay in the same order
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(n):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        torch.distributed.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        del graph  # graphs holding NCCL calls go before the process group does
+        return a.elapsed_time(b) / (n * reps) * 1e3
+
+    t_f = timed(fused)
+    t_r = timed(reference)
+    torch.cuda.synchronize(dev)
+    torch.distributed.barrier()
+    del op
+    torch.cuda.synchronize(dev)
+    torch.distributed.barrier()
+    return {"workload": f"o_proj + all-reduce, 256 tokens x hidden 4096, k {K} per rank, {world} ranks",
+            "fused_us": round(t_f, 1), "cublas_nccl_us": round(t_r, 1),
+            "speedup": round(t_r / t_f, 2)}
 
 
 # ---------------------------------------------------------------------- CPU arms

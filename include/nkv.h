@@ -217,6 +217,33 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
                            void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* 2e. o_proj GEMM + tensor-parallel all-reduce in one kernel (decode sizes) */
+/* Replaces RowParallelLinear.forward's F.linear + dist.all_reduce           */
+/* (nanokvllm/layers/linear.py:151-155) for tokens <= 512:                   */
+/*   y[t, :] = sum over ranks of x_rank[t, :] @ w_rank^T                    */
+/* x [tokens, k] bf16 (row stride ldx), w [n, k] bf16 (the rank's weight     */
+/* shard, row stride ldw), y [tokens, n] bf16 (row stride ldy). Each rank    */
+/* writes its fp32 partial product to its copy of a symmetric fp32          */
+/* [tokens, n] buffer (part_local; part_mc = the buffer's multicast          */
+/* address); after an in-kernel barrier every rank sums its 1/world slice    */
+/* through NVLink SHARP (multimem.ld_reduce) and broadcasts the bf16 result  */
+/* into every rank's copy of a symmetric bf16 [tokens, n] buffer (out_mc /   */
+/* out_local); after a second barrier it copies the result to y. sig_mc /    */
+/* sig_local: a symmetric uint32[2 * world] of epoch slots; flags: this      */
+/* rank's uint32[5] (arrival counters, release flags, the epoch); slots and  */
+/* flags zeroed once. The epoch is read and advanced on the device, so every */
+/* rank must make the same sequence of calls and a CUDA graph may replay     */
+/* them. Waits are bounded by timeout_ns (then NKV_DEVERR_WAIT_TIMEOUT).     */
+/* Needs k % 64 == 0, n % 32 == 0, 16-byte aligned x, w, y and buffers, row  */
+/* strides multiples of 8. Cooperative launch: n / 32 (or / 64, / 128) CTAs  */
+/* must fit the GPU.                                                         */
+int nkv_oproj_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t tokens,
+                        int32_t k, int32_t n, void* part_mc, void* part_local, void* out_mc,
+                        const void* out_local, void* sig_mc, void* sig_local, uint32_t* flags,
+                        int32_t rank, int32_t world, uint64_t timeout_ns, void* y, int64_t ldy,
+                        void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* 3a. Periodic window compression (one layer, all selected sequences)       */
 /* Replaces: MyCompressCompact, nanokvllm/layers/compress_utils.py:100-263,  */
 /*   with get_tail_window_and_tail_slots (:9-72), gather_kv_by_slots (:75-97) */

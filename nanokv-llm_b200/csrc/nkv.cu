@@ -16,6 +16,7 @@
 #include "paged_decode.cuh"
 #include "paged_prefill.cuh"
 #include "qk_norm_rope.cuh"
+#include "oproj_allreduce.cuh"
 #include "store_kvcache.cuh"
 #include "threshold_compress.cuh"
 #include "window_compress.cuh"
@@ -81,6 +82,22 @@ int encode_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NKV_OK : NKV_ERR_ALIGNMENT;
+}
+
+// 2-D bf16 map {d0 (contiguous), d1 rows} with row stride `stride1_bytes`,
+// box {64, box1} and 128-byte swizzle.
+int encode_2d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t stride1_bytes,
+              uint32_t box1) {
+  auto fn = encode_fn();
+  if (!fn) return NKV_ERR_CUDA;
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {stride1_bytes};
+  const cuuint32_t box[2] = {64, box1};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? NKV_OK : NKV_ERR_ALIGNMENT;
 }
 
@@ -523,6 +540,83 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
   nkv::qk_norm_rope_kernel<<<static_cast<unsigned>(blocks), nkv::kNormRopeWarps * 32, 0,
                              static_cast<cudaStream_t>(stream)>>>(p);
   return launch_status();
+}
+
+// ---------------------------------------------------------------- o_proj + all-reduce
+int nkv_oproj_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t tokens,
+                        int32_t k, int32_t n, void* part_mc, void* part_local, void* out_mc,
+                        const void* out_local, void* sig_mc, void* sig_local, uint32_t* flags,
+                        int32_t rank, int32_t world, uint64_t timeout_ns, void* y, int64_t ldy,
+                        void* stream) {
+  if (tokens < 0 || k <= 0 || n <= 0 || world < 1 || rank < 0 || rank >= world)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (tokens == 0) return NKV_OK;
+  if (!x || !w || !part_mc || !part_local || !out_mc || !out_local || !sig_mc || !sig_local ||
+      !flags || !y)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (tokens > nkv::kOpMaxMTiles * 128 || k % nkv::kOpK != 0 || n % 32 != 0) return NKV_ERR_UNSUPPORTED;
+  if (ldx < k || ldw < k || ldy < n) return NKV_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(part_mc) || !aligned16(part_local) ||
+      !aligned16(out_mc) || !aligned16(out_local) || !aligned16(y) || (ldx % 8) || (ldw % 8) ||
+      (ldy % 8) || (reinterpret_cast<uintptr_t>(sig_mc) & 3u) ||
+      (reinterpret_cast<uintptr_t>(sig_local) & 3u))
+    return NKV_ERR_ALIGNMENT;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = sm_count(dev);
+  const int mtiles = (tokens + 127) / 128;
+  int tn = 32;
+  while ((n / tn > sms || n % tn != 0) && tn < 128) tn *= 2;
+  if (n % tn != 0 || n / tn > sms || mtiles * tn > 512) return NKV_ERR_UNSUPPORTED;
+  const int stage_bytes = mtiles * nkv::kOpATile + tn * 128;
+  constexpr int kSmemLimit = 227 * 1024;
+  const int fixed = 1024 + 256;  // alignment slack, barriers, TMEM slot
+  const int stages = std::min(nkv::kOpMaxStages, (kSmemLimit - fixed) / stage_bytes);
+  if (stages < 2) return NKV_ERR_UNSUPPORTED;
+  const int smem = stages * stage_bytes + fixed;
+
+  CUtensorMap tx, tw;
+  int st;
+  if ((st = encode_2d(&tx, x, k, tokens, ldx * 2, 128)) != NKV_OK) return st;
+  if ((st = encode_2d(&tw, w, k, n, ldw * 2, tn)) != NKV_OK) return st;
+  nkv::OprojParams p{};
+  p.part_mc = static_cast<float*>(part_mc);
+  p.part_local = static_cast<float*>(part_local);
+  p.out_mc = static_cast<__nv_bfloat16*>(out_mc);
+  p.out_local = static_cast<const __nv_bfloat16*>(out_local);
+  p.sig_mc = static_cast<uint32_t*>(sig_mc);
+  p.sig_local = static_cast<uint32_t*>(sig_local);
+  p.flags = reinterpret_cast<unsigned int*>(flags);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.T = tokens;
+  p.K = k;
+  p.N = n;
+  p.mtiles = mtiles;
+  p.tn = tn;
+  p.stages = stages;
+  p.rank = rank;
+  p.world = world;
+  p.timeout_ns = timeout_ns;
+
+  static int attr_smem[kMaxDevices] = {0};
+  if (dev >= 0 && dev < kMaxDevices && attr_smem[dev] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(nkv::oproj_allreduce_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_smem[dev] = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n / tn, 1, 1);
+  cfg.blockDim = dim3(nkv::kOpThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the barrier waits on peers
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::oproj_allreduce_kernel, tx, tw, p));
 }
 
 // ---------------------------------------------------------------- prefill

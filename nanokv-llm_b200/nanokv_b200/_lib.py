@@ -8,7 +8,7 @@ lacks a symbol, loading fails loudly.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_void_p, POINTER
+from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libnkv.so"
@@ -66,6 +66,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, c_int64, c_int32, _P, _P, c_int64, _P, _P, c_float, _P, c_int64, _P, c_int64,
          _P, _P, c_int64, _I32P, c_int32, c_int32, c_int32, _P],
+    ),
+    "nkv_oproj_allreduce": (
+        c_int,
+        [_P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P,
+         c_int32, c_int32, c_uint64, _P, c_int64, _P],
     ),
     "nkv_paged_prefill": (
         c_int,
