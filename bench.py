@@ -816,7 +816,8 @@ def run_profile_case(kind: str) -> None:
     (Qwen3-8B shapes) 4 times;
     `compress` runs one config-3 window-compression event 4 times;
     `prefill` runs one chunked-prefill attention launch (Qwen3-32B shapes,
-    4 x 2,048 queries over 10,240 keys) 4 times."""
+    4 x 2,048 queries over 10,240 keys) 4 times; `norm_rope` runs the q/k
+    norm + RoPE + store of a 32k-token chunk 4 times."""
     from nanokv_b200 import ops
 
     dev = torch.device("cuda", 0)
@@ -825,6 +826,25 @@ def run_profile_case(kind: str) -> None:
         for _ in range(4):
             measure_compress(dev, HQ, HK)
         torch.cuda.synchronize()
+        return
+    if kind == "norm_rope":
+        # q/k norm + RoPE + store on a 32k-token prefill chunk of Qwen3-32B
+        # heads (671 MB read, 671 MB written: > L2)
+        T, hq, hk = 16 * 2048, 64, 8
+        g = torch.Generator(device=dev).manual_seed(7)
+        qkv = torch.randn(T, (hq + 2 * hk) * D, device=dev, generator=g).to(torch.bfloat16)
+        pos = torch.randint(0, 32768, (T,), device=dev, generator=g)
+        cs = torch.randn(40960, D, device=dev, generator=g)
+        w = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        kc = torch.empty(T * 2 // BLOCK, BLOCK, hk, D, device=dev, dtype=torch.bfloat16)
+        vc = torch.empty_like(kc)
+        sm = torch.randperm(T * 2, device=dev, generator=g)[:T].to(torch.int32)
+        for _ in range(4):
+            ops.qk_norm_rope_store(qkv, pos, cs, w, w, 1e-6, hq, hk, k_cache=kc, v_cache=vc,
+                                   slot_mapping=sm)
+        torch.cuda.synchronize()
+        nbytes = T * (hq + 2 * hk) * D * 2 + T * hq * D * 2 + T * 2 * hk * D * 2
+        print(json.dumps({"profile": kind, "alg_bytes": nbytes}))
         return
     if kind == "prefill":
         # 4 sequences of Qwen3-32B attention shapes: a 2,048-token causal
@@ -875,7 +895,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
-    ap.add_argument("--profile", choices=["decode", "compress", "prefill"], default=None,
+    ap.add_argument("--profile", choices=["decode", "compress", "prefill", "norm_rope"],
+                    default=None,
                     help="run a small case for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile:

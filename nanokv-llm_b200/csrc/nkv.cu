@@ -121,6 +121,10 @@ constexpr int kMaxDecodePairs = 1 << 16;
 #ifndef NKV_DECODE_MAX_SPLIT_TOKENS
 #define NKV_DECODE_MAX_SPLIT_TOKENS 4096
 #endif
+// Shortest split when the launch has enough work items without finer ones.
+#ifndef NKV_DECODE_MIN_SPLIT_TOKENS
+#define NKV_DECODE_MIN_SPLIT_TOKENS 2048
+#endif
 // Work items aimed for per SM (of a 148-SM part) when every row is full.
 #ifndef NKV_DECODE_TARGET_ITEMS_PER_SM
 #define NKV_DECODE_TARGET_ITEMS_PER_SM 7
@@ -140,6 +144,18 @@ DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block
   const int64_t block_units = static_cast<int64_t>(pl.pairs) * std::max(max_blocks, 1);
   const int64_t target_items = NKV_DECODE_TARGET_ITEMS_PER_SM * 148;
   int cb = static_cast<int>(block_units / target_items);
+  // Few (row, kv head) pairs with long rows (e.g. 16 rows x 1 kv head of 32k
+  // tokens on a TP8 shard) would otherwise be cut into 1-block splits whose
+  // fixed costs (grab, first-tile latency, a 128-way merge) dominate: keep
+  // splits >= 2,048 tokens whenever that still gives every SM an item
+  // (measured on that shard: 1-block splits 184 us, 1,024 tokens 83 us,
+  // 2,048 tokens 65 us per launch).
+  // Latency-bound shapes with few items in total (one short row) keep the
+  // fine splits.
+  const int min_cb = std::max(1, NKV_DECODE_MIN_SPLIT_TOKENS / block_size);
+  if (cb < min_cb &&
+      static_cast<int64_t>(pl.pairs) * ((std::max(max_blocks, 1) + min_cb - 1) / min_cb) >= 148)
+    cb = min_cb;
   const int max_cb = std::max(1, NKV_DECODE_MAX_SPLIT_TOKENS / block_size);
   pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
   pl.chunk_tokens = pl.chunk_blocks * block_size;
