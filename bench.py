@@ -227,6 +227,13 @@ def run_gpu(args, rank, world, dev):
     ms = t0.elapsed_time(t1)
     dec_ms = [a.elapsed_time(b) for a, b in dec_events]
 
+    # ---- the reference's own GPU path on the same inputs, beside ours:
+    # its slot write (torch index store, what its Triton store_kvcache does)
+    # and flash-attn's flash_attn_with_kvcache decode (library code), per
+    # layer, timed the same way (context only; not our measurement)
+    ref_gpu = reference_gpu_step_ms(args, dev, st, qkv, layer_views, kv, R, bt, cl, sm, scale,
+                                    hq, hk, barrier)
+
     # ---- end to end through the public API with host buffers
     from nanokv_b200.layers.attention import Attention
     from nanokv_b200.utils.context import reset_context, set_context
@@ -295,7 +302,8 @@ def run_gpu(args, rank, world, dev):
     # ---- the other BASELINE configs as kernel-level lines (rank 0's shard);
     # the big KV of the main workload is released first
     lens = st["lens"]
-    del kv, st, layers
+    # every holder of a view of the KV (the last layer built above included)
+    del kv, st, layers, a
     torch.cuda.empty_cache()
     extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world),
              "config4_prefill": measure_prefill(dev, world),
@@ -309,8 +317,53 @@ def run_gpu(args, rank, world, dev):
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms, dec_avg = vals.tolist()
     alg = algorithmic_decode_bytes(lens, hk, hq)
+    if ref_gpu is not None:
+        extra["reference_gpu_path"] = {
+            "what": "flash-attn flash_attn_with_kvcache decode + torch index slot write per layer "
+                    "(the reference's GPU path; flash-attn is library code), same inputs",
+            "ms_per_step": round(ref_gpu, 4), "tok_per_s": round(BATCH * 1000.0 / ref_gpu, 1),
+            "ours_speedup": round(ref_gpu / ms * args.steps, 3)}
     return dict(ms=ms, e2e_ms=e2e_ms, dec_avg_ms=dec_avg, alg_bytes=alg, clocks=clk,
                 resident=R, h2d=h2d, d2h=d2h, compress=comp, extra=extra)
+
+
+def reference_gpu_step_ms(args, dev, st, qkv, layer_views, kv, R, bt, cl, sm, scale, hq, hk,
+                          barrier):
+    """ms per config-2 step of the reference's GPU path: per layer the slot
+    write as a torch index store (k_cache.view(-1, Hk*D)[slot] = k, the
+    effect of its Triton store_kvcache) and flash_attn_with_kvcache
+    (nanokvllm/layers/attention.py:104-107). None when flash-attn is absent.
+    Collective-safe: every rank runs the same barriers."""
+    try:
+        from flash_attn import flash_attn_with_kvcache
+    except Exception:
+        barrier()
+        barrier()
+        return None
+    slots = sm.long()
+
+    def step():
+        for layer in range(LAYERS):
+            c = layer % R
+            q, k, v = layer_views(layer, qkv)
+            kv[0, c].view(-1, hk * D)[slots] = k.reshape(BATCH, hk * D)
+            kv[1, c].view(-1, hk * D)[slots] = v.reshape(BATCH, hk * D)
+            flash_attn_with_kvcache(q.unsqueeze(1), kv[0, c], kv[1, c], cache_seqlens=cl,
+                                    block_table=bt, softmax_scale=scale, causal=True)
+
+    for _ in range(max(1, min(args.warmup, 3))):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(1, min(args.steps, 5))
+    a.record()
+    for _ in range(n):
+        step()
+    b.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    return a.elapsed_time(b) / n
 
 
 def measure_compress(dev, hq, hk):
