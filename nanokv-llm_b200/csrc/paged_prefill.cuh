@@ -137,12 +137,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
 // Shared-memory address of K stage s (the last one is the q-tile buffer).
 __device__ __forceinline__ uint8_t* k_stage(uint8_t* k_mem, uint8_t* q_mem, int s) {
   return s < kPrefillKSmemStages ? k_mem + s * kPrefillTileBytes : q_mem;
