@@ -161,3 +161,46 @@ def test_threshold_events_truncate():
                                   "freed_block_ids": []}], bm)
     assert s.num_tokens == 513 and len(s.block_table) == 3
     assert list(bm.free_block_ids)[-1] == 3 or 3 in bm.free_block_ids
+
+
+def test_device_select_host_half_matches_host_selection():
+    """The host half of the graph-captured compression step: fill_context_device
+    uploads only the tail counters, and events_from_device, given the -1-padded
+    list the device selection copies back, builds the same events as the
+    host-selected path (oracle.window_compress.compression_events)."""
+    import torch
+
+    from oracle.window_compress import compression_events
+
+    Sequence.counter = count()
+    lens = (1500, 900, 2000, 1279, 3000)
+    tails = (1024, 2000, 1100, 1024, 5)
+    seqs = [Sequence(list(range(L))) for L in lens]
+    nxt = 0
+    for s, t in zip(seqs, tails):
+        s.block_table = list(range(nxt, nxt + s.num_blocks))
+        nxt += s.num_blocks
+        s.tail_uncompressed_len = t
+    cfg = types.SimpleNamespace(kv_compress_period=2, kv_compress_topk=4, kv_compress_window_blocks=4)
+    host_sched = PeriodicCompressScheduler(cfg, 256)
+    dev_sched = PeriodicCompressScheduler(cfg, 256)
+    bufs = dev_sched.device_buffers(8, "cpu")
+    meta = DecodeMetadata.build(seqs, 256)
+    for step in (1, 2):
+        is_step, sel, _ = host_sched.select(seqs)
+        ctx = Context(use_decode_kernel=True, context_lens=torch.from_numpy(meta.context_lens))
+        assert dev_sched.fill_context_device(ctx, seqs, bufs) == is_step
+        assert ctx.compress_device_select and not ctx.compress_any
+        assert ctx.compress_selected_t is bufs["selected"] and ctx.compress_topk == 4
+        if not is_step:
+            continue
+        # 1279 % 256 == 255 and the last tail is short: rows 0 and 2 only
+        assert sel == [0, 2]
+        assert ctx.compress_tail_uncompressed_t.tolist() == list(tails)
+        selected_host = sel + [-1] * (cfg.kv_compress_topk - len(sel))
+        window_tokens, keep_tokens = 4 * 256, 2 * 256 + 1
+        new_lens = torch.tensor([lens[b] - window_tokens + keep_tokens for b in sel])
+        events = dev_sched.events_from_device(selected_host, list(lens), meta.block_tables.tolist(),
+                                              keep_blocks=2, keep_extra_tokens=1, num_layers=28)
+        assert events == compression_events(torch.from_numpy(meta.block_tables), sel, new_lens,
+                                            256, 27)
