@@ -223,25 +223,52 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
 /*   y[t, :] = sum over ranks of x_rank[t, :] @ w_rank^T                    */
 /* x [tokens, k] bf16 (row stride ldx), w [n, k] bf16 (the rank's weight     */
 /* shard, row stride ldw), y [tokens, n] bf16 (row stride ldy). Each rank    */
-/* writes its fp32 partial product to its copy of a symmetric fp32          */
-/* [tokens, n] buffer (part_local; part_mc = the buffer's multicast          */
-/* address); after an in-kernel barrier every rank sums its 1/world slice    */
-/* through NVLink SHARP (multimem.ld_reduce) and broadcasts the bf16 result  */
-/* into every rank's copy of a symmetric bf16 [tokens, n] buffer (out_mc /   */
-/* out_local); after a second barrier it copies the result to y. sig_mc /    */
-/* sig_local: a symmetric uint32[2 * world] of epoch slots; flags: this      */
-/* rank's uint32[5] (arrival counters, release flags, the epoch); slots and  */
-/* flags zeroed once. The epoch is read and advanced on the device, so every */
-/* rank must make the same sequence of calls and a CUDA graph may replay     */
-/* them. Waits are bounded by timeout_ns (then NKV_DEVERR_WAIT_TIMEOUT).     */
-/* Needs k % 64 == 0, n % 32 == 0, 16-byte aligned x, w, y and buffers, row  */
-/* strides multiples of 8. Cooperative launch: n / 32 (or / 64, / 128) CTAs  */
-/* must fit the GPU.                                                         */
+/* writes its partial product, rounded to bf16 as F.linear's output is, to  */
+/* its copy of a symmetric bf16 [tokens, n] buffer (part_local; part_mc =   */
+/* the buffer's multicast address); after an in-kernel barrier every rank   */
+/* sums its 1/world slice in fp32 through NVLink SHARP (multimem.ld_reduce  */
+/* .acc::f32) and broadcasts the bf16 result into every rank's copy of a    */
+/* symmetric bf16 [tokens, n] buffer (out_mc / out_local); after a second    */
+/* barrier it copies the result to y. sig_mc / sig_local: a symmetric       */
+/* uint32[2 * world] of epoch slots; flags: this rank's uint32[5] (arrival  */
+/* counters, release flags, the epoch); slots and flags zeroed once. The    */
+/* epoch is read and advanced on the device, so every rank must make the    */
+/* same sequence of calls and a CUDA graph may replay them. Waits are       */
+/* bounded by timeout_ns (then NKV_DEVERR_WAIT_TIMEOUT). Needs k % 64 == 0,  */
+/* n % 32 == 0, 16-byte aligned x, w, y and buffers, row strides multiples  */
+/* of 8. Cooperative launch of (n / TN) * S CTAs, TN in {32, 64, 128}        */
+/* output columns per tile and S in {1, 2, 4} CTAs per tile (a cluster,      */
+/* each CTA a K / S range, their fp32 partial tiles summed through          */
+/* `workspace`, a 16-byte aligned device buffer of workspace_bytes: S > 1   */
+/* needs S * ceil(tokens / 128) * 128 * n * 4 bytes, so 16 * 512 * n bytes   */
+/* allow every S; with null or less, S = 1). The launch picks the pair that */
+/* streams the fewest bytes per CTA and fits the GPU at once.               */
 int nkv_oproj_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t tokens,
                         int32_t k, int32_t n, void* part_mc, void* part_local, void* out_mc,
                         const void* out_local, void* sig_mc, void* sig_local, uint32_t* flags,
-                        int32_t rank, int32_t world, uint64_t timeout_ns, void* y, int64_t ldy,
-                        void* stream);
+                        int32_t rank, int32_t world, uint64_t timeout_ns, void* workspace,
+                        int64_t workspace_bytes, void* y, int64_t ldy, void* stream);
+
+/* One-shot variant of the same replacement, without NVLink multicast: each  */
+/* rank stores its bf16 partial (rounded as F.linear's output is) straight   */
+/* from the GEMM epilogue into its slot of EVERY rank's receive buffer       */
+/* (plain stores through peer mappings, NVLink for the other ranks), then    */
+/* one in-kernel barrier, then every rank sums the world slots in rank order */
+/* (fp32, so all ranks hold the same bf16 result) into y. recv_peers: device */
+/* array of world pointers, rank q's receive buffer of                       */
+/* [2 parities][world][slot_stride] bf16 (slot_stride >= tokens * n, a       */
+/* multiple of 8); the parity alternates per call, so a rank's next call     */
+/* never overwrites a slot a peer is still summing. sig_peers: device array  */
+/* of world pointers to each rank's uint32[2 * world] epoch slots (sig_local */
+/* = this rank's). flags, epoch, waits, limits, workspace and the           */
+/* cooperative cluster launch as nkv_oproj_allreduce. Egress per rank:       */
+/* (world - 1) x the partial, so it suits small TP groups.                  */
+int nkv_oproj_allreduce_p2p(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                            int32_t tokens, int32_t k, int32_t n, void* const* recv_peers,
+                            int64_t slot_stride, uint32_t* const* sig_peers, void* sig_local,
+                            uint32_t* flags, int32_t rank, int32_t world, uint64_t timeout_ns,
+                            void* workspace, int64_t workspace_bytes, void* y, int64_t ldy,
+                            void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 3a. Periodic window compression (one layer, all selected sequences)       */

@@ -453,6 +453,129 @@ int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
 
 }  // namespace
 
+// ---------------------------------------------------------------- o_proj + all-reduce
+namespace {
+
+// Tiling choice and cooperative launch of oproj_allreduce_kernel; `p` comes
+// with its buffers, rank and mode filled in.
+int oproj_launch(nkv::OprojParams p, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                 int32_t tokens, int32_t k, int32_t n, void* workspace, int64_t workspace_bytes,
+                 void* y, int64_t ldy, void* stream) {
+  if (tokens > nkv::kOpMaxMTiles * 128 || k % nkv::kOpK != 0 || n % 32 != 0) return NKV_ERR_UNSUPPORTED;
+  if (ldx < k || ldw < k || ldy < n) return NKV_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (ldx % 8) || (ldw % 8) || (ldy % 8) ||
+      !aligned16(workspace))
+    return NKV_ERR_ALIGNMENT;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = sm_count(dev);
+  const int mtiles = (tokens + 127) / 128;
+  constexpr int kSmemLimit = 227 * 1024;
+  const int fixed = 1024 + 256;  // alignment slack, barriers, TMEM slot
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.T = tokens;
+  p.K = k;
+  p.N = n;
+  p.mtiles = mtiles;
+  p.splitk_ws = static_cast<float*>(workspace);
+
+  // Tile width TN and split count S: fewest bytes streamed per CTA
+  // ((rows + TN) * K/S bf16, plus the fp32 tile written and read back for
+  // the cluster sum when S > 1) with at most one CTA per SM, TN * mtiles
+  // TMEM columns, and S fp32 [mtiles * 128, n] slices fitting the workspace.
+  auto stages_for = [&](int tn) {
+    const int stage_bytes = mtiles * nkv::kOpATile + tn * 128;
+    return std::make_pair(std::min(nkv::kOpMaxStages, (kSmemLimit - fixed) / stage_bytes),
+                          stage_bytes);
+  };
+  auto fits = [&](int tn, int S) {
+    if (n % tn != 0 || (n / tn) * S > sms || mtiles * tn > 512) return false;
+    if (k % (S * nkv::kOpK) != 0) return false;
+    const auto st = stages_for(tn);
+    if (st.first < 2) return false;
+    if (S > 1 && (workspace == nullptr ||
+                  static_cast<int64_t>(S) * mtiles * 128 * n * 4 > workspace_bytes))
+      return false;
+    return true;
+  };
+  auto cost = [&](int tn, int S) {
+    const int64_t bytes = static_cast<int64_t>(mtiles * 128 + tn) * (k / S) * 2;
+    return bytes + (S > 1 ? static_cast<int64_t>(mtiles) * 128 * tn * 8 : 0);
+  };
+  auto launch = [&](int tn, int S) -> int {
+    const auto st = stages_for(tn);
+    const int smem = st.first * st.second + fixed;
+    CUtensorMap tx, tw;
+    int rc;
+    if ((rc = encode_2d(&tx, x, k, tokens, ldx * 2, 128)) != NKV_OK) return rc;
+    if ((rc = encode_2d(&tw, w, k, n, ldw * 2, tn)) != NKV_OK) return rc;
+    p.tn = tn;
+    p.splits = S;
+    p.stages = st.first;
+    static int attr_smem[kMaxDevices] = {0};
+    if (dev >= 0 && dev < kMaxDevices && attr_smem[dev] < smem) {
+      cudaError_t e = cudaFuncSetAttribute(nkv::oproj_allreduce_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return cuda_status(e);
+      attr_smem[dev] = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n / tn) * S, 1, 1);
+    cfg.blockDim = dim3(nkv::kOpThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the barrier waits on peers
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = S;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = S > 1 ? 2 : 1;
+    if (S > 1) {
+      cudaLaunchConfig_t q = cfg;  // the cluster shape alone, for the residency query
+      q.attrs = attr + 1;
+      q.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, nkv::oproj_allreduce_kernel, &q) !=
+              cudaSuccess ||
+          clusters < n / tn) {
+        cudaGetLastError();
+        return NKV_ERR_UNSUPPORTED;
+      }
+    }
+    return cuda_status(cudaLaunchKernelEx(&cfg, nkv::oproj_allreduce_kernel, tx, tw, p));
+  };
+
+  int best_tn = 0, best_s = 0;
+  int64_t best = 0;
+  for (int S = 1; S <= nkv::kOpMaxSplits; S *= 2)
+    for (int tn = 32; tn <= 128; tn *= 2)
+      if (fits(tn, S) && (best_tn == 0 || cost(tn, S) < best)) {
+        best = cost(tn, S);
+        best_tn = tn;
+        best_s = S;
+      }
+  if (best_tn == 0) return NKV_ERR_UNSUPPORTED;
+  int rc = launch(best_tn, best_s);
+  if (rc == NKV_OK || best_s == 1) return rc;
+  // the clusters do not all fit at once here, or a cooperative launch of
+  // clusters was refused: the best single-CTA tiling
+  cudaGetLastError();
+  best_tn = 0;
+  for (int tn = 32; tn <= 128; tn *= 2)
+    if (fits(tn, 1) && (best_tn == 0 || cost(tn, 1) < best)) {
+      best = cost(tn, 1);
+      best_tn = tn;
+    }
+  if (best_tn == 0) return NKV_ERR_UNSUPPORTED;
+  return launch(best_tn, 1);
+}
+
+}  // namespace
+
 extern "C" {
 
 int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -562,77 +685,60 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
 int nkv_oproj_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t tokens,
                         int32_t k, int32_t n, void* part_mc, void* part_local, void* out_mc,
                         const void* out_local, void* sig_mc, void* sig_local, uint32_t* flags,
-                        int32_t rank, int32_t world, uint64_t timeout_ns, void* y, int64_t ldy,
-                        void* stream) {
+                        int32_t rank, int32_t world, uint64_t timeout_ns, void* workspace,
+                        int64_t workspace_bytes, void* y, int64_t ldy, void* stream) {
   if (tokens < 0 || k <= 0 || n <= 0 || world < 1 || rank < 0 || rank >= world)
     return NKV_ERR_INVALID_ARGUMENT;
   if (tokens == 0) return NKV_OK;
   if (!x || !w || !part_mc || !part_local || !out_mc || !out_local || !sig_mc || !sig_local ||
       !flags || !y)
     return NKV_ERR_INVALID_ARGUMENT;
-  if (tokens > nkv::kOpMaxMTiles * 128 || k % nkv::kOpK != 0 || n % 32 != 0) return NKV_ERR_UNSUPPORTED;
-  if (ldx < k || ldw < k || ldy < n) return NKV_ERR_INVALID_ARGUMENT;
-  if (!aligned16(x) || !aligned16(w) || !aligned16(part_mc) || !aligned16(part_local) ||
-      !aligned16(out_mc) || !aligned16(out_local) || !aligned16(y) || (ldx % 8) || (ldw % 8) ||
-      (ldy % 8) || (reinterpret_cast<uintptr_t>(sig_mc) & 3u) ||
+  if (!aligned16(part_mc) || !aligned16(part_local) || !aligned16(out_mc) ||
+      !aligned16(out_local) || (reinterpret_cast<uintptr_t>(sig_mc) & 3u) ||
       (reinterpret_cast<uintptr_t>(sig_local) & 3u))
     return NKV_ERR_ALIGNMENT;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int sms = sm_count(dev);
-  const int mtiles = (tokens + 127) / 128;
-  int tn = 32;
-  while ((n / tn > sms || n % tn != 0) && tn < 128) tn *= 2;
-  if (n % tn != 0 || n / tn > sms || mtiles * tn > 512) return NKV_ERR_UNSUPPORTED;
-  const int stage_bytes = mtiles * nkv::kOpATile + tn * 128;
-  constexpr int kSmemLimit = 227 * 1024;
-  const int fixed = 1024 + 256;  // alignment slack, barriers, TMEM slot
-  const int stages = std::min(nkv::kOpMaxStages, (kSmemLimit - fixed) / stage_bytes);
-  if (stages < 2) return NKV_ERR_UNSUPPORTED;
-  const int smem = stages * stage_bytes + fixed;
-
-  CUtensorMap tx, tw;
-  int st;
-  if ((st = encode_2d(&tx, x, k, tokens, ldx * 2, 128)) != NKV_OK) return st;
-  if ((st = encode_2d(&tw, w, k, n, ldw * 2, tn)) != NKV_OK) return st;
   nkv::OprojParams p{};
-  p.part_mc = static_cast<float*>(part_mc);
-  p.part_local = static_cast<float*>(part_local);
+  p.part_mc = static_cast<__nv_bfloat16*>(part_mc);
+  p.part_local = static_cast<__nv_bfloat16*>(part_local);
   p.out_mc = static_cast<__nv_bfloat16*>(out_mc);
   p.out_local = static_cast<const __nv_bfloat16*>(out_local);
   p.sig_mc = static_cast<uint32_t*>(sig_mc);
   p.sig_local = static_cast<uint32_t*>(sig_local);
   p.flags = reinterpret_cast<unsigned int*>(flags);
-  p.y = static_cast<__nv_bfloat16*>(y);
-  p.ldy = ldy;
-  p.T = tokens;
-  p.K = k;
-  p.N = n;
-  p.mtiles = mtiles;
-  p.tn = tn;
-  p.stages = stages;
   p.rank = rank;
   p.world = world;
+  p.one_shot = 0;
   p.timeout_ns = timeout_ns;
+  return oproj_launch(p, x, ldx, w, ldw, tokens, k, n, workspace, workspace_bytes, y, ldy, stream);
+}
 
-  static int attr_smem[kMaxDevices] = {0};
-  if (dev >= 0 && dev < kMaxDevices && attr_smem[dev] < smem) {
-    cudaError_t e = cudaFuncSetAttribute(nkv::oproj_allreduce_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_smem[dev] = smem;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(n / tn, 1, 1);
-  cfg.blockDim = dim3(nkv::kOpThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the barrier waits on peers
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::oproj_allreduce_kernel, tx, tw, p));
+int nkv_oproj_allreduce_p2p(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                            int32_t tokens, int32_t k, int32_t n, void* const* recv_peers,
+                            int64_t slot_stride, uint32_t* const* sig_peers, void* sig_local,
+                            uint32_t* flags, int32_t rank, int32_t world, uint64_t timeout_ns,
+                            void* workspace, int64_t workspace_bytes, void* y, int64_t ldy,
+                            void* stream) {
+  if (tokens < 0 || k <= 0 || n <= 0 || world < 1 || rank < 0 || rank >= world)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (tokens == 0) return NKV_OK;
+  if (!x || !w || !recv_peers || !sig_peers || !sig_local || !flags || !y)
+    return NKV_ERR_INVALID_ARGUMENT;
+  if (slot_stride < static_cast<int64_t>(tokens) * n) return NKV_ERR_INVALID_ARGUMENT;
+  if ((slot_stride % 8) || (reinterpret_cast<uintptr_t>(recv_peers) & 7u) ||
+      (reinterpret_cast<uintptr_t>(sig_peers) & 7u) ||
+      (reinterpret_cast<uintptr_t>(sig_local) & 3u))
+    return NKV_ERR_ALIGNMENT;
+  nkv::OprojParams p{};
+  p.recv_peers = reinterpret_cast<__nv_bfloat16* const*>(recv_peers);
+  p.sig_peers = reinterpret_cast<uint32_t* const*>(sig_peers);
+  p.slot_stride = slot_stride;
+  p.sig_local = static_cast<uint32_t*>(sig_local);
+  p.flags = reinterpret_cast<unsigned int*>(flags);
+  p.rank = rank;
+  p.world = world;
+  p.one_shot = 1;
+  p.timeout_ns = timeout_ns;
+  return oproj_launch(p, x, ldx, w, ldw, tokens, k, n, workspace, workspace_bytes, y, ldy, stream);
 }
 
 // ---------------------------------------------------------------- prefill

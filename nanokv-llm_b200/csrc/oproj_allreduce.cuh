@@ -2,22 +2,29 @@
 // the B200 replacement for RowParallelLinear.forward,
 //   y = F.linear(x, W_local); dist.all_reduce(y)     nanokvllm/layers/linear.py:151-155
 // for decode-sized token counts (T <= 512), in ONE kernel per rank:
-//   * tcgen05 GEMM: CTA c owns output columns [c*TN, (c+1)*TN) of the
-//     hidden dim for all T rows (up to four 128-row M tiles, accumulated in
-//     TMEM), x and the W slice streamed by TMA (128-byte swizzle, no
-//     multicast) through a ring of up to 4 stages, one thread issuing UMMA
-//     128 x TN x 16.
-//   * epilogue: the fp32 partial tile goes from TMEM to this rank's copy of
-//     a symmetric fp32 [T, N] partial buffer (local stores);
+//   * tcgen05 GEMM: output tile t (columns [t*TN, (t+1)*TN) of the hidden
+//     dim, all T rows in up to four 128-row M tiles accumulated in TMEM) is
+//     computed by a cluster of S CTAs, CTA j taking the K range
+//     [j*K/S, (j+1)*K/S) -- so each CTA streams only 1/S of x and of its W
+//     slice (TMA, 128-byte swizzle, no multicast, a ring of up to 6
+//     stages; one thread issues UMMA 128 x TN x 16);
+//   * epilogue: each CTA stores its fp32 partial tile to an L2-resident
+//     workspace, the cluster synchronises, and CTA j sums rows
+//     [j*Tp/S, (j+1)*Tp/S) over the S K ranges, rounds them to bf16 (the
+//     reference's F.linear output type) and emits them; with S = 1 the
+//     tile goes from TMEM to bf16 directly. Emitting means: to this rank's
+//     copy of a symmetric bf16 [T, N] partial buffer (two-shot mode), or
+//     into this rank's slot of every rank's receive buffer (one-shot mode,
+//     below);
 //   * barrier 1 (all ranks' partials written), then each rank reduces its
-//     1/world slice of the T x N elements with multimem.ld_reduce (NVLink
-//     SHARP: the NVSwitch reads every rank's partial and returns the fp32
-//     sum), rounds it to bf16 and broadcasts it into every rank's copy of a
-//     symmetric bf16 [T, N] buffer with multimem.st -- each element crosses
-//     NVLink once per direction and partials are never rounded before the
-//     sum;
-//   * barrier 2 (all slices broadcast), then each CTA copies its share of
-//     the gathered result to y.
+//     1/world slice of the T x N elements with
+//     multimem.ld_reduce.add.acc::f32 (NVLink SHARP: the NVSwitch reads
+//     every rank's bf16 partial, sums in fp32 and returns bf16) and
+//     broadcasts it into every rank's copy of a symmetric bf16 [T, N]
+//     result buffer with multimem.st -- each element crosses NVLink once
+//     per direction; every thread keeps four 16-byte reductions in flight;
+//   * barrier 2 (all slices broadcast), then the tile's CTAs copy their
+//     share of the gathered result to y.
 // A barrier: after fence.acq_rel.sys and a device-scope arrival counter, the
 // last CTA of the rank stores the call's epoch into every rank's slot with
 // multimem.st.release and waits for all ranks' epochs (bounded by
@@ -39,22 +46,34 @@ constexpr int kOpMaxStages = 6;    // ring depth (fewer when the M tiles are man
 constexpr int kOpThreads = 192;     // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
 constexpr int kOpMaxMTiles = 4;     // T <= 512
 constexpr int kOpATile = 128 * 128;  // one 128-row x 64-K bf16 tile, bytes
+constexpr int kOpMaxSplits = 4;     // cluster size along K
+constexpr int kOpReduceUnroll = 4;  // switch reductions in flight per thread
+constexpr int kOpSumBatch = 4;      // one-shot: result groups per thread in flight
+
 
 struct OprojParams {
-  float* part_mc;         // multicast address of the fp32 [T, N] partial buffer
-  float* part_local;      // this rank's copy of it
+  // two-shot (NVLS) mode
+  __nv_bfloat16* part_mc;  // multicast address of the bf16 [T, N] partial buffer
+  __nv_bfloat16* part_local;       // this rank's copy of it
   __nv_bfloat16* out_mc;  // multicast address of the bf16 [T, N] gathered result
   const __nv_bfloat16* out_local;  // this rank's copy of it
   uint32_t* sig_mc;       // multicast address of the [2][world] epoch slots
+  // one-shot (peer-store) mode, device arrays indexed by rank
+  __nv_bfloat16* const* recv_peers;  // each rank's [2 parities][world][slot_stride] bf16
+  uint32_t* const* sig_peers;        // each rank's [2][world] epoch slots
+  int64_t slot_stride;               // elements per (parity, source rank) slot, >= T * N
   uint32_t* sig_local;    // this rank's copy of the slots
+  float* splitk_ws;       // S > 1: fp32 partial tiles, [S][N / TN][TN / 4][mtiles * 128][4]
   unsigned int* flags;    // this rank's [ctr 1, go 1, ctr 2, go 2, epoch]
   __nv_bfloat16* y;
   int64_t ldy;
   int T, K, N;
   int mtiles;             // ceil(T / 128)
-  int tn;                 // output columns per CTA: 32, 64 or 128
+  int tn;                 // output columns per tile: 32, 64 or 128
+  int splits;             // S: CTAs (one cluster) per tile, each a K / S range
   int stages;             // <= kOpMaxStages
   int rank, world;
+  int one_shot;           // 1: peer-store mode, 0: NVLS mode
   uint64_t timeout_ns;
 };
 
@@ -86,10 +105,29 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint4 pack8_bf16(const float (&a)[8]) {
+  return make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
+                    pack_bf16x2(a[6], a[7]));
+}
+
 // Cross-rank barrier `which` (0 or 1) of the call with `epoch`: every CTA
-// arrives once; the rank's last CTA signals all ranks and waits for theirs,
-// then releases the rank's CTAs. Bounded by p.timeout_ns.
-__device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, uint32_t epoch) {
+// arrives once; the rank's last CTA signals all ranks (one multicast store,
+// or a release store into each rank's slot) and waits for theirs, then
+// releases the rank's CTAs; at the call's last barrier it also stores the
+// epoch as the next call's base. Bounded by p.timeout_ns.
+__device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, uint32_t epoch,
+                                             bool last) {
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned int* ctr = p.flags + 2 * which;
@@ -97,11 +135,22 @@ __device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, ui
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     const unsigned int old = atomic_add_acq_rel_gpu(ctr, 1u);
     if (old == gridDim.x - 1) {
+      // every CTA's writes precede its arrival (its system fence, then the
+      // counter, which this CTA acquired); one system fence here, then
+      // relaxed signal stores, forms the release the other ranks acquire
       asm volatile("fence.acq_rel.sys;" ::: "memory");
-      asm volatile("multimem.st.release.sys.global.b32 [%0], %1;" ::"l"(
-                       p.sig_mc + which * p.world + p.rank),
-                   "r"(epoch)
-                   : "memory");
+      if (p.one_shot) {
+        for (int r = 0; r < p.world; ++r)
+          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(
+                           p.sig_peers[r] + which * p.world + p.rank),
+                       "r"(epoch)
+                       : "memory");
+      } else {
+        asm volatile("multimem.st.relaxed.sys.global.b32 [%0], %1;" ::"l"(
+                         p.sig_mc + which * p.world + p.rank),
+                     "r"(epoch)
+                     : "memory");
+      }
       const uint64_t t0 = global_ns();
       for (int r = 0; r < p.world; ++r) {
         while (static_cast<int32_t>(ld_acquire_sys(p.sig_local + which * p.world + r) - epoch) < 0) {
@@ -113,7 +162,7 @@ __device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, ui
         }
       }
       *ctr = 0u;
-      if (which == 1) p.flags[4] = epoch;  // the next call's base (all CTAs have read it)
+      if (last) p.flags[4] = epoch;  // the next call's base (all CTAs have read it)
       asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(go), "r"(epoch) : "memory");
     } else {
       const uint64_t t0 = global_ns();
@@ -127,6 +176,24 @@ __device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, ui
     }
   }
   __syncthreads();
+}
+
+// One 8-column bf16 group of this rank's partial: to the NVLS partial
+// buffer, or (one-shot) into this rank's slot of every rank's receive buffer
+// of the call's parity -- a local store for this rank, NVLink stores for the
+// others, issued while other tiles are still in their GEMM.
+__device__ __forceinline__ void emit_partial(const OprojParams& p, int r, int col, uint4 v,
+                                             uint32_t parity) {
+  const int64_t off = static_cast<int64_t>(r) * p.N + col;
+  if (!p.one_shot) {
+    *reinterpret_cast<uint4*>(p.part_local + off) = v;
+    return;
+  }
+  const int64_t slot = (static_cast<int64_t>(parity) * p.world + p.rank) * p.slot_stride + off;
+  for (int i = 0; i < p.world; ++i) {
+    const int q = (p.rank + 1 + i) % p.world;  // peers first, this rank last
+    *reinterpret_cast<uint4*>(p.recv_peers[q] + slot) = v;
+  }
 }
 
 __global__ void __launch_bounds__(kOpThreads, 1)
@@ -146,12 +213,17 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * p.tn;
+  const int S = p.splits;
+  const int split = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int n0 = (blockIdx.x / S) * p.tn;
+  const int kper = p.K / S;
+  const int k0 = split * kper;
   // The call's epoch lives on the device (so the launch can be replayed from
   // a CUDA graph): every CTA reads it here, before it arrives at the
   // counter that lets the last CTA advance it.
   const uint32_t epoch = ld_acquire_gpu(p.flags + 4) + 1u;
-  const int ksteps = p.K / kOpK;
+  const uint32_t parity = epoch & 1u;
+  const int ksteps = kper / kOpK;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(p.mtiles * p.tn)) cols <<= 1;
 
@@ -173,12 +245,13 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   const uint32_t tmem = *tmem_slot;
   grid_dependency_wait();
 
+  bool acc_ok = false;
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_w);
-      uint32_t armed = 0u, parity = 0u;
+      uint32_t armed = 0u, par = 0u;
       for (int ks = 0; ks < ksteps; ++ks) {
         const int s = ks % stages;
         const uint32_t ph = (ks / stages) & 1;
@@ -187,14 +260,14 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
         const uint32_t fb = smem_u32(&full[s]);
         mbar_arrive_expect_tx(fb, stage_bytes);
         armed |= 1u << s;
-        parity = (parity & ~(1u << s)) | (ph << s);
+        par = (par & ~(1u << s)) | (ph << s);
         const uint32_t base = smem_u32(smem + s * stage_bytes);
         for (int mt = 0; mt < p.mtiles; ++mt)
-          tma_load_2d(base + mt * kOpATile, &tm_x, fb, ks * kOpK, mt * 128);
-        tma_load_2d(base + p.mtiles * kOpATile, &tm_w, fb, ks * kOpK, n0);
+          tma_load_2d(base + mt * kOpATile, &tm_x, fb, k0 + ks * kOpK, mt * 128);
+        tma_load_2d(base + p.mtiles * kOpATile, &tm_w, fb, k0 + ks * kOpK, n0);
       }
       for (int s = 0; s < stages; ++s)
-        if (armed & (1u << s)) mbar_wait_bounded(smem_u32(&full[s]), (parity >> s) & 1u);
+        if (armed & (1u << s)) mbar_wait_bounded(smem_u32(&full[s]), (par >> s) & 1u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -226,24 +299,44 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     if (lane == 0) umma_commit(smem_u32(acc_full));
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue
+    acc_ok = mbar_wait_bounded(smem_u32(acc_full), 0);
+  }
+
+  // ---------------------------------------------------------------- epilogue
+  // warps 2-5, thread = one accumulator row. S = 1: bf16 groups straight to
+  // their destinations. S > 1: the fp32 row to this K range's block of the
+  // workspace, laid out [column / 4][row][4] so that a warp's 16-byte stores
+  // (32 consecutive rows) cover 512 contiguous bytes; rows
+  // [j*Tp/S, (j+1)*Tp/S) are then summed by cluster CTA j
+  const int tp = p.mtiles * 128;
+  const int rows = tp / S;
+  float* ws_tile = p.splitk_ws + (static_cast<int64_t>(split) * (p.N / p.tn) + blockIdx.x / S) *
+                                     p.tn * tp;
+  if (warp >= 2 && acc_ok) {
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, +32)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    if (mbar_wait_bounded(smem_u32(acc_full), 0)) {
-      tc_fence_after();
-      for (int mt = 0; mt < p.mtiles; ++mt) {
-        const int r = mt * 128 + quarter * 32 + lane;
-        for (int c = 0; c < p.tn; c += 32) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_base + mt * p.tn + c, v);
-          tmem_ld_wait(v);
-          if (r < p.T) {
-            float4* dst = reinterpret_cast<float4*>(p.part_local + static_cast<int64_t>(r) * p.N +
-                                                    n0 + c);
+    tc_fence_after();
+    for (int mt = 0; mt < p.mtiles; ++mt) {
+      const int r = mt * 128 + quarter * 32 + lane;
+      for (int c = 0; c < p.tn; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + mt * p.tn + c, v);
+        tmem_ld_wait(v);
+        if (r >= p.T) {
+        } else if (S > 1) {
+          float4* dst = reinterpret_cast<float4*>(ws_tile) + static_cast<int64_t>(c / 4) * tp + r;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          for (int i = 0; i < 8; ++i)
+            __stcg(dst + static_cast<int64_t>(i) * tp,
+                   make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float a[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a[e] = __uint_as_float(v[8 * i + e]);
+            emit_partial(p, r, n0 + c + 8 * i, pack8_bf16(a), parity);
           }
         }
       }
@@ -256,38 +349,142 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     tmem_dealloc(tmem, cols);
   }
 
+  if (S > 1) {
+    // ------------------------------------ split-K sum of this CTA's rows
+    // the cluster barrier (release / acquire at cluster scope) makes every
+    // CTA's workspace block visible. A warp takes 8 rows x 4 eight-column
+    // groups (its workspace reads: 128 contiguous bytes per group; its
+    // emitted stores: 64 contiguous bytes per row), all S blocks' loads
+    // issued before the sums, which run in block (= K range) order; the
+    // result is rounded to bf16 and emitted
+    cluster_sync_all();
+    const int groups = p.tn / 8;          // 8-column groups per row: 4, 8 or 16
+    const int r0 = split * rows;          // rows is a multiple of 32
+    const int tiles = (rows / 8) * (groups / 4);
+    const int rsub = lane & 7, gsub = lane >> 3;
+    for (int t = warp; t < tiles; t += kOpThreads / 32) {
+      const int lr = (t % (rows / 8)) * 8 + rsub;
+      const int g = (t / (rows / 8)) * 4 + gsub;
+      const int r = r0 + lr;
+      if (r >= p.T) continue;
+      float4 u[kOpMaxSplits][2];
+#pragma unroll
+      for (int q = 0; q < kOpMaxSplits; ++q) {
+        if (q < S) {
+          const float4* src = reinterpret_cast<const float4*>(
+                                  p.splitk_ws + (static_cast<int64_t>(q) * (p.N / p.tn) +
+                                                 blockIdx.x / S) * p.tn * tp) +
+                              static_cast<int64_t>(2 * g) * tp + r;
+          u[q][0] = __ldcg(src);
+          u[q][1] = __ldcg(src + tp);
+        }
+      }
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < kOpMaxSplits; ++q) {
+        if (q < S) {
+          a[0] += u[q][0].x; a[1] += u[q][0].y; a[2] += u[q][0].z; a[3] += u[q][0].w;
+          a[4] += u[q][1].x; a[5] += u[q][1].y; a[6] += u[q][1].z; a[7] += u[q][1].w;
+        }
+      }
+      emit_partial(p, r, n0 + 8 * g, pack8_bf16(a), parity);
+    }
+  }
+
+  const int per_row = p.tn / 8;
+  if (p.one_shot) {
+    // ------------------------------------------------------------ barrier
+    rank_barrier(p, 0, epoch, true);
+    // every rank's partial of this tile is in this rank's receive buffer:
+    // sum them in rank order (the same order on every rank, so every rank
+    // holds the same result) and write y; the tile's S CTAs share the rows
+    // (kOpSumBatch groups per thread at a time, each slot's loads issued
+    // together)
+    const __nv_bfloat16* recv = p.recv_peers[p.rank] +
+                                static_cast<int64_t>(parity) * p.world * p.slot_stride;
+    const int items = p.T * per_row;
+    const int step = S * kOpThreads;
+    for (int i0 = split * kOpThreads + threadIdx.x; i0 < items; i0 += kOpSumBatch * step) {
+      int64_t off[kOpSumBatch];
+#pragma unroll
+      for (int b = 0; b < kOpSumBatch; ++b) {
+        const int i = i0 + b * step;
+        const int r = i / per_row;
+        off[b] = i < items ? static_cast<int64_t>(r) * p.N + n0 + (i - r * per_row) * 8 : -1;
+      }
+      float a[kOpSumBatch][8] = {};
+      for (int q = 0; q < p.world; ++q) {
+        uint4 u[kOpSumBatch];
+#pragma unroll
+        for (int b = 0; b < kOpSumBatch; ++b)
+          if (off[b] >= 0)
+            u[b] = __ldcg(reinterpret_cast<const uint4*>(recv + q * p.slot_stride + off[b]));
+#pragma unroll
+        for (int b = 0; b < kOpSumBatch; ++b) {
+          if (off[b] < 0) continue;
+          const uint32_t w4[4] = {u[b].x, u[b].y, u[b].z, u[b].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            a[b][2 * e] += __uint_as_float(w4[e] << 16);
+            a[b][2 * e + 1] += __uint_as_float(w4[e] & 0xffff0000u);
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kOpSumBatch; ++b) {
+        if (off[b] < 0) continue;
+        const int i = i0 + b * step;
+        const int r = i / per_row;
+        *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(r) * p.ldy + n0 +
+                                  (i - r * per_row) * 8) = pack8_bf16(a[b]);
+      }
+    }
+    return;
+  }
+
   // ---------------------------------------------------------------- barrier 1
-  rank_barrier(p, 0, epoch);
+  rank_barrier(p, 0, epoch, false);
 
   // ------------------------------------------------- reduce this rank's slice
-  // elements [lo, hi) of the T x N result, 4 per step: fp32 sum of every
-  // rank's partial through the switch, bf16 to every rank's result buffer
+  // 16-byte groups [lo, hi) of the T x N result: fp32 sum of every rank's
+  // bf16 partial through the switch, bf16 to every rank's result buffer;
+  // kOpReduceUnroll reductions in flight per thread before their stores
   {
-    const int64_t total4 = static_cast<int64_t>(p.T) * p.N / 4;
-    const int64_t lo = total4 * p.rank / p.world, hi = total4 * (p.rank + 1) / p.world;
+    const int64_t total8 = static_cast<int64_t>(p.T) * p.N / 8;
+    const int64_t lo = total8 * p.rank / p.world, hi = total8 * (p.rank + 1) / p.world;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kOpThreads;
-    for (int64_t i = lo + static_cast<int64_t>(blockIdx.x) * kOpThreads + threadIdx.x; i < hi;
-         i += stride) {
-      float a, b, c, d;
-      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-                   : "=f"(a), "=f"(b), "=f"(c), "=f"(d)
-                   : "l"(p.part_mc + 4 * i)
-                   : "memory");
-      const float lo2 = __uint_as_float(pack_bf16x2(a, b));
-      const float hi2 = __uint_as_float(pack_bf16x2(c, d));
-      asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(p.out_mc + 4 * i),
-                   "f"(lo2), "f"(hi2)
-                   : "memory");
+    for (int64_t i0 = lo + static_cast<int64_t>(blockIdx.x) * kOpThreads + threadIdx.x; i0 < hi;
+         i0 += kOpReduceUnroll * stride) {
+      uint32_t v[kOpReduceUnroll][4];
+#pragma unroll
+      for (int u = 0; u < kOpReduceUnroll; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < hi)
+          asm volatile(
+              "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+              : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3])
+              : "l"(p.part_mc + 8 * i)
+              : "memory");
+      }
+#pragma unroll
+      for (int u = 0; u < kOpReduceUnroll; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < hi)
+          asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                           p.out_mc + 8 * i),
+                       "f"(__uint_as_float(v[u][0])), "f"(__uint_as_float(v[u][1])),
+                       "f"(__uint_as_float(v[u][2])), "f"(__uint_as_float(v[u][3]))
+                       : "memory");
+      }
     }
   }
 
   // ---------------------------------------------------------------- barrier 2
-  rank_barrier(p, 1, epoch);
+  rank_barrier(p, 1, epoch, true);
 
   // ---------------------------------------------------------------- copy out
-  // this CTA's columns of the gathered bf16 result -> y
-  const int per_row = p.tn / 8;
-  for (int i = threadIdx.x; i < p.T * per_row; i += kOpThreads) {
+  // the tile's columns of the gathered bf16 result -> y, shared by its S CTAs
+  for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
     const int r = i / per_row;
     const int c = n0 + (i - r * per_row) * 8;
     const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.out_local + static_cast<int64_t>(r) * p.N + c));

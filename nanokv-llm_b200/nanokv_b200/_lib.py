@@ -70,7 +70,12 @@ SIGNATURES: dict[str, tuple] = {
     "nkv_oproj_allreduce": (
         c_int,
         [_P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P,
-         c_int32, c_int32, c_uint64, _P, c_int64, _P],
+         c_int32, c_int32, c_uint64, _P, c_int64, _P, c_int64, _P],
+    ),
+    "nkv_oproj_allreduce_p2p": (
+        c_int,
+        [_P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P, c_int64, _P, _P, _P,
+         c_int32, c_int32, c_uint64, _P, c_int64, _P, c_int64, _P],
     ),
     "nkv_paged_prefill": (
         c_int,

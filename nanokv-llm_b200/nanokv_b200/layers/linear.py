@@ -3,10 +3,12 @@
 The reference's RowParallelLinear.forward (nanokvllm/layers/linear.py:151-155)
 runs F.linear on the rank's weight shard and then dist.all_reduce of the
 bf16 result (NCCL). OProjAllReduce does both in ONE kernel per rank
-(nkv_oproj_allreduce): a tcgen05 GEMM writing fp32 partials to a symmetric
-buffer, an in-kernel cross-rank barrier, each rank's slice summed through
-NVLink SHARP (multimem.ld_reduce) and broadcast as bf16 (multimem.st), a
-second barrier, and the copy to the output.
+(nkv_oproj_allreduce): a split-K tcgen05 GEMM (a cluster of CTAs per output
+tile, summed through distributed shared memory) writing bf16 partials -- the
+reference's F.linear output type -- to a symmetric buffer, an in-kernel
+cross-rank barrier, each rank's slice summed in fp32 through NVLink SHARP
+(multimem.ld_reduce) and broadcast as bf16 (multimem.st), a second barrier,
+and the copy to the output.
 It serves decode-sized steps (tokens <= 512); RowParallelOProj falls back to
 the reference's own two calls for larger (prefill) steps or groups without
 NVLink multicast.
@@ -26,16 +28,28 @@ MAX_FUSED_TOKENS = 512
 class OProjAllReduce:
     """Fused y = all_reduce(x @ w_shard^T) for one process group.
 
+    Two modes, one kernel (nkv_oproj_allreduce / nkv_oproj_allreduce_p2p):
+    one-shot -- every rank stores its bf16 partial from the GEMM epilogue
+    into every rank's receive buffer over NVLink, one in-kernel barrier, a
+    local sum -- which moves (world - 1) partials per rank and suits small
+    groups; and two-shot through NVLink SHARP (NVLS multicast: each rank sums
+    its slice in the switch and broadcasts it, two barriers), whose traffic
+    does not grow with the group. one_shot=None picks one-shot for groups of
+    at most two ranks (and whenever the group has no multicast).
+
     Collective construction (every rank of `group` constructs it, in the same
-    order): allocates a symmetric buffer (fp32 partials and the bf16 result,
-    max_tokens x hidden each, plus the epoch slots) and rendezvouses it
-    (torch symmetric memory), so the kernel gets its NVLS multicast address. Every rank must then
-    make the same sequence of calls; the call counter lives on the device, so
-    the calls can be captured in and replayed from a CUDA graph.
+    order): allocates a symmetric buffer (one-shot: [2 parities][world]
+    receive slots of max_tokens x hidden bf16; two-shot: bf16 partials and
+    the bf16 result, max_tokens x hidden each; plus the epoch slots) and
+    rendezvouses it (torch symmetric memory) for the peers' addresses and the
+    multicast address. Every rank must then make the same sequence of calls;
+    the call counter lives on the device, so the calls can be captured in and
+    replayed from a CUDA graph.
     """
 
     def __init__(self, hidden: int, max_tokens: int = MAX_FUSED_TOKENS, group=None,
-                 device: torch.device | None = None, timeout_s: float = 2.0):
+                 device: torch.device | None = None, timeout_s: float = 2.0,
+                 one_shot: bool | None = None):
         import torch.distributed._symmetric_memory as symm_mem
 
         group = group if group is not None else dist.group.WORLD
@@ -47,18 +61,38 @@ class OProjAllReduce:
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         name = group.group_name
         E = max_tokens * hidden
-        # [fp32 partials E][bf16 result E (E/2 fp32 slots)][2 * world epoch slots]
-        sig_words = (2 * self.world + 3) // 4 * 4
-        self._part_off, self._out_off, self._sig_off = 0, 4 * E, 6 * E
-        self.buf = symm_mem.empty(E + E // 2 + sig_words, dtype=torch.float32, device=self.device)
+        W = self.world
+        sig_words = (2 * W + 3) // 4 * 4
+        want_one_shot = W <= 2 if one_shot is None else bool(one_shot)
+        # one-shot needs W * E words of receive slots, two-shot E words
+        # (partials + result); unless two-shot was asked for, room for
+        # one-shot (the fallback without multicast); epoch slots after them
+        data_words = W * E if one_shot is not False else E
+        self.buf = symm_mem.empty(data_words + sig_words, dtype=torch.float32, device=self.device)
         self.buf.zero_()
         self.handle = symm_mem.rendezvous(self.buf, name)
-        mc = int(self.handle.multicast_ptr)
-        if mc == 0:
-            raise RuntimeError("OProjAllReduce: no NVLink multicast (NVLS) on this process group")
         offset = self.buf.data_ptr() - int(self.handle.buffer_ptrs[self.rank])
-        self.mc_base = mc + offset
+        mc = int(self.handle.multicast_ptr)
+        if not want_one_shot and mc == 0:
+            if one_shot is False:
+                raise RuntimeError("OProjAllReduce: no NVLink multicast (NVLS) on this process group")
+            want_one_shot = True
+        self.one_shot = want_one_shot
+        self._sig_off = 4 * data_words
+        if self.one_shot:
+            peers = [int(self.handle.buffer_ptrs[q]) + offset for q in range(W)]
+            self.slot_stride = E
+            self.recv_ptrs = torch.tensor(peers, dtype=torch.int64, device=self.device)
+            self.sig_ptrs = torch.tensor([b + self._sig_off for b in peers], dtype=torch.int64,
+                                         device=self.device)
+        else:
+            self.mc_base = mc + offset
+            self._part_off, self._out_off = 0, 2 * E
         self.flags = torch.zeros(5, dtype=torch.int32, device=self.device)  # ctr/go x2, epoch
+        # split-K partial tiles: up to 4 K ranges x max_tokens (rounded up to
+        # 128-row tiles) x hidden fp32, L2-resident at decode sizes
+        self.workspace = torch.empty(4 * ((max_tokens + 127) // 128 * 128) * hidden,
+                                     dtype=torch.float32, device=self.device)
         self.timeout_ns = int(timeout_s * 1e9)
         torch.cuda.synchronize(self.device)
         dist.barrier(group)
@@ -72,13 +106,23 @@ class OProjAllReduce:
         if out is None:
             out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
         assert out.stride(-1) == 1
-        base, mc = self.buf.data_ptr(), self.mc_base
+        base = self.buf.data_ptr()
         lib = _lib.load()
+        if self.one_shot:
+            _lib.check("nkv_oproj_allreduce_p2p", lib.nkv_oproj_allreduce_p2p(
+                x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), T, K, N,
+                self.recv_ptrs.data_ptr(), self.slot_stride, self.sig_ptrs.data_ptr(),
+                base + self._sig_off, self.flags.data_ptr(), self.rank, self.world,
+                self.timeout_ns, self.workspace.data_ptr(), self.workspace.numel() * 4,
+                out.data_ptr(), out.stride(0), ops._stream(x.device)))
+            return out
+        mc = self.mc_base
         _lib.check("nkv_oproj_allreduce", lib.nkv_oproj_allreduce(
             x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), T, K, N,
             mc + self._part_off, base + self._part_off, mc + self._out_off, base + self._out_off,
             mc + self._sig_off, base + self._sig_off, self.flags.data_ptr(), self.rank,
-            self.world, self.timeout_ns, out.data_ptr(), out.stride(0), ops._stream(x.device)))
+            self.world, self.timeout_ns, self.workspace.data_ptr(), self.workspace.numel() * 4,
+            out.data_ptr(), out.stride(0), ops._stream(x.device)))
         return out
 
 
@@ -86,10 +130,7 @@ class RowParallelOProj:
     """Drop-in forward of the attention block's o_proj (RowParallelLinear
     without bias, nanokvllm/layers/linear.py:133-155): with fused=True the
     fused kernel for decode-sized steps, otherwise (and for larger steps) the
-    reference's F.linear + dist.all_reduce. The fused kernel is opt-in: at
-    config 2's decode shape on 2 GPUs it measures 0.5x the speed of cuBLAS +
-    NCCL (its GEMM re-reads x per output tile, and its two rank barriers
-    wait on system-scope fences)."""
+    reference's F.linear + dist.all_reduce. The fused kernel is opt-in."""
 
     def __init__(self, weight: torch.Tensor, group=None, max_tokens: int = MAX_FUSED_TOKENS,
                  fused: bool = False):
