@@ -230,11 +230,13 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
 /* .acc::f32) and broadcasts the bf16 result into every rank's copy of a    */
 /* symmetric bf16 [tokens, n] buffer (out_mc / out_local); after a second    */
 /* barrier it copies the result to y. sig_mc / sig_local: a symmetric       */
-/* uint32[2 * world] of epoch slots; flags: this rank's uint32[5] (arrival  */
-/* counters, release flags, the epoch); slots and flags zeroed once. The    */
-/* epoch is read and advanced on the device, so every rank must make the    */
-/* same sequence of calls and a CUDA graph may replay them. Waits are       */
-/* bounded by timeout_ns (then NKV_DEVERR_WAIT_TIMEOUT). Needs k % 64 == 0,  */
+/* uint32[2] of arrival counters (every CTA of every rank adds one per       */
+/* barrier); flags: this rank's uint32[5] (the two barriers' counter         */
+/* targets, two unused words, the call's epoch); counters and flags zeroed  */
+/* once. Targets and epoch are read and advanced on the device, so every    */
+/* rank must make the same sequence of calls and a CUDA graph may replay     */
+/* them. Waits are bounded by timeout_ns (then NKV_DEVERR_WAIT_TIMEOUT).     */
+/* Needs k % 64 == 0,                                                       */
 /* n % 32 == 0, 16-byte aligned x, w, y and buffers, row strides multiples  */
 /* of 8. Cooperative launch of (n / TN) * S CTAs, TN in {32, 64, 128}        */
 /* output columns per tile and S in {1, 2, 4} CTAs per tile (a cluster,      */
@@ -259,8 +261,8 @@ int nkv_oproj_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw, 
 /* [2 parities][world][slot_stride] bf16 (slot_stride >= tokens * n, a       */
 /* multiple of 8); the parity alternates per call, so a rank's next call     */
 /* never overwrites a slot a peer is still summing. sig_peers: device array  */
-/* of world pointers to each rank's uint32[2 * world] epoch slots (sig_local */
-/* = this rank's). flags, epoch, waits, limits, workspace and the           */
+/* of world pointers to each rank's uint32[2] arrival counters (sig_local =  */
+/* this rank's). flags, epoch, waits, limits, workspace and the             */
 /* cooperative cluster launch as nkv_oproj_allreduce. Egress per rank:       */
 /* (world - 1) x the partial, so it suits small TP groups.                  */
 int nkv_oproj_allreduce_p2p(const void* x, int64_t ldx, const void* w, int64_t ldw,

@@ -8,33 +8,39 @@
 //     [j*K/S, (j+1)*K/S) -- so each CTA streams only 1/S of x and of its W
 //     slice (TMA, 128-byte swizzle, no multicast, a ring of up to 6
 //     stages; one thread issues UMMA 128 x TN x 16);
-//   * epilogue: each CTA stores its fp32 partial tile to an L2-resident
-//     workspace, the cluster synchronises, and CTA j sums rows
-//     [j*Tp/S, (j+1)*Tp/S) over the S K ranges, rounds them to bf16 (the
-//     reference's F.linear output type) and emits them; with S = 1 the
-//     tile goes from TMEM to bf16 directly. Emitting means: to this rank's
-//     copy of a symmetric bf16 [T, N] partial buffer (two-shot mode), or
-//     into this rank's slot of every rank's receive buffer (one-shot mode,
-//     below);
-//   * barrier 1 (all ranks' partials written), then each rank reduces its
-//     1/world slice of the T x N elements with
-//     multimem.ld_reduce.add.acc::f32 (NVLink SHARP: the NVSwitch reads
-//     every rank's bf16 partial, sums in fp32 and returns bf16) and
-//     broadcasts it into every rank's copy of a symmetric bf16 [T, N]
-//     result buffer with multimem.st -- each element crosses NVLink once
-//     per direction; every thread keeps four 16-byte reductions in flight;
-//   * barrier 2 (all slices broadcast), then the tile's CTAs copy their
-//     share of the gathered result to y.
-// A barrier: after fence.acq_rel.sys and a device-scope arrival counter, the
-// last CTA of the rank stores the call's epoch into every rank's slot with
-// multimem.st.release and waits for all ranks' epochs (bounded by
-// %globaltimer; on timeout it flags NKV_DEVERR_WAIT_TIMEOUT and goes on),
-// then releases the rank's other CTAs. Two barriers per call also order the
-// buffers' reuse: no rank writes call n+1's partials or broadcasts before
-// every rank has finished call n. The epoch counter lives in device memory,
-// so a CUDA graph can replay the launch.
-// The launch is cooperative (all CTAs resident: non-last CTAs wait on the
-// last one); every wait is bounded.
+//   * epilogue: S > 1: each CTA stores its fp32 partial tile to an
+//     L2-resident workspace, the cluster synchronises, and CTA j sums rows
+//     [j*Tp/S, (j+1)*Tp/S) over the S K ranges (in K order); the sum -- or,
+//     with S = 1, the accumulator -- is rounded to bf16 (the reference's
+//     F.linear output type) into a block in shared memory (the drained
+//     ring), which one thread sends with a bulk copy (cp.async.bulk, the
+//     TMA engine, no multicast) -- large transfers, so NVLink carries them
+//     at full width. The bf16 [T, N] buffers below are tile-major,
+//     [N / TN][T][TN], so a CTA's block is contiguous there:
+//       two-shot mode: to this rank's copy of a symmetric bf16 [T, N]
+//         partial buffer; barrier 1; each rank reduces its 1/world slice
+//         with multimem.ld_reduce.add.acc::f32 (NVLink SHARP: the NVSwitch
+//         reads every rank's bf16 partial, sums in fp32, returns bf16) and
+//         broadcasts it into every rank's copy of a symmetric bf16 [T, N]
+//         result buffer with multimem.st (four 16-byte reductions in flight
+//         per thread); barrier 2; the tile's CTAs copy their share to y.
+//         NVLink traffic per rank does not grow with the group.
+//       one-shot mode: into this rank's slot of EVERY rank's receive buffer
+//         (a bulk copy per rank, over NVLink for the others, issued while
+//         other tiles still run their GEMM); one barrier; every rank sums
+//         the world slots of its tile in rank order (fp32, so every rank
+//         holds the same bf16 result) into y. Receive buffers alternate
+//         between two parities per call, so no second barrier guards their
+//         reuse: a rank can only be one call ahead of the slowest.
+// A barrier: every CTA fences its stores (fence.acq_rel.sys) and adds one
+// to every rank's arrival counter (one multimem.red through the switch, or
+// a red per rank), then waits until its own rank's counter reaches this
+// call's target (ld.acquire.sys, bounded by %globaltimer; on timeout it
+// flags NKV_DEVERR_WAIT_TIMEOUT and goes on). Counters only grow; the
+// targets and the call's epoch (its parity) live in device memory and are
+// advanced by CTA 0 once every CTA has read them, so a CUDA graph can replay
+// the launch. The launch is cooperative (all CTAs resident: each waits on
+// all the others).
 #pragma once
 #include "nkv_common.cuh"
 #include "tcgen05.cuh"
@@ -42,29 +48,31 @@
 namespace nkv {
 
 constexpr int kOpK = 64;            // K elements per stage (one 128-byte row)
-constexpr int kOpMaxStages = 6;    // ring depth (fewer when the M tiles are many)
+constexpr int kOpMaxStages = 6;     // ring depth (fewer when the M tiles are many)
 constexpr int kOpThreads = 192;     // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
 constexpr int kOpMaxMTiles = 4;     // T <= 512
 constexpr int kOpATile = 128 * 128;  // one 128-row x 64-K bf16 tile, bytes
 constexpr int kOpMaxSplits = 4;     // cluster size along K
-constexpr int kOpReduceUnroll = 4;  // switch reductions in flight per thread
-constexpr int kOpSumBatch = 4;      // one-shot: result groups per thread in flight
-
+constexpr int kOpReduceUnroll = 4;  // two-shot: switch reductions in flight per thread
+constexpr int kOpSumBatch = 8;      // one-shot: result groups per thread in flight
+constexpr int kOpSplitBatch = 3;    // split-K sum: 8-column groups per thread in flight
+constexpr int kOpSendRows = 32;     // rows per bulk send (the next chunk is summed meanwhile)
 
 struct OprojParams {
   // two-shot (NVLS) mode
-  __nv_bfloat16* part_mc;  // multicast address of the bf16 [T, N] partial buffer
+  // (the bf16 [T, N] buffers are tile-major: [N / TN][T][TN])
+  __nv_bfloat16* part_mc;          // multicast address of the bf16 [T, N] partial buffer
   __nv_bfloat16* part_local;       // this rank's copy of it
-  __nv_bfloat16* out_mc;  // multicast address of the bf16 [T, N] gathered result
+  __nv_bfloat16* out_mc;           // multicast address of the bf16 [T, N] gathered result
   const __nv_bfloat16* out_local;  // this rank's copy of it
-  uint32_t* sig_mc;       // multicast address of the [2][world] epoch slots
+  uint32_t* sig_mc;                // multicast address of the [2] arrival counters
   // one-shot (peer-store) mode, device arrays indexed by rank
   __nv_bfloat16* const* recv_peers;  // each rank's [2 parities][world][slot_stride] bf16
-  uint32_t* const* sig_peers;        // each rank's [2][world] epoch slots
+  uint32_t* const* sig_peers;        // each rank's [2] arrival counters
   int64_t slot_stride;               // elements per (parity, source rank) slot, >= T * N
-  uint32_t* sig_local;    // this rank's copy of the slots
+  uint32_t* sig_local;    // this rank's [2] arrival counters
   float* splitk_ws;       // S > 1: fp32 partial tiles, [S][N / TN][TN / 4][mtiles * 128][4]
-  unsigned int* flags;    // this rank's [ctr 1, go 1, ctr 2, go 2, epoch]
+  unsigned int* flags;    // this rank's [target 1, target 2, -, -, epoch]
   __nv_bfloat16* y;
   int64_t ldy;
   int T, K, N;
@@ -116,84 +124,76 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
+__device__ __forceinline__ uint2 pack4_bf16(float a, float b, float c, float d) {
+  return make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+}
+
 __device__ __forceinline__ uint4 pack8_bf16(const float (&a)[8]) {
   return make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
                     pack_bf16x2(a[6], a[7]));
 }
 
-// Cross-rank barrier `which` (0 or 1) of the call with `epoch`: every CTA
-// arrives once; the rank's last CTA signals all ranks (one multicast store,
-// or a release store into each rank's slot) and waits for theirs, then
-// releases the rank's CTAs; at the call's last barrier it also stores the
-// epoch as the next call's base. Bounded by p.timeout_ns.
-__device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, uint32_t epoch,
-                                             bool last) {
+// Cross-rank barrier `which` (0 or 1) with this call's counter target:
+// every CTA arrives at every rank's counter after fencing its own stores (a
+// release pattern at system scope), then waits for its rank's counter to
+// reach the target (an acquire). Bounded by p.timeout_ns.
+__device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, uint32_t target) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    unsigned int* ctr = p.flags + 2 * which;
-    unsigned int* go = p.flags + 2 * which + 1;
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-    const unsigned int old = atomic_add_acq_rel_gpu(ctr, 1u);
-    if (old == gridDim.x - 1) {
-      // every CTA's writes precede its arrival (its system fence, then the
-      // counter, which this CTA acquired); one system fence here, then
-      // relaxed signal stores, forms the release the other ranks acquire
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      if (p.one_shot) {
-        for (int r = 0; r < p.world; ++r)
-          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(
-                           p.sig_peers[r] + which * p.world + p.rank),
-                       "r"(epoch)
-                       : "memory");
-      } else {
-        asm volatile("multimem.st.relaxed.sys.global.b32 [%0], %1;" ::"l"(
-                         p.sig_mc + which * p.world + p.rank),
-                     "r"(epoch)
+    if (p.one_shot) {
+      for (int r = 0; r < p.world; ++r)
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(p.sig_peers[r] + which)
                      : "memory");
-      }
-      const uint64_t t0 = global_ns();
-      for (int r = 0; r < p.world; ++r) {
-        while (static_cast<int32_t>(ld_acquire_sys(p.sig_local + which * p.world + r) - epoch) < 0) {
-          if (global_ns() - t0 > p.timeout_ns) {
-            raise_error(NKV_DEVERR_WAIT_TIMEOUT);
-            break;
-          }
-          __nanosleep(32);
-        }
-      }
-      *ctr = 0u;
-      if (last) p.flags[4] = epoch;  // the next call's base (all CTAs have read it)
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(go), "r"(epoch) : "memory");
     } else {
-      const uint64_t t0 = global_ns();
-      while (static_cast<int32_t>(ld_acquire_gpu(go) - epoch) < 0) {
-        if (global_ns() - t0 > p.timeout_ns) {
-          raise_error(NKV_DEVERR_WAIT_TIMEOUT);
-          break;
-        }
-        __nanosleep(32);
+      asm volatile("multimem.red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(p.sig_mc + which)
+                   : "memory");
+    }
+    const uint64_t t0 = global_ns();
+    while (static_cast<int32_t>(ld_acquire_sys(p.sig_local + which) - target) < 0) {
+      if (global_ns() - t0 > p.timeout_ns) {
+        raise_error(NKV_DEVERR_WAIT_TIMEOUT);
+        break;
       }
+      __nanosleep(32);
     }
   }
   __syncthreads();
 }
 
-// One 8-column bf16 group of this rank's partial: to the NVLS partial
-// buffer, or (one-shot) into this rank's slot of every rank's receive buffer
-// of the call's parity -- a local store for this rank, NVLink stores for the
-// others, issued while other tiles are still in their GEMM.
-__device__ __forceinline__ void emit_partial(const OprojParams& p, int r, int col, uint4 v,
-                                             uint32_t parity) {
-  const int64_t off = static_cast<int64_t>(r) * p.N + col;
+// Sends rows [row, row + nrows) of this CTA's bf16 block -- rows
+// [r0, r0 + ...) of tile `tile`, row-major in shared memory at `block` -- to
+// the NVLS partial buffer, or (one-shot) into this rank's slot of every
+// rank's receive buffer of the call's parity (peers first). One thread,
+// after the writing threads' proxy fences and a CTA barrier; asynchronous:
+// send_wait() completes every send of the thread.
+__device__ __forceinline__ void send_rows(const OprojParams& p, uint32_t block, int tile, int r0,
+                                          int row, int nrows, uint32_t parity) {
+  const int64_t off = (static_cast<int64_t>(tile) * p.T + r0 + row) * p.tn;
+  const uint32_t src = block + static_cast<uint32_t>(row * p.tn * 2);
+  const uint32_t bytes = static_cast<uint32_t>(nrows * p.tn * 2);
   if (!p.one_shot) {
-    *reinterpret_cast<uint4*>(p.part_local + off) = v;
-    return;
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                     p.part_local + off),
+                 "r"(src), "r"(bytes)
+                 : "memory");
+  } else {
+    const int64_t slot = (static_cast<int64_t>(parity) * p.world + p.rank) * p.slot_stride + off;
+    for (int i = 0; i < p.world; ++i) {
+      const int q = (p.rank + 1 + i) % p.world;
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                       p.recv_peers[q] + slot),
+                   "r"(src), "r"(bytes)
+                   : "memory");
+    }
   }
-  const int64_t slot = (static_cast<int64_t>(parity) * p.world + p.rank) * p.slot_stride + off;
-  for (int i = 0; i < p.world; ++i) {
-    const int q = (p.rank + 1 + i) % p.world;  // peers first, this rank last
-    *reinterpret_cast<uint4*>(p.recv_peers[q] + slot) = v;
-  }
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// The thread's bulk sends have completed; ordered before its later accesses.
+__device__ __forceinline__ void send_wait() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  asm volatile("fence.proxy.async;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(kOpThreads, 1)
@@ -215,14 +215,18 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   const int lane = threadIdx.x & 31;
   const int S = p.splits;
   const int split = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-  const int n0 = (blockIdx.x / S) * p.tn;
+  const int tile = blockIdx.x / S;
+  const int n0 = tile * p.tn;
   const int kper = p.K / S;
   const int k0 = split * kper;
-  // The call's epoch lives on the device (so the launch can be replayed from
-  // a CUDA graph): every CTA reads it here, before it arrives at the
-  // counter that lets the last CTA advance it.
+  // The call's epoch and counter targets live on the device (so the launch
+  // can be replayed from a CUDA graph): every CTA reads them here, before
+  // its first arrival; CTA 0 advances them after the call's last barrier.
   const uint32_t epoch = ld_acquire_gpu(p.flags + 4) + 1u;
   const uint32_t parity = epoch & 1u;
+  const uint32_t arrivals = gridDim.x * static_cast<uint32_t>(p.world);
+  const uint32_t target0 = ld_acquire_gpu(p.flags + 0) + arrivals;
+  const uint32_t target1 = ld_acquire_gpu(p.flags + 1) + arrivals;
   const int ksteps = kper / kOpK;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(p.mtiles * p.tn)) cols <<= 1;
@@ -299,22 +303,25 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     if (lane == 0) umma_commit(smem_u32(acc_full));
     __syncwarp();
   } else {
+    // acc_full: every MMA has completed, so every TMA load has landed and
+    // the ring is free for staging
     acc_ok = mbar_wait_bounded(smem_u32(acc_full), 0);
   }
 
   // ---------------------------------------------------------------- epilogue
-  // warps 2-5, thread = one accumulator row. S = 1: bf16 groups straight to
-  // their destinations. S > 1: the fp32 row to this K range's block of the
-  // workspace, laid out [column / 4][row][4] so that a warp's 16-byte stores
-  // (32 consecutive rows) cover 512 contiguous bytes; rows
-  // [j*Tp/S, (j+1)*Tp/S) are then summed by cluster CTA j
+  // warps 2-5, thread = one accumulator row. S > 1: the fp32 row to this K
+  // range's workspace tile, laid out [column / 4][row][4] so that a warp's
+  // 16-byte stores (32 consecutive rows) cover 512 contiguous bytes. S = 1:
+  // the bf16 row into the shared-memory block [T][TN].
   const int tp = p.mtiles * 128;
-  const int rows = tp / S;
-  float* ws_tile = p.splitk_ws + (static_cast<int64_t>(split) * (p.N / p.tn) + blockIdx.x / S) *
-                                     p.tn * tp;
+  const int rows = tp / S;  // rows summed per cluster CTA, a multiple of 32
+  const int64_t ws_tiles = static_cast<int64_t>(p.N / p.tn) * tp * p.tn;  // one K range
+  __nv_bfloat16* block = reinterpret_cast<__nv_bfloat16*>(smem);
   if (warp >= 2 && acc_ok) {
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, +32)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    float4* ws4 = reinterpret_cast<float4*>(p.splitk_ws + split * ws_tiles +
+                                            static_cast<int64_t>(tile) * tp * p.tn);
     tc_fence_after();
     for (int mt = 0; mt < p.mtiles; ++mt) {
       const int r = mt * 128 + quarter * 32 + lane;
@@ -324,23 +331,24 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
         tmem_ld_wait(v);
         if (r >= p.T) {
         } else if (S > 1) {
-          float4* dst = reinterpret_cast<float4*>(ws_tile) + static_cast<int64_t>(c / 4) * tp + r;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            __stcg(dst + static_cast<int64_t>(i) * tp,
+            __stcg(ws4 + static_cast<int64_t>(c / 4 + i) * tp + r,
                    make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
         } else {
+          uint4* dst = reinterpret_cast<uint4*>(block + r * p.tn + c);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             float a[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) a[e] = __uint_as_float(v[8 * i + e]);
-            emit_partial(p, r, n0 + c + 8 * i, pack8_bf16(a), parity);
+            dst[i] = pack8_bf16(a);
           }
         }
       }
     }
+    fence_proxy_async_shared();  // block rows written for the bulk send (S = 1)
   }
   tc_fence_before();
   __syncthreads();
@@ -349,59 +357,88 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     tmem_dealloc(tmem, cols);
   }
 
+  int r0 = 0, nrows = p.T;
   if (S > 1) {
     // ------------------------------------ split-K sum of this CTA's rows
     // the cluster barrier (release / acquire at cluster scope) makes every
-    // CTA's workspace block visible. A warp takes 8 rows x 4 eight-column
-    // groups (its workspace reads: 128 contiguous bytes per group; its
-    // emitted stores: 64 contiguous bytes per row), all S blocks' loads
-    // issued before the sums, which run in block (= K range) order; the
-    // result is rounded to bf16 and emitted
+    // CTA's workspace tile visible. Rows go in chunks of kOpSendRows, each
+    // sent as soon as it is summed, so NVLink carries one chunk while the
+    // next is summed. Within a chunk a warp takes 8 rows x 4 eight-column
+    // groups (its reads: 128 contiguous bytes per group and K range),
+    // kOpSplitBatch such items per thread with all their loads issued
+    // before the sums, which run in K-range order; bf16 into the block
     cluster_sync_all();
-    const int groups = p.tn / 8;          // 8-column groups per row: 4, 8 or 16
-    const int r0 = split * rows;          // rows is a multiple of 32
-    const int tiles = (rows / 8) * (groups / 4);
-    const int rsub = lane & 7, gsub = lane >> 3;
-    for (int t = warp; t < tiles; t += kOpThreads / 32) {
-      const int lr = (t % (rows / 8)) * 8 + rsub;
-      const int g = (t / (rows / 8)) * 4 + gsub;
-      const int r = r0 + lr;
-      if (r >= p.T) continue;
-      float4 u[kOpMaxSplits][2];
+    r0 = split * rows;
+    nrows = max(0, min(rows, p.T - r0));
+    const int gblocks = p.tn / 32;  // 4-group column blocks: 1, 2 or 4
+    const float4* ws4 = reinterpret_cast<const float4*>(p.splitk_ws +
+                                                        static_cast<int64_t>(tile) * tp * p.tn);
+    for (int row0 = 0; row0 < nrows; row0 += kOpSendRows) {
+      const int crows = min(kOpSendRows, nrows - row0);
+      const int rtiles = (crows + 7) / 8;
+      const int items = rtiles * gblocks * 32;
+      for (int i0 = threadIdx.x; i0 < items; i0 += kOpSplitBatch * kOpThreads) {
+        float4 u[kOpSplitBatch][kOpMaxSplits][2];
+        int lr[kOpSplitBatch], g[kOpSplitBatch];
 #pragma unroll
-      for (int q = 0; q < kOpMaxSplits; ++q) {
-        if (q < S) {
-          const float4* src = reinterpret_cast<const float4*>(
-                                  p.splitk_ws + (static_cast<int64_t>(q) * (p.N / p.tn) +
-                                                 blockIdx.x / S) * p.tn * tp) +
-                              static_cast<int64_t>(2 * g) * tp + r;
-          u[q][0] = __ldcg(src);
-          u[q][1] = __ldcg(src + tp);
+        for (int b = 0; b < kOpSplitBatch; ++b) {
+          const int i = i0 + b * kOpThreads;
+          const int t = i >> 5, l = i & 31;
+          lr[b] = row0 + (t % rtiles) * 8 + (l & 7);
+          g[b] = (t / rtiles) * 4 + (l >> 3);
+          if (i < items && lr[b] < row0 + crows) {
+#pragma unroll
+            for (int q = 0; q < kOpMaxSplits; ++q) {
+              if (q < S) {
+                const float4* src = ws4 + q * (ws_tiles / 4) +
+                                    static_cast<int64_t>(2 * g[b]) * tp + r0 + lr[b];
+                u[b][q][0] = __ldcg(src);
+                u[b][q][1] = __ldcg(src + tp);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kOpSplitBatch; ++b) {
+          const int i = i0 + b * kOpThreads;
+          if (i >= items || lr[b] >= row0 + crows) continue;
+          float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int q = 0; q < kOpMaxSplits; ++q) {
+            if (q < S) {
+              a[0] += u[b][q][0].x; a[1] += u[b][q][0].y; a[2] += u[b][q][0].z;
+              a[3] += u[b][q][0].w; a[4] += u[b][q][1].x; a[5] += u[b][q][1].y;
+              a[6] += u[b][q][1].z; a[7] += u[b][q][1].w;
+            }
+          }
+          *reinterpret_cast<uint4*>(block + lr[b] * p.tn + 8 * g[b]) = pack8_bf16(a);
         }
       }
-      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q = 0; q < kOpMaxSplits; ++q) {
-        if (q < S) {
-          a[0] += u[q][0].x; a[1] += u[q][0].y; a[2] += u[q][0].z; a[3] += u[q][0].w;
-          a[4] += u[q][1].x; a[5] += u[q][1].y; a[6] += u[q][1].z; a[7] += u[q][1].w;
-        }
-      }
-      emit_partial(p, r, n0 + 8 * g, pack8_bf16(a), parity);
+      fence_proxy_async_shared();  // this chunk's rows, for the bulk send
+      __syncthreads();
+      if (threadIdx.x == 0) send_rows(p, smem_u32(block), tile, r0, row0, crows, parity);
     }
+  } else if (threadIdx.x == 0 && nrows > 0) {
+    send_rows(p, smem_u32(block), tile, 0, 0, nrows, parity);
   }
+  if (threadIdx.x == 0) send_wait();
 
   const int per_row = p.tn / 8;
   if (p.one_shot) {
     // ------------------------------------------------------------ barrier
-    rank_barrier(p, 0, epoch, true);
+    rank_barrier(p, 0, target0);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {  // every CTA read them before arriving
+      p.flags[0] = target0;
+      p.flags[4] = epoch;
+    }
     // every rank's partial of this tile is in this rank's receive buffer:
     // sum them in rank order (the same order on every rank, so every rank
     // holds the same result) and write y; the tile's S CTAs share the rows
-    // (kOpSumBatch groups per thread at a time, each slot's loads issued
+    // (kOpSumBatch groups per thread at a time, two slots' loads issued
     // together)
     const __nv_bfloat16* recv = p.recv_peers[p.rank] +
-                                static_cast<int64_t>(parity) * p.world * p.slot_stride;
+                                static_cast<int64_t>(parity) * p.world * p.slot_stride +
+                                static_cast<int64_t>(tile) * p.T * p.tn;
     const int items = p.T * per_row;
     const int step = S * kOpThreads;
     for (int i0 = split * kOpThreads + threadIdx.x; i0 < items; i0 += kOpSumBatch * step) {
@@ -409,24 +446,30 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
 #pragma unroll
       for (int b = 0; b < kOpSumBatch; ++b) {
         const int i = i0 + b * step;
-        const int r = i / per_row;
-        off[b] = i < items ? static_cast<int64_t>(r) * p.N + n0 + (i - r * per_row) * 8 : -1;
+        off[b] = i < items ? static_cast<int64_t>(i) * 8 : -1;  // tile block, row-major
       }
       float a[kOpSumBatch][8] = {};
-      for (int q = 0; q < p.world; ++q) {
-        uint4 u[kOpSumBatch];
+      for (int q0 = 0; q0 < p.world; q0 += 2) {
+        uint4 u[2][kOpSumBatch];
 #pragma unroll
-        for (int b = 0; b < kOpSumBatch; ++b)
-          if (off[b] >= 0)
-            u[b] = __ldcg(reinterpret_cast<const uint4*>(recv + q * p.slot_stride + off[b]));
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int b = 0; b < kOpSumBatch; ++b) {
-          if (off[b] < 0) continue;
-          const uint32_t w4[4] = {u[b].x, u[b].y, u[b].z, u[b].w};
+          for (int b = 0; b < kOpSumBatch; ++b)
+            if (off[b] >= 0 && q0 + h < p.world)
+              u[h][b] = __ldcg(reinterpret_cast<const uint4*>(recv + (q0 + h) * p.slot_stride +
+                                                              off[b]));
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            a[b][2 * e] += __uint_as_float(w4[e] << 16);
-            a[b][2 * e + 1] += __uint_as_float(w4[e] & 0xffff0000u);
+        for (int h = 0; h < 2; ++h) {  // rank order
+          if (q0 + h >= p.world) break;
+#pragma unroll
+          for (int b = 0; b < kOpSumBatch; ++b) {
+            if (off[b] < 0) continue;
+            const uint32_t w4[4] = {u[h][b].x, u[h][b].y, u[h][b].z, u[h][b].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              a[b][2 * e] += __uint_as_float(w4[e] << 16);
+              a[b][2 * e + 1] += __uint_as_float(w4[e] & 0xffff0000u);
+            }
           }
         }
       }
@@ -443,7 +486,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 
   // ---------------------------------------------------------------- barrier 1
-  rank_barrier(p, 0, epoch, false);
+  rank_barrier(p, 0, target0);
 
   // ------------------------------------------------- reduce this rank's slice
   // 16-byte groups [lo, hi) of the T x N result: fp32 sum of every rank's
@@ -480,14 +523,20 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 
   // ---------------------------------------------------------------- barrier 2
-  rank_barrier(p, 1, epoch, true);
+  rank_barrier(p, 1, target1);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {  // every CTA read them before arriving
+    p.flags[0] = target0;
+    p.flags[1] = target1;
+    p.flags[4] = epoch;
+  }
 
   // ---------------------------------------------------------------- copy out
   // the tile's columns of the gathered bf16 result -> y, shared by its S CTAs
   for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
     const int r = i / per_row;
     const int c = n0 + (i - r * per_row) * 8;
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.out_local + static_cast<int64_t>(r) * p.N + c));
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(
+        p.out_local + static_cast<int64_t>(tile) * p.T * p.tn + static_cast<int64_t>(i) * 8));
     *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(r) * p.ldy + c) = v;
   }
 }
