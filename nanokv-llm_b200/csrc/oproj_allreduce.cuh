@@ -124,10 +124,6 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
-__device__ __forceinline__ uint2 pack4_bf16(float a, float b, float c, float d) {
-  return make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
-}
-
 __device__ __forceinline__ uint4 pack8_bf16(const float (&a)[8]) {
   return make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
                     pack_bf16x2(a[6], a[7]));
