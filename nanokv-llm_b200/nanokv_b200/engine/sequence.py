@@ -37,6 +37,9 @@ class Sequence:
     def __len__(self) -> int:
         return self.num_tokens
 
+    def __getitem__(self, key):
+        return self.token_ids[key]
+
     @property
     def is_prefill_done(self) -> bool:
         return self.num_computed_tokens >= self.num_prompt_tokens

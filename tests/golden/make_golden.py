@@ -21,6 +21,9 @@ only their sha256 digests are stored):
   host_metadata.json  reference BlockManager / Scheduler.postprocess traces,
                       ModelRunner.prepare_decode periodic selection, and KvChat
                       prepare_compression_context decisions.
+  step_metadata.json  reference ModelRunner.prepare_step (the unified
+                      scheduler's per-step metadata) on mixed prefill-chunk +
+                      decode batches, an all-decode batch and a single prefill.
 
 The store that precedes compression is the reference's Triton kernel (CUDA
 only); the script applies it with oracle.attention.store_kvcache_ref, which
@@ -335,6 +338,71 @@ def gen_host(ref):
     print("host_metadata.json written")
 
 
+def gen_step(ref):
+    """The unified scheduler's per-step metadata: ModelRunner.prepare_step
+    (nanokvllm/engine/model_runner.py:160-219) on mixed prefill-chunk +
+    decode batches, an all-decode batch and a single prefill, run on the CPU
+    (tensor uploads stubbed out as in gen_host)."""
+    from nanokvllm.engine.model_runner import ModelRunner
+    import nanokvllm.engine.model_runner as mr
+    from nanokvllm.engine.sequence import ScheduledSeq, Sequence
+    from nanokvllm.sampling_params import SamplingParams
+    from nanokvllm.utils.context import get_context, reset_context
+    rng = np.random.default_rng(17)
+    sp = SamplingParams(max_tokens=10**6, ignore_eos=True)
+    Sequence.counter = iter(range(10**6))
+    stub = types.SimpleNamespace(block_size=256)
+    stub.prepare_block_tables = lambda seqs: ModelRunner.prepare_block_tables(stub, seqs)
+    pool = rng.permutation(4096).tolist()
+
+    def make(prompt_len, computed, generated=0):
+        s = Sequence(rng.integers(0, 100, prompt_len).tolist(), sp)  # small ids: small file
+        for t in rng.integers(0, 100, generated).tolist():
+            s.append_token(int(t))
+        s.num_computed_tokens = computed
+        nb = (len(s) + 255) // 256
+        s.block_table = [pool.pop() for _ in range(nb)]
+        return s
+
+    batches = []
+    # mixed: decode rows, a first chunk, a middle chunk, a one-token last chunk
+    d0, d1 = make(300, 304, 5), make(1800, 1800 + 40, 41)
+    c0, c1, c2 = make(5000, 0), make(5000, 2048), make(2049, 2048)
+    batches.append(("mixed", [ScheduledSeq(d0, 1), ScheduledSeq(c0, 2048), ScheduledSeq(d1, 1),
+                              ScheduledSeq(c1, 1000), ScheduledSeq(c2, 1)], False))
+    dec = [make(int(n), int(n) + 7, 8) for n in rng.integers(200, 3000, 6)]
+    batches.append(("all_decode", [ScheduledSeq(s, 1) for s in dec], True))
+    batches.append(("single_prefill", [ScheduledSeq(make(300, 0), 300)], False))
+    real_cuda = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *a, **k: self
+    mr_torch = mr.torch
+    mr.torch = _TorchNoPin()
+    out = []
+    try:
+        for name, sched, all_decode in batches:
+            ids, pos, logits_idx = ModelRunner.prepare_step(stub, sched, all_decode)
+            c = get_context()
+            t = lambda x: None if x is None else x.tolist()
+            out.append({"name": name, "all_decode": all_decode,
+                        "seqs": [{"token_ids": list(s.seq.token_ids),
+                                  "num_computed_tokens": s.seq.num_computed_tokens,
+                                  "block_table": list(s.seq.block_table),
+                                  "num_new_tokens": s.num_new_tokens} for s in sched],
+                        "input_ids": ids.tolist(), "positions": pos.tolist(),
+                        "logits_indices": logits_idx.tolist(),
+                        "use_decode_kernel": c.use_decode_kernel,
+                        "cu_seqlens_q": t(c.cu_seqlens_q), "cu_seqlens_k": t(c.cu_seqlens_k),
+                        "max_seqlen_q": c.max_seqlen_q, "max_seqlen_k": c.max_seqlen_k,
+                        "slot_mapping": t(c.slot_mapping), "context_lens": t(c.context_lens),
+                        "block_tables": t(c.block_tables)})
+            reset_context()
+    finally:
+        torch.Tensor.cuda = real_cuda
+        mr.torch = mr_torch
+    (OUT / "step_metadata.json").write_text(json.dumps({"block_size": 256, "batches": out}))
+    print("step_metadata.json written")
+
+
 def main():
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
     sys.path.insert(0, str(ref))
@@ -343,6 +411,7 @@ def main():
     gen_window(ref)
     gen_threshold(ref)
     gen_host(ref)
+    gen_step(ref)
 
 
 if __name__ == "__main__":

@@ -204,3 +204,54 @@ def test_device_select_host_half_matches_host_selection():
                                               keep_blocks=2, keep_extra_tokens=1, num_layers=28)
         assert events == compression_events(torch.from_numpy(meta.block_tables), sel, new_lens,
                                             256, 27)
+
+
+def test_step_metadata_matches_prepare_step(golden_dir):
+    """StepMetadata (vectorised) against the reference's own prepare_step
+    (nanokvllm/engine/model_runner.py:160-219) on mixed prefill-chunk +
+    decode, all-decode and single-prefill batches
+    (tests/golden/step_metadata.json): every array and the Context it sets."""
+    import torch
+
+    from nanokv_b200.engine.sequence import ScheduledSeq
+    from nanokv_b200.engine.step_metadata import StepMetadata
+    from nanokv_b200.utils.context import get_context, reset_context
+
+    tr = json.loads((golden_dir / "step_metadata.json").read_text())
+    bs = tr["block_size"]
+    for rec in tr["batches"]:
+        Sequence.counter = count()
+        sched = []
+        for r in rec["seqs"]:
+            s = Sequence(r["token_ids"])
+            s.num_computed_tokens = r["num_computed_tokens"]
+            s.block_table = list(r["block_table"])
+            sched.append(ScheduledSeq(s, r["num_new_tokens"]))
+        meta = StepMetadata.build(sched, bs)
+        ids, pos, logits_idx = meta.set_context(rec["all_decode"], "cpu")
+        c = get_context()
+        name = rec["name"]
+        assert ids.tolist() == rec["input_ids"], name
+        assert ids.dtype == torch.int64 and pos.dtype == torch.int64
+        assert pos.tolist() == rec["positions"], name
+        assert logits_idx.tolist() == rec["logits_indices"], name
+        assert c.use_decode_kernel == rec["use_decode_kernel"], name
+        assert c.slot_mapping.tolist() == rec["slot_mapping"] and c.slot_mapping.dtype == torch.int32
+        assert c.block_tables.tolist() == rec["block_tables"], name
+        assert (c.max_seqlen_q, c.max_seqlen_k) == (rec["max_seqlen_q"], rec["max_seqlen_k"])
+        for key in ("cu_seqlens_q", "cu_seqlens_k", "context_lens"):
+            got = getattr(c, key)
+            assert (None if got is None else got.tolist()) == rec[key], (name, key)
+            assert got is None or got.dtype == torch.int32
+        reset_context()
+
+
+def test_step_metadata_rejects_token_past_block_table():
+    from nanokv_b200.engine.sequence import ScheduledSeq
+    from nanokv_b200.engine.step_metadata import StepMetadata
+
+    Sequence.counter = count()
+    s = Sequence(list(range(300)))
+    s.block_table = [7]  # 300 tokens need two 256-token blocks
+    with pytest.raises(IndexError):
+        StepMetadata.build([ScheduledSeq(s, 300)], 256)
