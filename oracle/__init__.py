@@ -14,6 +14,7 @@ reference computes on the path that libnkv replaces:
   * KvChat threshold compression     (KvChat/layers/compress_utils.py:10-171,
                                       :218-252) and its query window
                                       (KvChat/engine/query_window_manager.py)
+  * unified-step metadata            (nanokvllm/engine/model_runner.py:154-219)
 
 It is the checker, never the product: only tests/, __graft_entry__.smoke()
 and bench.py's CPU-baseline leg import it. The product (nanokv_b200) never

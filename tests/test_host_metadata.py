@@ -255,3 +255,60 @@ def test_step_metadata_rejects_token_past_block_table():
     s.block_table = [7]  # 300 tokens need two 256-token blocks
     with pytest.raises(IndexError):
         StepMetadata.build([ScheduledSeq(s, 300)], 256)
+
+
+def test_step_metadata_oracle_pinned_and_random_batches(golden_dir):
+    """The oracle's token-by-token prepare_step restatement reproduces the
+    reference's own outputs (golden), and StepMetadata equals it on 200
+    random mixed batches (prefill chunks of 1..2,100 tokens, decode rows,
+    ragged block tables, 64- and 256-token blocks)."""
+    from nanokv_b200.engine.sequence import ScheduledSeq
+    from nanokv_b200.engine.step_metadata import StepMetadata
+    from oracle.step_metadata import prepare_step_ref
+
+    tr = json.loads((golden_dir / "step_metadata.json").read_text())
+    for rec in tr["batches"]:
+        Sequence.counter = count()
+        sched = []
+        for r in rec["seqs"]:
+            s = Sequence(r["token_ids"])
+            s.num_computed_tokens = r["num_computed_tokens"]
+            s.block_table = list(r["block_table"])
+            sched.append(ScheduledSeq(s, r["num_new_tokens"]))
+        ref = prepare_step_ref(sched, tr["block_size"])
+        for key in ("input_ids", "positions", "slot_mapping", "logits_indices", "block_tables",
+                    "max_seqlen_q", "max_seqlen_k"):
+            assert ref[key] == rec[key], (rec["name"], key)
+        if rec["all_decode"]:
+            assert ref["context_lens"] == rec["context_lens"]
+        else:
+            assert (ref["cu_seqlens_q"], ref["cu_seqlens_k"]) == (rec["cu_seqlens_q"],
+                                                                 rec["cu_seqlens_k"])
+
+    rng = np.random.default_rng(23)
+    for trial in range(200):
+        bs = int(rng.choice([64, 256]))
+        Sequence.counter = count()
+        sched, next_block = [], 0
+        for _ in range(int(rng.integers(1, 12))):
+            total = int(rng.integers(1, 6000))
+            computed = int(rng.integers(0, total))
+            new = 1 if rng.random() < 0.5 else int(rng.integers(1, min(2100, total - computed) + 1))
+            new = min(new, total - computed)
+            s = Sequence(rng.integers(0, 1000, total).tolist())
+            s.num_computed_tokens = computed
+            nb = (computed + new + bs - 1) // bs + int(rng.integers(0, 3))  # spare blocks too
+            s.block_table = (rng.permutation(nb) + next_block).tolist()
+            next_block += nb
+            sched.append(ScheduledSeq(s, new))
+        ref = prepare_step_ref(sched, bs)
+        m = StepMetadata.build(sched, bs)
+        assert m.input_ids.tolist() == ref["input_ids"], trial
+        assert m.positions.tolist() == ref["positions"], trial
+        assert m.slot_mapping.tolist() == ref["slot_mapping"], trial
+        assert m.cu_seqlens_q.tolist() == ref["cu_seqlens_q"], trial
+        assert m.cu_seqlens_k.tolist() == ref["cu_seqlens_k"], trial
+        assert m.context_lens.tolist() == ref["context_lens"], trial
+        assert m.logits_indices.tolist() == ref["logits_indices"], trial
+        assert m.block_tables.tolist() == ref["block_tables"], trial
+        assert (m.max_seqlen_q, m.max_seqlen_k) == (ref["max_seqlen_q"], ref["max_seqlen_k"])
