@@ -273,6 +273,22 @@ def gen_host(ref):
                           "seqs": [_seq_state(s) for s in seqs], "bm": _bm_state(bm)})
     trace["block_manager"] = {"prompts": prompts, "steps": steps}
 
+    # --- then release and reuse: can_append, deallocate (shared prefix
+    # blocks), can_allocate / allocate of a new prompt sharing the prefix
+    rel = [{"op": "can_append", "value": [bm.can_append(s) for s in seqs]}]
+    bm.deallocate(seqs[1])
+    rel.append({"op": "deallocate1", "seqs": [_seq_state(s) for s in seqs], "bm": _bm_state(bm)})
+    new_prompt = shared + rng.integers(0, 50000, 700).tolist()
+    new = Sequence(new_prompt, sp)
+    rel.append({"op": "can_allocate", "value": bm.can_allocate(new)})
+    bm.allocate(new)
+    rel.append({"op": "allocate_new", "seq": _seq_state(new), "bm": _bm_state(bm)})
+    bm.deallocate(seqs[3])
+    bm.deallocate(new)
+    rel.append({"op": "deallocate3_new", "seqs": [_seq_state(s) for s in seqs],
+                "new": _seq_state(new), "bm": _bm_state(bm)})
+    trace["block_manager_release"] = {"new_prompt": new_prompt, "steps": rel}
+
     # --- periodic selection: ModelRunner.prepare_decode (model_runner.py:265-333)
     cfg = types.SimpleNamespace(kv_compress_window_blocks=4, kv_compress_topk=2,
                                 kv_compress_period=3)

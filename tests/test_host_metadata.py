@@ -36,7 +36,7 @@ def _bm_state(bm):
             "ref": [b.ref_count for b in bm.blocks], "hash_set": [b.hash != -1 for b in bm.blocks]}
 
 
-def test_block_manager_and_events_replay(trace):
+def _replay_block_manager(trace, check: bool):
     tr = trace["block_manager"]
     rng = np.random.default_rng(5)
     shared = rng.integers(0, 50000, 512).tolist()
@@ -76,14 +76,43 @@ def test_block_manager_and_events_replay(trace):
         for s, t in zip(seqs, token_ids):
             s.num_computed_tokens += 1
             s.append_token(t)
-        if events or step % 50 == 0:
+        if check and (events or step % 50 == 0):
             rec = next(recorded)
             assert rec["op"] == f"step{step}"
             assert rec["events"] == events
             assert [_seq_state(s) for s in seqs] == rec["seqs"], f"seq state at step {step}"
             assert _bm_state(bm) == rec["bm"], f"block manager at step {step}"
             checked += 1
-    assert checked == len(tr["steps"])
+    assert not check or checked == len(tr["steps"])
+    return bm, seqs
+
+
+def test_block_manager_and_events_replay(trace):
+    _replay_block_manager(trace, check=True)
+
+
+def test_block_manager_release_and_prefix_reuse(trace):
+    """After the replay: can_append, deallocate of a sequence sharing prefix
+    blocks, can_allocate / allocate of a new prompt that hits the prefix
+    cache, and two more deallocations, against the reference's BlockManager
+    (nanokvllm/engine/block_manager.py:55-96)."""
+    bm, seqs = _replay_block_manager(trace, check=False)
+    rel = iter(trace["block_manager_release"]["steps"])
+    rec = next(rel)
+    assert [bm.can_append(s) for s in seqs] == rec["value"]
+    bm.deallocate(seqs[1])
+    rec = next(rel)
+    assert [_seq_state(s) for s in seqs] == rec["seqs"] and _bm_state(bm) == rec["bm"]
+    new = Sequence(trace["block_manager_release"]["new_prompt"], max_tokens=10**6, ignore_eos=True)
+    assert bm.can_allocate(new) == next(rel)["value"]
+    bm.allocate(new)
+    rec = next(rel)
+    assert _seq_state(new) == rec["seq"] and _bm_state(bm) == rec["bm"]
+    bm.deallocate(seqs[3])
+    bm.deallocate(new)
+    rec = next(rel)
+    assert [_seq_state(s) for s in seqs] == rec["seqs"] and _seq_state(new) == rec["new"]
+    assert _bm_state(bm) == rec["bm"]
 
 
 def test_periodic_selection_matches_prepare_decode(trace):
