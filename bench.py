@@ -911,11 +911,33 @@ def run_profile_case(kind: str) -> None:
     `compress` runs one config-3 window-compression event 4 times;
     `prefill` runs one chunked-prefill attention launch (Qwen3-32B shapes,
     4 x 2,048 queries over 10,240 keys) 4 times; `norm_rope` runs the q/k
-    norm + RoPE + store of a 32k-token chunk 4 times."""
+    norm + RoPE + store of a 32k-token chunk 4 times; `threshold` runs one
+    layer of config 5's KvChat threshold compression (Qwen3-0.6B shapes, one
+    sequence, S = prompt + 511 -> R = prompt + 257, W = 50) 4 times."""
     from nanokv_b200 import ops
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if kind == "threshold":
+        hq, hk, P, W = 16, 8, 256, 50
+        S, R = P + 511, P + 257
+        nb = (S + BLOCK - 1) // BLOCK
+        g = torch.Generator(device=dev).manual_seed(5)
+        kc = torch.randn(nb, BLOCK, hk, D, device=dev, generator=g).to(torch.bfloat16)
+        vc = torch.randn(nb, BLOCK, hk, D, device=dev, generator=g).to(torch.bfloat16)
+        ring = torch.randn(1, 1, W, hq, D, device=dev, generator=g).to(torch.bfloat16)
+        bt = torch.arange(nb, dtype=torch.int32, device=dev).view(1, nb)
+        cl = torch.tensor([S], dtype=torch.int32, device=dev)
+        zero = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(4):
+            cl.fill_(S)
+            ops.threshold_compress(ring, zero, 0, kc, vc, bt, cl, zero, S, R)
+        torch.cuda.synchronize()
+        keys = S - W
+        nbytes = keys * hk * D * 2 + 2 * 2 * R * hk * D * 2 + W * hq * D * 2
+        print(json.dumps({"profile": kind, "alg_bytes": nbytes,
+                          "score_flops": 2 * W * hq * keys * D}))
+        return
     if kind == "compress":
         for _ in range(4):
             measure_compress(dev, HQ, HK)
@@ -989,7 +1011,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
-    ap.add_argument("--profile", choices=["decode", "compress", "prefill", "norm_rope"],
+    ap.add_argument("--profile", choices=["decode", "compress", "prefill", "norm_rope", "threshold"],
                     default=None,
                     help="run a small case for an ncu capture and exit")
     args = ap.parse_args()
