@@ -850,7 +850,7 @@ def run_reference(args, rank, world):
         return None
     # the CPU implementation serves the whole job (all heads) whatever N is
     hq, hk = HQ, HK
-    per_step = max(2.0, 40.0 / max(1, args.steps + args.warmup))
+    per_step = max(min(2.0, args.ref_seconds), args.ref_seconds / max(1, args.steps + args.warmup))
     vals = []
     desc = ""
     threads = 1
@@ -1011,6 +1011,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
+    ap.add_argument("--ref-seconds", type=float, default=40.0,
+                    help="CPU work the reference arm samples over the whole run (seconds)")
     ap.add_argument("--profile", choices=["decode", "compress", "prefill", "norm_rope", "threshold"],
                     default=None,
                     help="run a small case for an ncu capture and exit")
