@@ -292,12 +292,22 @@ def run_gpu(args, rank, world, dev):
         e2e_body(False)
     torch.cuda.synchronize(dev)
     e2e_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(e2e_graph):
-        e2e_body(True)
-    torch.cuda.synchronize(dev)
+    e2e_mode = "cuda_graph"
+    try:
+        with torch.cuda.graph(e2e_graph):
+            e2e_body(True)
+        torch.cuda.synchronize(dev)
+    except RuntimeError as exc:  # capture refused: the same step, eagerly
+        print(f"e2e graph capture failed ({exc}); timing the eager step", file=sys.stderr)
+        reset_context()
+        e2e_graph, e2e_mode = None, "eager"
+        torch.cuda.synchronize(dev)
 
     def e2e_step():
-        e2e_graph.replay()
+        if e2e_graph is not None:
+            e2e_graph.replay()
+        else:
+            e2e_body(False)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -343,7 +353,7 @@ def run_gpu(args, rank, world, dev):
             "ms_per_step": round(ref_gpu, 4), "tok_per_s": round(BATCH * 1000.0 / ref_gpu, 1),
             "ours_speedup": round(ref_gpu / ms * args.steps, 3)}
     return dict(ms=ms, e2e_ms=e2e_ms, dec_avg_ms=dec_avg, alg_bytes=alg, clocks=clk,
-                resident=R, h2d=h2d, d2h=d2h, compress=comp, extra=extra)
+                resident=R, h2d=h2d, d2h=d2h, compress=comp, extra=extra, e2e_mode=e2e_mode)
 
 
 def reference_gpu_step_ms(args, dev, st, qkv, layer_views, kv, R, bt, cl, sm, scale, hq, hk,
@@ -1061,10 +1071,11 @@ def main():
             "data": "synthetic (N(0,1) q/k/v and cache, seeded)",
             "config": config_dict(world, r["resident"]),
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": r["h2d"],
-                    "d2h_bytes_per_step": r["d2h"],
+                    "d2h_bytes_per_step": r["d2h"], "mode": r["e2e_mode"],
                     "path": "nanokv_b200.layers.attention.Attention.forward per layer, the step "
                             "captured in a CUDA graph (as ModelRunner captures decode) and "
-                            "replayed; every step copies all layers' q/k/v and metadata from "
+                            "replayed (mode 'eager' if the capture was refused); every step "
+                            "copies all layers' q/k/v and metadata from "
                             "pinned host memory (copy stream, overlapped with compute) and "
                             "copies every output back"},
             "roofline": {"kernel": "nkv paged_decode_kernel (fused decode step: slot write + "
