@@ -310,6 +310,49 @@ def test_window_compress_tp_shapes(cuda_lib):
         assert _deverr() == 0
 
 
+def test_window_compaction_maximal_overlap(cuda_lib):
+    """The compaction's read-all-then-write hazard, made maximal: keep 1,021
+    of the window's 1,022 candidate keys (keep_tokens 1,023) and make key 1
+    the least important (its K opposes every q head of its group), so the
+    kept set is [0, 2, 3, ..., 1023] and every kept row moves down by
+    exactly one slot, onto the row read just before it. The reference stages
+    the rows through .clone() (nanokvllm/layers/compress_utils.py:257-260);
+    the kernel reads each 64-row chunk before writing it. Cache bytes must
+    equal the oracle's staged copy bit for bit."""
+    ops = _ops()
+    Hq, Hk, D, B, wb = 32, 8, 128, 256, 4
+    g = Hq // Hk
+    pb = make_paged_batch(seed=91, lens=[1500, 2600], Hq=Hq, Hk=Hk)
+    k0, v0 = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(pb.k_new, pb.v_new, k0, v0, pb.slot_mapping)
+    kf = k0.view(-1, Hk, D)
+    for b in range(2):
+        full = int(pb.context_lens[b]) // B  # the window: the last 4 full blocks
+        slot = int(pb.block_tables[b, full - wb]) * B + 1
+        for h in range(Hk):
+            qs = pb.q[b, h * g:(h + 1) * g].float().sum(0)
+            kf[slot, h] = (-30.0 * qs / qs.norm()).to(torch.bfloat16)
+    keep_tokens = 3 * B + 255
+    expect = [0] + list(range(2, wb * B))
+    assert len(expect) == keep_tokens
+    kd, vd = k0.to(DEV), v0.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    sel = torch.tensor([0, 1], dtype=torch.int32, device=DEV)
+    keep_out = torch.full((2, keep_tokens), -7, dtype=torch.int32, device=DEV)
+    ops.window_compress(pb.q.to(DEV), kd, vd, pb.block_tables.to(DEV), cl.clone(), cl, sel, wb,
+                        keep_tokens, out_keep_idx=keep_out)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    assert keep_out.cpu().tolist() == [expect, expect]
+    k1, v1, cl1 = k0.clone(), v0.clone(), pb.context_lens.clone()
+    okeep, _ = window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1,
+                                   [0, 1], B, wb, 3, 255)
+    assert okeep.tolist() == [expect, expect]
+    assert torch.equal(kd.cpu().view(torch.int16), k1.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v1.view(torch.int16))
+    assert cl.cpu().tolist() == cl1.tolist()
+
+
 # ------------------------------------------------------------------ KvChat
 @pytest.mark.parametrize("case", THRESHOLD_CASES, ids=[c[0] for c in THRESHOLD_CASES])
 def test_threshold_compress_parity(cuda_lib, golden_dir, case):
