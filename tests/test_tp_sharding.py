@@ -86,3 +86,55 @@ def test_two_rank_kv_head_sharding():
     assert gathered[0]["events"] == gathered[1]["events"]
     assert gathered[0]["lens"] == gathered[1]["lens"] == [300, 789, 1589, 989]
     assert gathered[0]["keep"].shape == gathered[1]["keep"].shape
+
+
+def _faulty_rank_main(rank, world, port, repo, out_q):
+    """Rank 1 fails (raises) before the step's metadata exchange; rank 0 must
+    learn it from the collective -- an error within the group's short
+    timeout -- instead of blocking forever."""
+    import datetime
+    import sys
+    sys.path[:0] = [repo]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    from oracle.inputs import make_paged_batch
+    from oracle.window_compress import compression_events, window_compress_ref
+
+    pb = make_paged_batch(seed=5, lens=[300, 1300, 2100, 1500], Hq=16, Hk=8)
+    hk, hq = 8 // world, 16 // world
+    ks, qs = slice(rank * hk, (rank + 1) * hk), slice(rank * hq, (rank + 1) * hq)
+    kc, vc = pb.k_cache[:, :, ks].contiguous(), pb.v_cache[:, :, ks].contiguous()
+    cl = pb.context_lens.clone()
+    _, new_lens = window_compress_ref(pb.q[:, qs].contiguous(), kc, vc, pb.block_tables,
+                                      pb.context_lens.clone(), cl, [1, 2], 256, 4, 2, 1)
+    ev = compression_events(pb.block_tables, [1, 2], new_lens, 256, 0)
+    if rank == 1:
+        raise SystemExit(3)  # dies between steps, with no collective in flight
+    import time
+    t0 = time.monotonic()
+    try:
+        got = [None] * world
+        dist.all_gather_object(got, ev)
+        out_q.put(("no error", time.monotonic() - t0))
+    except Exception as exc:  # noqa: BLE001 - any collective error is the detection
+        out_q.put(("detected", time.monotonic() - t0, type(exc).__name__))
+
+
+@pytest.mark.timeout(300)
+def test_dead_rank_is_detected_not_waited_for():
+    world = 2
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_faulty_rank_main, args=(r, world, port, repo, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "detected", res
+    assert res[1] < 60, res  # well inside the group's timeout plus set-up slack
+    assert procs[1].exitcode == 3
