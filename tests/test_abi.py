@@ -101,3 +101,55 @@ def test_norm_rope_argument_errors_need_no_gpu():
     assert call(cs=24) == 4                 # cos/sin cache must be 16-byte aligned
     assert call(kc=16) == 1                 # cache without v_cache / slot_mapping
     assert call(T=0) == 0
+
+
+def _header_prototypes() -> dict[str, list[str]]:
+    """name -> parameter type strings, parsed from include/nkv.h."""
+    text = (REPO / "include" / "nkv.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    protos = {}
+    for m in re.finditer(r"\b(nkv_[a-z_0-9]+)\s*\(([^)]*)\)\s*;", text):
+        params = [p.strip() for p in m.group(2).split(",") if p.strip()]
+        if params == ["void"]:
+            params = []
+        # drop the parameter name: the type is everything before the last word
+        protos[m.group(1)] = [re.sub(r"\s*\b\w+$", "", p).strip() for p in params]
+    return protos
+
+
+def _ctypes_kind(ct) -> str:
+    import ctypes
+    if ct in (ctypes.c_void_p, ctypes.c_char_p) or hasattr(ct, "contents") or \
+            getattr(ct, "_type_", None) is not None and ct.__name__.startswith("LP_"):
+        return "ptr"
+    size = ctypes.sizeof(ct)
+    if ct in (ctypes.c_float,):
+        return "f32"
+    if ct in (ctypes.c_double,):
+        return "f64"
+    return f"int{size * 8}"
+
+
+def _c_kind(t: str) -> str:
+    if "*" in t:
+        return "ptr"
+    t = t.replace("const", "").strip()
+    return {"float": "f32", "double": "f64", "int": "int32", "int32_t": "int32",
+            "uint32_t": "int32", "int64_t": "int64", "uint64_t": "int64", "size_t": "int64",
+            "unsigned": "int32", "unsigned int": "int32"}.get(t, "?" + t)
+
+
+def test_ctypes_argtypes_match_header_prototypes():
+    """Every binding in _lib.SIGNATURES has the prototype's parameter count,
+    and each parameter's kind (pointer / 32- or 64-bit integer / float)
+    matches the header's type, so the ABI cannot drift silently."""
+    from nanokv_b200 import _lib
+
+    protos = _header_prototypes()
+    assert set(protos) == set(_lib.SIGNATURES)
+    for name, (_, argtypes) in _lib.SIGNATURES.items():
+        ctypes_kinds = [_ctypes_kind(a) for a in argtypes]
+        c_kinds = [_c_kind(t) for t in protos[name]]
+        assert len(ctypes_kinds) == len(c_kinds), (name, len(ctypes_kinds), len(c_kinds))
+        assert ctypes_kinds == c_kinds, (name, list(zip(c_kinds, ctypes_kinds)))
