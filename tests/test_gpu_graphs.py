@@ -91,3 +91,61 @@ def test_query_window_append_replayed_from_graph(cuda_lib):
     for step in range(W):
         assert torch.all(r[2, 1, step] == step + 1) and torch.all(r[0, 1, step] == step + 1)
     assert torch.all(r[1] == 0) and torch.all(r[:, 0] == 0)
+
+
+def test_graph_replay_with_padding_rows(cuda_lib):
+    """The reference's graph replay for a batch smaller than the captured
+    one (nanokvllm/engine/model_runner.py:370-376): rows past the batch get
+    slot_mapping -1 and context_lens 0. The fused decode step must skip
+    their store, give them a defined (zero) output instead of NaNs, and
+    leave the live rows and the cache exactly as for the unpadded batch."""
+    from nanokv_b200 import _lib, ops
+
+    Hq, Hk, D = 32, 8, 128
+    lens = [700, 3000, 1900, 260]
+    live = 2  # the step's real batch; rows 2 and 3 are padding
+    pb = make_paged_batch(seed=62, lens=lens, Hq=Hq, Hk=Hk, num_blocks=64)
+    B = len(lens)
+    kc, vc = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+    bt = pb.block_tables.to(DEV).clone()
+    cl = torch.zeros(B, dtype=torch.int32, device=DEV)
+    sm = torch.full((B,), -1, dtype=torch.int32, device=DEV)
+    qkv = torch.zeros(B, (Hq + 2 * Hk) * D, dtype=torch.bfloat16, device=DEV)
+    q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
+    q, k, v = q.view(B, Hq, D), k.view(B, Hk, D), v.view(B, Hk, D)
+    out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=DEV)
+    ws = ops.decode_workspace(torch.device(DEV), B, Hq, Hk, D, bt.size(1), 256)
+
+    def step():
+        ops.decode_step(q, k, v, kc, vc, sm, bt, cl, D ** -0.5, out=out, workspace=ws)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    new = bf16(np.random.default_rng(63).standard_normal((B, (Hq + 2 * Hk) * D),
+                                                          dtype=np.float32))
+    qkv.copy_(new.to(DEV))
+    slots = [int(pb.block_tables[b, (lens[b] - 1) // 256]) * 256 + (lens[b] - 1) % 256
+             for b in range(live)]
+    # as the reference fills its graph inputs: -1 slots and zero lengths past bs
+    sm.fill_(-1)
+    sm[:live] = torch.tensor(slots, dtype=torch.int32)
+    cl.zero_()
+    cl[:live] = torch.tensor(lens[:live], dtype=torch.int32)
+    out.fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert _lib.read_device_error(clear=True) == 0
+    nq, nk, nv = new.split([Hq * D, Hk * D, Hk * D], dim=-1)
+    ref_k, ref_v = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(nk[:live].reshape(live, Hk, D), nv[:live].reshape(live, Hk, D), ref_k, ref_v,
+                      torch.tensor(slots, dtype=torch.int32))
+    ref = paged_decode_ref(nq[:live].reshape(live, Hq, D), ref_k, ref_v, pb.block_tables[:live],
+                           torch.tensor(lens[:live], dtype=torch.int32), D ** -0.5)
+    got = out.float().cpu()
+    assert (got[:live] - ref).abs().max().item() <= 2e-2
+    assert torch.equal(got[live:], torch.zeros_like(got[live:]))  # defined, not NaN
+    assert torch.equal(kc.cpu().view(torch.int16), ref_k.view(torch.int16))
+    assert torch.equal(vc.cpu().view(torch.int16), ref_v.view(torch.int16))
