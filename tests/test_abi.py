@@ -153,3 +153,88 @@ def test_ctypes_argtypes_match_header_prototypes():
         c_kinds = [_c_kind(t) for t in protos[name]]
         assert len(ctypes_kinds) == len(c_kinds), (name, len(ctypes_kinds), len(c_kinds))
         assert ctypes_kinds == c_kinds, (name, list(zip(c_kinds, ctypes_kinds)))
+
+
+def test_newer_entry_points_validate_before_any_cuda_call():
+    """Status codes (no exceptions across the ABI) for the prefill, q/k
+    norm + RoPE, device selection and o_proj entries, from argument checks
+    that run before any CUDA call. Status: 0 ok, 1 invalid argument,
+    2 unsupported, 4 alignment."""
+    from nanokv_b200 import _lib
+
+    lib = _lib.load()
+    OK, INVALID, UNSUPPORTED, ALIGN = 0, 1, 2, 4
+    nan = float("nan")
+
+    def prefill(**kw):
+        a = dict(q=4096, qst=4096, qsh=128, T=16, k=4096, kst=1024, v=8192, vst=1024, rows=256,
+                 bt=None, mb=0, bs=0, cuq=16, cuk=16, batch=1, maxq=16, causal=1, out=4096,
+                 ost=4096, hq=32, hk=8, d=128, scale=0.088)
+        a.update(kw)
+        return lib.nkv_paged_prefill(a["q"], a["qst"], a["qsh"], a["T"], a["k"], a["kst"], a["v"],
+                                     a["vst"], a["rows"], a["bt"], a["mb"], a["bs"], a["cuq"],
+                                     a["cuk"], a["batch"], a["maxq"], a["causal"], a["out"],
+                                     a["ost"], a["hq"], a["hk"], a["d"], a["scale"], None)
+
+    assert prefill(batch=0) == OK
+    assert prefill(hq=30) == INVALID          # Hq not a multiple of Hk
+    assert prefill(scale=nan) == INVALID
+    assert prefill(d=64) == UNSUPPORTED
+    assert prefill(bt=16, mb=4, bs=100) == UNSUPPORTED  # 128-key tiles need 64 or k*128
+    assert prefill(q=4098) == ALIGN
+    assert prefill(ost=100) == INVALID         # output rows shorter than Hq * 128
+
+    def norm_rope(**kw):
+        a = dict(qkv=4096, st=6144, T=4, pos=16, cs=4096, maxpos=1024, qw=4096, kw=4096, eps=1e-6,
+                 qo=4096, qost=4096, ko=None, kost=0, kc=None, vc=None, ns=0, sm=None, hq=32,
+                 hk=8, d=128)
+        a.update(kw)
+        return lib.nkv_qk_norm_rope_store(a["qkv"], a["st"], a["T"], a["pos"], a["cs"],
+                                          a["maxpos"], a["qw"], a["kw"], a["eps"], a["qo"],
+                                          a["qost"], a["ko"], a["kost"], a["kc"], a["vc"],
+                                          a["ns"], a["sm"], a["hq"], a["hk"], a["d"], None)
+
+    assert norm_rope(T=0) == OK
+    assert norm_rope(d=64) == UNSUPPORTED
+    assert norm_rope(eps=-1.0) == INVALID
+    assert norm_rope(kc=4096, vc=8192, ns=64) == INVALID   # a cache needs its slot_mapping
+    assert norm_rope(st=100) == INVALID
+    assert norm_rope(qkv=4098) == ALIGN
+
+    assert lib.nkv_window_select(16, 16, -1, 256, 4, 2, 16, None, None, None) == INVALID
+    assert lib.nkv_window_select(None, None, 0, 256, 4, 0, None, None, None, None) == OK
+    assert lib.nkv_window_select(16, 16, 2, 256, 4, 2, None, None, None, None) == INVALID
+
+    def oproj(**kw):
+        a = dict(x=4096, ldx=512, w=8192, ldw=512, T=16, k=512, n=1024, pmc=4096, pl=4096,
+                 omc=4096, ol=4096, smc=4096, sl=4096, flags=4096, rank=0, world=2, to=10**9,
+                 ws=4096, wsb=1 << 20, y=4096, ldy=1024)
+        a.update(kw)
+        return lib.nkv_oproj_allreduce(a["x"], a["ldx"], a["w"], a["ldw"], a["T"], a["k"], a["n"],
+                                       a["pmc"], a["pl"], a["omc"], a["ol"], a["smc"], a["sl"],
+                                       a["flags"], a["rank"], a["world"], a["to"], a["ws"],
+                                       a["wsb"], a["y"], a["ldy"], None)
+
+    assert oproj(T=0) == OK
+    assert oproj(rank=2) == INVALID
+    assert oproj(pl=None) == INVALID
+    assert oproj(k=100) == UNSUPPORTED
+    assert oproj(T=513) == UNSUPPORTED         # decode-sized steps only
+    assert oproj(ldy=100) == INVALID
+    assert oproj(x=4098) == ALIGN
+
+    def p2p(**kw):
+        a = dict(x=4096, ldx=512, w=8192, ldw=512, T=16, k=512, n=1024, rp=4096, ss=16 * 1024,
+                 sp=4096, sl=4096, flags=4096, rank=0, world=2, to=10**9, ws=4096, wsb=1 << 20,
+                 y=4096, ldy=1024)
+        a.update(kw)
+        return lib.nkv_oproj_allreduce_p2p(a["x"], a["ldx"], a["w"], a["ldw"], a["T"], a["k"],
+                                           a["n"], a["rp"], a["ss"], a["sp"], a["sl"], a["flags"],
+                                           a["rank"], a["world"], a["to"], a["ws"], a["wsb"],
+                                           a["y"], a["ldy"], None)
+
+    assert p2p(T=0) == OK
+    assert p2p(rp=None) == INVALID
+    assert p2p(ss=16 * 1024 - 8) == INVALID    # a slot must hold tokens x n
+    assert p2p(ss=16 * 1024 + 4) == ALIGN      # slots start on 16 bytes
+    assert p2p(world=0) == INVALID
