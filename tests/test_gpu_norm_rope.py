@@ -176,3 +176,56 @@ def test_attention_forward_qkv_prefill_step(cuda_lib):
         out = o.float().cpu()
         assert (out - ref).abs().max().item() <= 2e-2, f"paged={paged}"
         assert ((out - ref).norm() / ref.norm()).item() <= 1e-2, f"paged={paged}"
+
+
+def test_kvchat_forward_qkv_decode_step_with_query_window(cuda_lib):
+    """KvChat's Attention.forward_qkv on a decode step inside the query
+    window (S - W < len <= S, no compression yet): q/k norm + RoPE + slot
+    write in one launch, then this step's rotated queries appended to the
+    window ring, then decode -- against the oracle sequence (norm, RoPE,
+    store, the reference's QueryWindowManager.append, decode)."""
+    from nanokv_b200.engine.compress_schedule import prepare_threshold_context
+    from nanokv_b200.engine.query_window import QueryWindowManager
+    from nanokv_b200.engine.sequence import Sequence
+    from nanokv_b200.layers.kvchat import Attention as KvChatAttention
+    from nanokv_b200.utils.context import get_context, reset_context, set_kvchat_context
+
+    P, Hq, Hk, D, W = 64, 16, 8, 128, 50
+    S = P + 511
+    length = S - W + 5
+    cfg = types.SimpleNamespace(kv_compress_enabled=True, kv_compress_N=4, kv_compress_S=511,
+                                kv_compress_R=257, query_window_size=W)
+    pb = make_paged_batch(seed=87, lens=[length], Hq=Hq, Hk=Hk)
+    qwm = QueryWindowManager(1, W, Hq, D, device=DEV)
+    a = KvChatAttention(Hq, D, D ** -0.5, Hk, cfg, 1)
+    a.query_window_manager = qwm
+    a.k_cache, a.v_cache = pb.k_cache.clone().to(DEV), pb.v_cache.clone().to(DEV)
+    seq = Sequence(list(range(P)))
+    seq.num_tokens = length
+    rng = np.random.default_rng(88)
+    qkv = torch.from_numpy(rng.standard_normal((1, (Hq + 2 * Hk) * D), dtype=np.float32)
+                           ).to(torch.bfloat16)
+    positions = torch.tensor([length - 1], dtype=torch.int64)
+    cs = rope_cache(4096, 1000000.0)
+    qw, kw = _layer_weights(89)
+    set_kvchat_context(False, slot_mapping=pb.slot_mapping.to(DEV),
+                       context_lens=pb.context_lens.to(DEV), block_tables=pb.block_tables.to(DEV))
+    ctx = get_context()
+    prepare_threshold_context(ctx, [seq], cfg, qwm)
+    assert ctx.q_window_active_indices == [0] and not ctx.compress_any
+    slot = qwm.slot_of(seq.seq_id)
+    o = a.forward_qkv(qkv.to(DEV), positions.to(DEV), qw.to(DEV), kw.to(DEV), cs.to(DEV), 1e-6, 0)
+    torch.cuda.synchronize()
+    reset_context()
+    assert _deverr() == 0
+    kc, vc = pb.k_cache.clone(), pb.v_cache.clone()
+    q_ref, _, _ = qk_norm_rope_store_ref(qkv, positions, cs, qw, kw, 1e-6, Hq, Hk, kc, vc,
+                                         pb.slot_mapping)
+    ref = paged_decode_ref(q_ref, kc, vc, pb.block_tables, pb.context_lens, D ** -0.5)
+    out = o[:, 0].float().cpu()
+    assert (out - ref).abs().max().item() <= 2e-2
+    assert ((out - ref).norm() / ref.norm()).item() <= 1e-2
+    _ulp_close(qwm.ring[slot, 0, 0].cpu(), q_ref[0], "query window row")
+    assert qwm.buffers[seq.seq_id][1] == 1  # the write position moved on
+    _ulp_close(a.k_cache, kc, "stored k")
+    assert torch.equal(a.v_cache.cpu().view(torch.int16), vc.view(torch.int16))
