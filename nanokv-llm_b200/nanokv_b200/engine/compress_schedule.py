@@ -21,11 +21,28 @@
 from __future__ import annotations
 
 from dataclasses import dataclass
+from itertools import chain
 
 import numpy as np
 import torch
 
 from ..utils.context import Context
+
+
+def padded_block_tables(seqs) -> tuple[np.ndarray, np.ndarray]:
+    """The reference's prepare_block_tables (nanokvllm/engine/model_runner.py:154-158)
+    on the host: rows padded with -1 to the longest table, int32; one
+    scatter of all tables instead of a copy per row. Also returns the
+    widths."""
+    tables = [s.block_table for s in seqs]
+    n = len(tables)
+    widths = np.fromiter(map(len, tables), dtype=np.int64, count=n)
+    mb = int(widths.max()) if n else 0
+    bt = np.full((n, mb), -1, dtype=np.int32)
+    if n:
+        bt[np.arange(mb) < widths[:, None]] = np.fromiter(
+            chain.from_iterable(tables), dtype=np.int32, count=int(widths.sum()))
+    return bt, widths
 
 
 @dataclass
@@ -40,11 +57,7 @@ class DecodeMetadata:
     def build(cls, seqs, block_size: int) -> "DecodeMetadata":
         n = len(seqs)
         lens = np.fromiter((s.num_tokens for s in seqs), dtype=np.int64, count=n)
-        widths = np.fromiter((len(s.block_table) for s in seqs), dtype=np.int64, count=n)
-        mb = int(widths.max()) if n else 0
-        bt = np.full((n, mb), -1, dtype=np.int32)
-        for i, s in enumerate(seqs):
-            bt[i, :widths[i]] = s.block_table
+        bt, widths = padded_block_tables(seqs)
         last_blk = bt[np.arange(n), np.maximum(widths - 1, 0)].astype(np.int64)
         last_cnt = lens - (((lens + block_size - 1) // block_size) - 1) * block_size
         slots = last_blk * block_size + last_cnt - 1

@@ -32,6 +32,7 @@ import numpy as np
 import torch
 
 from ..utils.context import set_context
+from .compress_schedule import padded_block_tables
 
 
 @dataclass
@@ -63,11 +64,7 @@ class StepMetadata:
         rows = np.repeat(np.arange(n), news)
         positions = np.arange(total, dtype=np.int64) - np.repeat(cu_q[:-1] - starts, news)
 
-        widths = np.fromiter((len(s.block_table) for s in seqs), dtype=np.int64, count=n)
-        mb = int(widths.max()) if n else 0
-        bt = np.full((n, mb), -1, dtype=np.int32)
-        for i, s in enumerate(seqs):
-            bt[i, :widths[i]] = s.block_table
+        bt, widths = padded_block_tables(seqs)
         blk = positions // block_size
         # the reference indexes seq.block_table[pos // block_size] and fails
         # past its end
