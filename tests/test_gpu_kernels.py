@@ -161,6 +161,48 @@ def test_decode_config2_shape_subset(cuda_lib):
     _check_decode(pb, 32)
 
 
+def test_decode_config2_full_batch_properties(cuda_lib):
+    """BASELINE config 2 at full size for one layer: 256 rows of Qwen3-8B
+    shapes (32 q / 8 kv heads), lengths U[1024, 8192] (seed 0), ~4.8 GB of
+    K/V generated on the device. Size-independent properties: 8 sampled rows
+    equal the oracle (each row checked on its own blocks), and the batch
+    processed in reverse order gives bit-identical rows (a row's result does
+    not depend on which CTA or split order served it)."""
+    ops = _ops()
+    B, Hq, Hk, D, BS = 256, 32, 8, 128, 256
+    lens = np.random.default_rng(0).integers(1024, 8193, B)
+    nblk = (lens + BS - 1) // BS
+    nb = int(nblk.sum())
+    g = torch.Generator(device=DEV).manual_seed(21)
+    kc = torch.randn(nb, BS, Hk, D, device=DEV, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(nb, BS, Hk, D, device=DEV, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(B, Hq, D, device=DEV, generator=g, dtype=torch.bfloat16)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(22)).to(torch.int32)
+    bt = torch.full((B, int(nblk.max())), -1, dtype=torch.int32)
+    o = 0
+    for b in range(B):
+        bt[b, :nblk[b]] = perm[o:o + nblk[b]]
+        o += int(nblk[b])
+    cl = torch.tensor(lens, dtype=torch.int32)
+    btd, cld = bt.to(DEV), cl.to(DEV)
+    out = ops.paged_decode(q, kc, vc, btd, cld, D ** -0.5)
+    rev = torch.arange(B - 1, -1, -1, device=DEV)
+    out_rev = ops.paged_decode(q[rev].contiguous(), kc, vc, btd[rev].contiguous(),
+                               cld[rev].contiguous(), D ** -0.5)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    assert torch.equal(out_rev[rev].view(torch.int16), out.view(torch.int16))
+    for b in (0, 17, 64, 100, 128, 200, 231, 255):
+        blocks = bt[b, :nblk[b]].long().to(DEV)
+        ks, vs = kc[blocks].cpu(), vc[blocks].cpu()
+        ref = paged_decode_ref(q[b:b + 1].cpu(), ks, vs,
+                               torch.arange(int(nblk[b]), dtype=torch.int32).view(1, -1),
+                               cl[b:b + 1], D ** -0.5)
+        got = out[b:b + 1].float().cpu()
+        assert (got - ref).abs().max().item() <= ATOL, f"row {b}"
+        assert ((got - ref).norm() / ref.norm()).item() <= RTOL, f"row {b}"
+
+
 def test_decode_repeated_calls_reuse_workspace(cuda_lib):
     """The workspace must come back zeroed: many calls, same results."""
     ops = _ops()
