@@ -234,3 +234,40 @@ def test_attention_layer_prefill_step(cuda_lib):
     ref = varlen_attention_ref(vb.q, kr, vr, vb.cu_seqlens_q, vb.cu_seqlens_k, D ** -0.5, True,
                                vb.block_tables)
     _close(o, ref, "layer prefill")
+
+
+def test_prefill_config4_full_chunk_sampled_rows(cuda_lib):
+    """BASELINE config 4's last prefill chunk at full size for one layer: 16
+    rows x 2,048 new tokens over 30,720 cached tokens, Qwen3-32B attention
+    shapes (64 q / 8 kv heads), the cache in 256-token blocks (~1 GB each of
+    K and V, generated on the device). Size-independent property: sampled
+    query rows -- first, middle and last of the chunk of three sequences --
+    equal the oracle attending over their own causal prefix."""
+    ops = _ops()
+    B, Hq, Hk, D, BS, chunk, L = 16, 64, 8, 128, 256, 2048, 32768
+    nbs = L // BS
+    nb = B * nbs
+    g = torch.Generator(device=DEV).manual_seed(31)
+    kc = torch.randn(nb, BS, Hk, D, device=DEV, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(nb, BS, Hk, D, device=DEV, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(B * chunk, Hq, D, device=DEV, generator=g, dtype=torch.bfloat16)
+    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(32)).to(torch.int32).view(B, nbs)
+    cu_q = torch.arange(B + 1, dtype=torch.int32) * chunk
+    cu_k = torch.arange(B + 1, dtype=torch.int32) * L
+    out = ops.paged_prefill(q, kc, vc, cu_q.to(DEV), cu_k.to(DEV), chunk, D ** -0.5,
+                            block_table=bt.to(DEV))
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    for b in (0, 9, 15):
+        for i in (0, chunk // 2, chunk - 1):
+            p = L - chunk + i  # absolute position; keys 0..p are visible
+            nblk = p // BS + 1
+            blocks = bt[b, :nblk].long().to(DEV)
+            ks = kc[blocks].cpu().view(-1, Hk, D)[:p + 1]
+            vs = vc[blocks].cpu().view(-1, Hk, D)[:p + 1]
+            row = b * chunk + i
+            ref = varlen_attention_ref(q[row:row + 1].cpu(), ks, vs,
+                                       torch.tensor([0, 1], dtype=torch.int32),
+                                       torch.tensor([0, p + 1], dtype=torch.int32), D ** -0.5,
+                                       True, None)
+            _close(out[row:row + 1], ref, f"seq {b} row {i}")
