@@ -352,6 +352,48 @@ def test_window_compress_tp_shapes(cuda_lib):
         assert _deverr() == 0
 
 
+def test_window_compress_config3_event_full_size(cuda_lib):
+    """BASELINE config 3's compression event at full size for one layer: 20
+    selected sequences of Qwen3-8B shapes (32 q / 8 kv heads) with config 3's
+    per-head outlier channels (sigma 4 on 5 % of the dims), contexts of
+    1,100-4,396 tokens, a 4-block window, 513 kept tokens. Kept sets equal
+    the oracle's up to swaps inside the bf16 tie band at the cut, new lengths
+    exactly, and the compaction is bit-exact given the kernel's kept set."""
+    ops = _ops()
+    lens = np.random.default_rng(33).integers(1100, 4397, 20).tolist()
+    pb = make_paged_batch(seed=34, lens=lens, Hq=32, Hk=8, outlier_sigma=4.0, outlier_frac=0.05)
+    sel = list(range(20))
+    wb, kb, ke = 4, 2, 1
+    keep_tokens, num_keep = kb * 256 + ke, kb * 256 + ke - 2
+    kd, vd = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    keep_out = torch.full((len(sel), keep_tokens), -7, dtype=torch.int32, device=DEV)
+    ops.window_compress(pb.q.to(DEV), kd, vd, pb.block_tables.to(DEV), cl.clone(), cl,
+                        torch.tensor(sel, dtype=torch.int32, device=DEV), wb, keep_tokens,
+                        out_keep_idx=keep_out)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    gk = keep_out.cpu().long()
+    k1, v1, cl1 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    okeep, onew = window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1,
+                                      sel, 256, wb, kb, ke)
+    assert cl.cpu().tolist() == cl1.tolist() == [L - 1024 + keep_tokens for L in lens]
+    window = window_importance(pb.q, pb.k_cache, pb.block_tables, pb.context_lens, sel, 256, wb)
+    for i in range(len(sel)):
+        assert gk[i, 0] == 0 and gk[i, -1] == wb * 256 - 1 and torch.all(gk[i].diff() > 0)
+        if torch.equal(gk[i], okeep[i]):
+            continue
+        cut = torch.sort(window[i].float(), descending=True).values[num_keep - 1].item()
+        ok, why = tie_band_ok(window[i], gk[i, 1:1 + num_keep], okeep[i, 1:1 + num_keep], num_keep,
+                              band=_bf16_ulp(cut))
+        assert ok, f"seq {i}: {why}"
+    k2, v2, cl2 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    window_compress_ref(pb.q, k2, v2, pb.block_tables, pb.context_lens.clone(), cl2, sel, 256, wb,
+                        kb, ke, keep_idx_override=gk)
+    assert torch.equal(kd.cpu().view(torch.int16), k2.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v2.view(torch.int16))
+
+
 def test_window_compaction_maximal_overlap(cuda_lib):
     """The compaction's read-all-then-write hazard, made maximal: keep 1,021
     of the window's 1,022 candidate keys (keep_tokens 1,023) and make key 1
