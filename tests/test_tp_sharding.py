@@ -138,3 +138,46 @@ def test_dead_rank_is_detected_not_waited_for():
     assert res[0] == "detected", res
     assert res[1] < 60, res  # well inside the group's timeout plus set-up slack
     assert procs[1].exitcode == 3
+
+
+def _oproj_rank_main(rank, world, port, repo, out_q):
+    import sys
+    sys.path[:0] = [repo, os.path.join(repo, "nanokv-llm_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nanokv_b200.layers.linear import RowParallelOProj
+
+        g = torch.Generator().manual_seed(40)
+        x_full = torch.randn(8, 64, generator=g)
+        w_full = torch.randn(32, 64, generator=g)
+        k = 64 // world  # the rank's shard of the input dim (RowParallelLinear)
+        layer = RowParallelOProj(w_full[:, rank * k:(rank + 1) * k].contiguous())
+        assert layer.fused is None  # opt-in only
+        y = layer(x_full[:, rank * k:(rank + 1) * k].contiguous())
+        if rank == 0:
+            out_q.put((y, x_full @ w_full.T))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_row_parallel_oproj_default_path_two_ranks():
+    """RowParallelOProj without fusion is the reference's RowParallelLinear
+    forward (nanokvllm/layers/linear.py:151-155): each rank's F.linear of its
+    input shard, then dist.all_reduce -- two gloo ranks on the CPU give the
+    unsharded product."""
+    world = 2
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_oproj_rank_main, args=(r, world, port, repo, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    y, ref = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert torch.allclose(y, ref, atol=1e-4, rtol=1e-5)
