@@ -33,6 +33,7 @@ is a plain indexed copy.
 from __future__ import annotations
 
 import json
+import os
 import sys
 import types
 from collections import deque
@@ -420,7 +421,11 @@ def gen_step(ref):
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NANOKV_REFERENCE")
+    if not arg:
+        raise SystemExit(f"usage: python {Path(__file__).name} /path/to/nanokv-llm checkout "
+                         "(or set NANOKV_REFERENCE)")
+    ref = Path(arg).resolve()
     sys.path.insert(0, str(ref))
     torch.set_num_threads(8)
     gen_snapkv(ref)

@@ -28,7 +28,11 @@ from oracle.inputs import digest  # noqa: E402
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NANOKV_REFERENCE")
+    if not arg:
+        raise SystemExit(f"usage: python {Path(__file__).name} /path/to/nanokv-llm checkout "
+                         "(or set NANOKV_REFERENCE)")
+    ref = Path(arg).resolve()
     sys.path.insert(0, str(ref))
     from nanokvllm.layers.layernorm import RMSNorm
     from nanokvllm.layers.rotary_embedding import RotaryEmbedding
