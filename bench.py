@@ -292,16 +292,22 @@ def run_gpu(args, rank, world, dev):
         e2e_body(False)
     torch.cuda.synchronize(dev)
     e2e_graph = torch.cuda.CUDAGraph()
-    e2e_mode = "cuda_graph"
+    e2e_mode, e2e_capture_error = "cuda_graph", None
     try:
         with torch.cuda.graph(e2e_graph):
             e2e_body(True)
         torch.cuda.synchronize(dev)
-    except Exception as exc:  # noqa: BLE001 -- capture refused: the same step, eagerly
+    except RuntimeError as exc:  # capture refused: the same step, eagerly
         print(f"e2e graph capture failed ({exc}); timing the eager step", file=sys.stderr)
         reset_context()
-        e2e_graph, e2e_mode = None, "eager"
+        e2e_graph, e2e_mode, e2e_capture_error = None, "eager", str(exc)[:300]
+        # a real CUDA failure (not a refused capture) is sticky: synchronize
+        # raises it here, and the kernels' own error word must be clean
         torch.cuda.synchronize(dev)
+        from nanokv_b200 import _lib
+        bits = _lib.read_device_error(clear=False)
+        if bits:
+            raise RuntimeError(f"device error word {bits:#x} after the e2e capture attempt") from exc
 
     def e2e_step():
         if e2e_graph is not None:
@@ -353,7 +359,8 @@ def run_gpu(args, rank, world, dev):
             "ms_per_step": round(ref_gpu, 4), "tok_per_s": round(BATCH * 1000.0 / ref_gpu, 1),
             "ours_speedup": round(ref_gpu / ms * args.steps, 3)}
     return dict(ms=ms, e2e_ms=e2e_ms, dec_avg_ms=dec_avg, alg_bytes=alg, clocks=clk,
-                resident=R, h2d=h2d, d2h=d2h, compress=comp, extra=extra, e2e_mode=e2e_mode)
+                resident=R, h2d=h2d, d2h=d2h, compress=comp, extra=extra, e2e_mode=e2e_mode,
+                e2e_capture_error=e2e_capture_error)
 
 
 def reference_gpu_step_ms(args, dev, st, qkv, layer_views, kv, R, bt, cl, sm, scale, hq, hk,
@@ -794,11 +801,49 @@ def measure_oproj(dev, world):
         del graph  # graphs holding NCCL calls go before the process group does
         return a.elapsed_time(b) / (n * reps) * 1e3
 
+    def parity(o):
+        # one fused call against the reference's F.linear + dist.all_reduce
+        # on the same inputs (nanokvllm/layers/linear.py:151-155): the error
+        # bound is one bf16 ulp of the result plus one of each rank's bf16
+        # partial (the reference rounds each partial to bf16; our fp32
+        # accumulation order differs from cuBLAS's) plus fp32 order slack.
+        # Every rank takes part (collectives), and the ranks agree on the
+        # worst ratio.
+        from nanokv_b200.layers.linear import OProjAllReduceError
+        yf = torch.full((T, N), float("nan"), dtype=torch.bfloat16, device=dev)
+        status = None
+        try:
+            o(x, w, out=yf)
+            o.check()
+        except OProjAllReduceError as e:
+            status = str(e)
+        ref = F.linear(x, w).float()
+        torch.distributed.all_reduce(ref)
+        mag = F.linear(x, w).float().abs()
+        torch.distributed.all_reduce(mag)
+        err = (yf.float() - ref).abs()
+        err = torch.where(torch.isnan(err), torch.full_like(err, float("inf")), err)
+        bound = 2.0 ** -7 * ref.abs() + 2.0 ** -7 * mag + 1e-4
+        worst = torch.stack([err.max(), (err / bound).max()])
+        torch.distributed.all_reduce(worst, op=torch.distributed.ReduceOp.MAX)
+        tn, splits = o.tiling()
+        res = {"max_abs_err": float(worst[0]), "max_err_over_bound": round(float(worst[1]), 4),
+               "ok": bool(worst[1] <= 1.0) and status is None, "tiling": {"TN": tn, "S": splits},
+               "bound": "2^-7 |sum| + 2^-7 sum|partial| + 1e-4, max over ranks"}
+        if status is not None:
+            res["status"] = status
+        return res
+
     mode = "one-shot" if op.one_shot else "two-shot"
     other = "two-shot" if op.one_shot else "one-shot"
     alt_made = alt is not None
-    t_f = timed(fused)
-    t_a = timed(fused_alt) if alt_made else None
+    par = parity(op)
+    par_alt = parity(alt) if alt_made else None
+    # a mode whose parity call failed (NaN output, a wait that gave up) is
+    # reported, not timed; the ranks agree on it through the all-reduced ratio
+    t_f = timed(fused) if math.isfinite(par["max_err_over_bound"]) else None
+    t_a = (timed(fused_alt) if alt_made and math.isfinite(par_alt["max_err_over_bound"])
+           else None)
     t_r = timed(reference)
     # every rank releases the symmetric (multicast-bound) buffers together
     torch.cuda.synchronize(dev)
@@ -809,7 +854,8 @@ def measure_oproj(dev, world):
     res = {"workload": f"o_proj + all-reduce, 256 tokens x hidden 4096, k {K} per rank, {world} ranks",
            "mode": mode, "fused_us": round(t_f, 1) if t_f is not None else None,
            f"fused_{other}_us": round(t_a, 1) if t_a is not None else None,
-           "cublas_nccl_us": round(t_r, 1) if t_r is not None else None}
+           "cublas_nccl_us": round(t_r, 1) if t_r is not None else None,
+           "parity": par, f"parity_{other}": par_alt}
     if t_f is None or (alt_made and t_a is None):
         res["error"] = "a mode flagged a device error (a bounded wait gave up); not timed"
     if t_f is not None and t_r is not None:
@@ -1072,6 +1118,7 @@ def main():
             "config": config_dict(world, r["resident"]),
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"], "mode": r["e2e_mode"],
+                    **({"capture_error": r["e2e_capture_error"]} if r["e2e_capture_error"] else {}),
                     "path": "nanokv_b200.layers.attention.Attention.forward per layer, the step "
                             "captured in a CUDA graph (as ModelRunner captures decode) and "
                             "replayed (mode 'eager' if the capture was refused); every step "

@@ -232,10 +232,15 @@ int nkv_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_token, int32_t nu
 /* barrier it copies the result to y. sig_mc / sig_local: a symmetric       */
 /* uint32[2] of arrival counters (every CTA of every rank adds one per       */
 /* barrier); flags: this rank's uint32[5] (the two barriers' counter         */
-/* targets, two unused words, the call's epoch); counters and flags zeroed  */
-/* once. Targets and epoch are read and advanced on the device, so every    */
-/* rank must make the same sequence of calls and a CUDA graph may replay     */
-/* them. Waits are bounded by timeout_ns (then NKV_DEVERR_WAIT_TIMEOUT).     */
+/* targets, the tiling of the last launch as (TN << 8) | S, the status word, */
+/* the call's epoch); counters and flags zeroed once. Targets and epoch are  */
+/* read and advanced on the device, so every rank must make the same        */
+/* sequence of calls and a CUDA graph may replay them. Waits are bounded by  */
+/* timeout_ns. A wait that gives up sets NKV_DEVERR_WAIT_TIMEOUT and ORs     */
+/* into the status word which one (1 TMA ring, 2 MMA stage, 4 accumulator,   */
+/* 8 cross-rank barrier); the data it guarded becomes NaN (a failed GEMM     */
+/* sends NaN partials, a failed barrier leaves NaN in y), the targets are    */
+/* not advanced, and the group must rebuild its buffers before calling again.*/
 /* Needs k % 64 == 0,                                                       */
 /* n % 32 == 0, 16-byte aligned x, w, y and buffers, row strides multiples  */
 /* of 8. Cooperative launch of (n / TN) * S CTAs, TN in {32, 64, 128}        */
@@ -288,7 +293,9 @@ int nkv_oproj_allreduce_p2p(const void* x, int64_t ldx, const void* w, int64_t l
 /*   them, and context_lens[b] = L0 - window_blocks*block_size + keep_tokens. */
 /* out_keep_idx (optional, [num_selected, keep_tokens]) receives the window-  */
 /* relative kept indices; out_new_lens (optional, [num_selected]) the new     */
-/* lengths. Needs num_kv_heads <= 8 (one thread-block cluster per sequence). */
+/* lengths; out_importance (optional, bf16 [num_selected, window_tokens -     */
+/* obs_window]) the importance the top-k ranked (SnapKV's key_importance).    */
+/* Needs num_kv_heads <= 8 (one thread-block cluster per sequence).          */
 /* Entries of selected_batch_indices equal to -1 are skipped.                */
 /* The caller guarantees what the reference asserts (full_blocks >=          */
 /* window_blocks); rows violating it are skipped and flag                    */
@@ -301,7 +308,8 @@ int nkv_window_compress(const void* q, int64_t q_stride_token,
                         int32_t window_blocks, int32_t keep_tokens, int32_t obs_window,
                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                         int32_t block_size, float softmax_scale,
-                        int32_t* out_keep_idx, int32_t* out_new_lens, void* stream);
+                        int32_t* out_keep_idx, int32_t* out_new_lens, void* out_importance,
+                        void* stream);
 
 /* 3a'. Device-side selection of the rows a periodic compression step takes */
 /* (the reference's host loop in prepare_decode, nanokvllm/engine/          */
@@ -345,7 +353,8 @@ int nkv_query_window_append(const void* q, int64_t q_stride_token,
 /* ring queries of ring slot ring_slot_of_selected[i] (all heads, all W      */
 /* queries); SnapKV keeps token 0, the top R-W-1 and the last W; kept rows   */
 /* are compacted to positions [0, R) of the sequence's block table and       */
-/* context_lens[b] = R. out_keep_idx is optional ([num_selected, R]).        */
+/* context_lens[b] = R. out_keep_idx is optional ([num_selected, R]), and so */
+/* is out_importance (bf16 [num_selected, S - W]: the importance ranked).    */
 int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num_layers,
                            int32_t window_size, int32_t layer_id,
                            const int32_t* ring_slot_of_selected,
@@ -356,7 +365,7 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
                            int32_t compress_S, int32_t compress_R,
                            int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                            int32_t block_size, float softmax_scale,
-                           int32_t* out_keep_idx, void* stream);
+                           int32_t* out_keep_idx, void* out_importance, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 4. Paged decode without a caller-provided workspace                       */

@@ -275,7 +275,7 @@ const char* nkv_status_string(int status) {
   }
 }
 
-int nkv_abi_version(void) { return 100; }
+int nkv_abi_version(void) { return 101; }
 
 int nkv_last_cuda_error(void) { return t_last_cuda_error; }
 
@@ -841,7 +841,7 @@ int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, vo
                         int32_t window_blocks, int32_t keep_tokens, int32_t obs_window,
                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                         int32_t block_size, float softmax_scale, int32_t* out_keep_idx,
-                        int32_t* out_new_lens, void* stream) {
+                        int32_t* out_new_lens, void* out_importance, void* stream) {
   if (num_selected < 0) return NKV_ERR_INVALID_ARGUMENT;
   if (num_selected == 0) return NKV_OK;
   if (!q || !k_cache || !v_cache || !block_tables || !base_context_lens || !context_lens ||
@@ -873,6 +873,7 @@ int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, vo
   p.selected = selected_batch_indices;
   p.out_keep_idx = out_keep_idx;
   p.out_new_lens = out_new_lens;
+  p.out_importance = static_cast<uint16_t*>(out_importance);
   p.scale = softmax_scale;
   p.max_blocks = max_blocks;
   p.window_blocks = window_blocks;
@@ -947,7 +948,7 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
                            int32_t num_selected, int32_t compress_S, int32_t compress_R,
                            int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                            int32_t block_size, float softmax_scale, int32_t* out_keep_idx,
-                           void* stream) {
+                           void* out_importance, void* stream) {
   if (num_selected < 0) return NKV_ERR_INVALID_ARGUMENT;
   if (num_selected == 0) return NKV_OK;
   if (!ring || !ring_slot_of_selected || !k_cache || !v_cache || !block_tables || !context_lens ||
@@ -971,6 +972,7 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
   p.context_lens = context_lens;
   p.selected = selected_batch_indices;
   p.out_keep_idx = out_keep_idx;
+  p.out_importance = static_cast<uint16_t*>(out_importance);
   p.scale = softmax_scale;
   p.num_ring_slots = num_ring_slots;
   p.num_layers = num_layers;

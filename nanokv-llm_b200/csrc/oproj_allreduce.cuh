@@ -35,12 +35,19 @@
 // A barrier: every CTA fences its stores (fence.acq_rel.sys) and adds one
 // to every rank's arrival counter (one multimem.red through the switch, or
 // a red per rank), then waits until its own rank's counter reaches this
-// call's target (ld.acquire.sys, bounded by %globaltimer; on timeout it
-// flags NKV_DEVERR_WAIT_TIMEOUT and goes on). Counters only grow; the
-// targets and the call's epoch (its parity) live in device memory and are
-// advanced by CTA 0 once every CTA has read them, so a CUDA graph can replay
-// the launch. The launch is cooperative (all CTAs resident: each waits on
-// all the others).
+// call's target (ld.acquire.sys, bounded by %globaltimer). Counters only
+// grow; the targets and the call's epoch (its parity) live in device memory
+// and are advanced by CTA 0 once every CTA has read them, so a CUDA graph can
+// replay the launch. The launch is cooperative (all CTAs resident: each
+// waits on all the others).
+// A wait that gives up never yields a plausible wrong result: the CTA records
+// which wait failed in the call's status word (flags[3], sticky, plus
+// NKV_DEVERR_WAIT_TIMEOUT in the device error word) and its share of the
+// data becomes NaN -- a failed GEMM sends NaN partials (so every rank's sum
+// of that tile is NaN), a failed rank barrier writes NaN to the CTA's rows of
+// y instead of summing slots that may be incomplete -- and CTA 0 does not
+// advance the targets after a barrier it did not pass. CTA 0 also records
+// the tiling that ran in flags[2] ((TN << 8) | S).
 #pragma once
 #include "nkv_common.cuh"
 #include "tcgen05.cuh"
@@ -72,7 +79,7 @@ struct OprojParams {
   int64_t slot_stride;               // elements per (parity, source rank) slot, >= T * N
   uint32_t* sig_local;    // this rank's [2] arrival counters
   float* splitk_ws;       // S > 1: fp32 partial tiles, [S][N / TN][TN / 4][mtiles * 128][4]
-  unsigned int* flags;    // this rank's [target 1, target 2, -, -, epoch]
+  unsigned int* flags;    // this rank's [target 1, target 2, tiling, status, epoch]
   __nv_bfloat16* y;
   int64_t ldy;
   int T, K, N;
@@ -132,10 +139,13 @@ __device__ __forceinline__ uint4 pack8_bf16(const float (&a)[8]) {
 // Cross-rank barrier `which` (0 or 1) with this call's counter target:
 // every CTA arrives at every rank's counter after fencing its own stores (a
 // release pattern at system scope), then waits for its rank's counter to
-// reach the target (an acquire). Bounded by p.timeout_ns.
-__device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, uint32_t target) {
+// reach the target (an acquire). Bounded by p.timeout_ns; returns false, to
+// every thread of the CTA, if the wait gave up (`passed` is a shared word).
+__device__ __forceinline__ bool rank_barrier(const OprojParams& p, int which, uint32_t target,
+                                             volatile uint32_t* passed) {
   __syncthreads();
   if (threadIdx.x == 0) {
+    uint32_t ok = 1u;
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     if (p.one_shot) {
       for (int r = 0; r < p.world; ++r)
@@ -148,14 +158,30 @@ __device__ __forceinline__ void rank_barrier(const OprojParams& p, int which, ui
     const uint64_t t0 = global_ns();
     while (static_cast<int32_t>(ld_acquire_sys(p.sig_local + which) - target) < 0) {
       if (global_ns() - t0 > p.timeout_ns) {
-        raise_error(NKV_DEVERR_WAIT_TIMEOUT);
+        ok = 0u;
         break;
       }
       __nanosleep(32);
     }
+    *passed = ok;
   }
   __syncthreads();
+  return *passed != 0u;
 }
+
+// Status bits of one call (flags[3]): which bounded wait gave up.
+constexpr uint32_t kOpStatusRing = 1u;     // producer: a ring slot never freed
+constexpr uint32_t kOpStatusMma = 2u;      // MMA issuer: a stage's TMA never landed
+constexpr uint32_t kOpStatusAcc = 4u;      // epilogue: the accumulator never completed
+constexpr uint32_t kOpStatusBarrier = 8u;  // a cross-rank barrier's counter never reached its target
+
+// Records a failed wait: the call's sticky status word and the device error word.
+__device__ __forceinline__ void op_fail(const OprojParams& p, uint32_t bit) {
+  atomicOr(p.flags + 3, bit);
+  raise_error(NKV_DEVERR_WAIT_TIMEOUT);
+}
+
+constexpr uint32_t kBf16NanPair = 0x7FC07FC0u;  // two bf16 quiet NaNs
 
 // Sends rows [row, row + nrows) of this CTA's bf16 block -- rows
 // [r0, r0 + ...) of tile `tile`, row-major in shared memory at `block` -- to
@@ -206,6 +232,9 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   uint64_t* empty = bars + kOpMaxStages;   // [stages]
   uint64_t* acc_full = bars + 2 * kOpMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kOpMaxStages + 1);
+  // status bits of this CTA's GEMM waits, and the last barrier's outcome
+  volatile uint32_t* cta_status = tmem_slot + 1;
+  volatile uint32_t* barrier_passed = tmem_slot + 2;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -234,6 +263,8 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     }
     mbar_init(smem_u32(acc_full), 1);
     fence_barrier_init();
+    *cta_status = 0u;
+    if (blockIdx.x == 0) p.flags[2] = (static_cast<uint32_t>(p.tn) << 8) | static_cast<uint32_t>(S);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), cols);
@@ -255,7 +286,10 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
       for (int ks = 0; ks < ksteps; ++ks) {
         const int s = ks % stages;
         const uint32_t ph = (ks / stages) & 1;
-        if (!mbar_wait_bounded(smem_u32(&empty[s]), ph ^ 1u)) break;
+        if (!mbar_wait_bounded(smem_u32(&empty[s]), ph ^ 1u)) {
+          atomicOr(const_cast<uint32_t*>(cta_status), kOpStatusRing);
+          break;
+        }
         armed &= ~(1u << s);
         const uint32_t fb = smem_u32(&full[s]);
         mbar_arrive_expect_tx(fb, stage_bytes);
@@ -277,6 +311,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
       const int s = ks % stages;
       if (!mbar_wait_bounded(smem_u32(&full[s]), (ks / stages) & 1)) {
         ok = false;
+        if (lane == 0) atomicOr(const_cast<uint32_t*>(cta_status), kOpStatusMma);
         break;
       }
       tc_fence_after();
@@ -302,6 +337,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     // acc_full: every MMA has completed, so every TMA load has landed and
     // the ring is free for staging
     acc_ok = mbar_wait_bounded(smem_u32(acc_full), 0);
+    if (!acc_ok && lane == 0) atomicOr(const_cast<uint32_t*>(cta_status), kOpStatusAcc);
   }
 
   // ---------------------------------------------------------------- epilogue
@@ -351,6 +387,26 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, cols);
+  }
+  // A GEMM wait gave up: the accumulator is incomplete, so this CTA's
+  // partial becomes NaN (its workspace tile, or with S = 1 its bf16 block)
+  // and every rank's sum of the tile is NaN rather than a plausible value.
+  const uint32_t gemm_status = *cta_status;
+  if (gemm_status != 0u) {
+    if (threadIdx.x == 0) op_fail(p, gemm_status);
+    if (S > 1) {
+      float4* ws4 = reinterpret_cast<float4*>(p.splitk_ws + split * ws_tiles +
+                                              static_cast<int64_t>(tile) * tp * p.tn);
+      const float nan = __uint_as_float(0x7FC00000u);
+      for (int i = threadIdx.x; i < tp * p.tn / 4; i += kOpThreads)
+        __stcg(ws4 + i, make_float4(nan, nan, nan, nan));
+    } else {
+      uint4* b4 = reinterpret_cast<uint4*>(block);
+      for (int i = threadIdx.x; i < p.T * p.tn / 8; i += kOpThreads)
+        b4[i] = make_uint4(kBf16NanPair, kBf16NanPair, kBf16NanPair, kBf16NanPair);
+      fence_proxy_async_shared();
+    }
+    __syncthreads();
   }
 
   int r0 = 0, nrows = p.T;
@@ -422,7 +478,18 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   const int per_row = p.tn / 8;
   if (p.one_shot) {
     // ------------------------------------------------------------ barrier
-    rank_barrier(p, 0, target0);
+    const bool passed = rank_barrier(p, 0, target0, barrier_passed);
+    if (!passed) {
+      // a rank's partials may be missing: this CTA's rows of y become NaN
+      if (threadIdx.x == 0) op_fail(p, kOpStatusBarrier);
+      const uint4 nan8 = make_uint4(kBf16NanPair, kBf16NanPair, kBf16NanPair, kBf16NanPair);
+      for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
+        const int r = i / per_row;
+        *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(r) * p.ldy + n0 +
+                                  (i - r * per_row) * 8) = nan8;
+      }
+      return;
+    }
     if (blockIdx.x == 0 && threadIdx.x == 0) {  // every CTA read them before arriving
       p.flags[0] = target0;
       p.flags[4] = epoch;
@@ -482,7 +549,10 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 
   // ---------------------------------------------------------------- barrier 1
-  rank_barrier(p, 0, target0);
+  // (on a timeout this CTA's share of the switch reduction broadcasts NaN,
+  // so no rank reads a sum of partials that may be incomplete)
+  const bool passed1 = rank_barrier(p, 0, target0, barrier_passed);
+  if (!passed1 && threadIdx.x == 0) op_fail(p, kOpStatusBarrier);
 
   // ------------------------------------------------- reduce this rank's slice
   // 16-byte groups [lo, hi) of the T x N result: fp32 sum of every rank's
@@ -498,12 +568,15 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
 #pragma unroll
       for (int u = 0; u < kOpReduceUnroll; ++u) {
         const int64_t i = i0 + u * stride;
-        if (i < hi)
+        if (i < hi && passed1) {
           asm volatile(
               "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
               : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3])
               : "l"(p.part_mc + 8 * i)
               : "memory");
+        } else {
+          v[u][0] = v[u][1] = v[u][2] = v[u][3] = kBf16NanPair;
+        }
       }
 #pragma unroll
       for (int u = 0; u < kOpReduceUnroll; ++u) {
@@ -519,8 +592,19 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 
   // ---------------------------------------------------------------- barrier 2
-  rank_barrier(p, 1, target1);
-  if (blockIdx.x == 0 && threadIdx.x == 0) {  // every CTA read them before arriving
+  const bool passed2 = rank_barrier(p, 1, target1, barrier_passed);
+  if (!passed2) {
+    // the gathered result may be incomplete: this CTA's rows of y become NaN
+    if (threadIdx.x == 0) op_fail(p, kOpStatusBarrier);
+    const uint4 nan8 = make_uint4(kBf16NanPair, kBf16NanPair, kBf16NanPair, kBf16NanPair);
+    for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
+      const int r = i / per_row;
+      *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(r) * p.ldy + n0 +
+                                (i - r * per_row) * 8) = nan8;
+    }
+    return;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && passed1) {  // every CTA read them before arriving
     p.flags[0] = target0;
     p.flags[1] = target1;
     p.flags[4] = epoch;

@@ -68,6 +68,7 @@ struct ThresholdCompressParams {
   int32_t* context_lens;
   const int32_t* selected;
   int32_t* out_keep_idx;
+  uint16_t* out_importance;  // bf16 bits [num_selected][num_keys], or null
   float scale;
   int num_ring_slots;
   int num_layers;
@@ -293,6 +294,8 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
       float s = 0.f;
       for (int c = 0; c < nranks; ++c) s += cluster.map_shared_rank(partial, c)[t];
       keys[t] = (t < nk) ? static_cast<uint16_t>(bf16_key(s)) : 0;
+      if (head == 0 && p.out_importance != nullptr && t < nk)
+        p.out_importance[static_cast<int64_t>(sel_i) * nk + t] = keys[t];
     }
   }
   cluster.sync();

@@ -41,6 +41,7 @@ struct WindowCompressParams {
   const int32_t* selected;
   int32_t* out_keep_idx;
   int32_t* out_new_lens;
+  uint16_t* out_importance;  // bf16 bits [num_selected][num_keys], or null
   float scale;
   int max_blocks;
   int window_blocks;
@@ -214,6 +215,8 @@ window_compress_kernel(const WindowCompressParams p) {
       float s = 0.f;
       for (int c = 0; c < nranks; ++c) s += cluster.map_shared_rank(partial, c)[t];
       keys[t] = (t < nk) ? static_cast<uint16_t>(bf16_key(s)) : 0;
+      if (head == 0 && p.out_importance != nullptr && t < nk)
+        p.out_importance[static_cast<int64_t>(sel_i) * nk + t] = keys[t];
     }
   }
   cluster.sync();  // no CTA may leave while a peer still reads its partials

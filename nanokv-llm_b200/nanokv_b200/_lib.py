@@ -87,7 +87,7 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, c_int64, _P, _P, c_int64, _I32P, c_int32, _I32P, _I32P, _I32P, c_int32,
          c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float,
-         _I32P, _I32P, _P],
+         _I32P, _I32P, _P, _P],
     ),
     "nkv_window_select": (
         c_int,
@@ -107,7 +107,7 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, c_int32, c_int32, c_int32, c_int32, _I32P, _P, _P, c_int64, _I32P, c_int32,
          _I32P, _I32P, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
-         c_float, _I32P, _P],
+         c_float, _I32P, _P, _P],
     ),
 }
 

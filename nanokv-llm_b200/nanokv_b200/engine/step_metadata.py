@@ -50,7 +50,8 @@ class StepMetadata:
 
     @classmethod
     def build(cls, scheduled, block_size: int) -> "StepMetadata":
-        """`scheduled`: ScheduledSeq-like items (`.seq`, `.num_new_tokens`)."""
+        """`scheduled`: items with `.seq` (a request: token_ids, num_computed_tokens,
+        block_table) and `.num_new_tokens`."""
         n = len(scheduled)
         seqs = [s.seq for s in scheduled]
         news = np.fromiter((s.num_new_tokens for s in scheduled), dtype=np.int64, count=n)

@@ -3,12 +3,13 @@
 The reference's RowParallelLinear.forward (nanokvllm/layers/linear.py:151-155)
 runs F.linear on the rank's weight shard and then dist.all_reduce of the
 bf16 result (NCCL). OProjAllReduce does both in ONE kernel per rank
-(nkv_oproj_allreduce): a split-K tcgen05 GEMM (a cluster of CTAs per output
-tile, summed through distributed shared memory) writing bf16 partials -- the
-reference's F.linear output type -- to a symmetric buffer, an in-kernel
-cross-rank barrier, each rank's slice summed in fp32 through NVLink SHARP
-(multimem.ld_reduce) and broadcast as bf16 (multimem.st), a second barrier,
-and the copy to the output.
+(nkv_oproj_allreduce_p2p / nkv_oproj_allreduce): a split-K tcgen05 GEMM (a
+cluster of CTAs per output tile, their fp32 partial tiles summed through an
+L2-resident workspace) whose bf16 partials -- the reference's F.linear output
+type -- go either into every rank's receive buffer (one-shot: one in-kernel
+barrier, then a local fp32 sum in rank order) or to a symmetric buffer summed
+in fp32 through NVLink SHARP (two-shot: multimem.ld_reduce, multimem.st, two
+barriers).
 It serves decode-sized steps (tokens <= 512); RowParallelOProj falls back to
 the reference's own two calls for larger (prefill) steps or groups without
 NVLink multicast.
@@ -24,6 +25,29 @@ from .. import _lib, ops
 
 MAX_FUSED_TOKENS = 512
 
+# Bits of a call's status word (flags[3] of the kernel, sticky): which
+# bounded wait gave up. The kernel turns the affected data into NaN instead of
+# returning a plausible wrong sum.
+OPROJ_STATUS_BITS = {
+    1: "TMA ring slot never freed",
+    2: "a stage's TMA load never landed",
+    4: "accumulator never completed",
+    8: "cross-rank barrier timed out",
+}
+
+
+def oproj_status_text(status: int) -> str:
+    return ", ".join(t for b, t in OPROJ_STATUS_BITS.items() if status & b) or "ok"
+
+
+def oproj_tiling(word: int) -> tuple[int, int]:
+    """(TN output columns per tile, S CTAs per tile) from flags[2]."""
+    return int(word) >> 8, int(word) & 0xFF
+
+
+class OProjAllReduceError(RuntimeError):
+    """A fused o_proj call whose bounded waits gave up (its output holds NaN)."""
+
 
 class OProjAllReduce:
     """Fused y = all_reduce(x @ w_shard^T) for one process group.
@@ -38,6 +62,15 @@ class OProjAllReduce:
     at most four ranks (measured faster there: 23.5 vs 34.5 us at 2 ranks,
     30.8 vs 33.6 us at 4, config 2's decode shape) and whenever the group
     has no multicast.
+
+    Failure: a bounded wait that gives up (a rank that never arrives within
+    timeout_s, or a TMA / MMA stage that never completes) sets the call's
+    status word and turns the affected output into NaN. Outside CUDA-graph
+    capture every call queues a 8-byte copy of (tiling, status) to pinned host
+    memory; the next call (without waiting) or check() (waiting) raises
+    OProjAllReduceError once it sees a nonzero status, and the object then
+    refuses further calls: the ranks' counters no longer agree, so the group
+    must build a new one.
 
     Collective construction (every rank of `group` constructs it, in the same
     order): allocates a symmetric buffer (one-shot: [2 parities][world]
@@ -90,7 +123,11 @@ class OProjAllReduce:
         else:
             self.mc_base = mc + offset
             self._part_off, self._out_off = 0, 2 * E
-        self.flags = torch.zeros(5, dtype=torch.int32, device=self.device)  # ctr/go x2, epoch
+        # [barrier 1 target, barrier 2 target, tiling, status, epoch]
+        self.flags = torch.zeros(5, dtype=torch.int32, device=self.device)
+        self._status_host = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+        self._status_event = None
+        self.failed = 0
         # split-K partial tiles: up to 4 K ranges x max_tokens (rounded up to
         # 128-row tiles) x hidden fp32, L2-resident at decode sizes
         self.workspace = torch.empty(4 * ((max_tokens + 127) // 128 * 128) * hidden,
@@ -99,7 +136,56 @@ class OProjAllReduce:
         torch.cuda.synchronize(self.device)
         dist.barrier(group)
 
+    def _poll(self, wait: bool) -> None:
+        ev = self._status_event
+        if ev is None:
+            return
+        if wait:
+            ev.synchronize()
+        elif not ev.query():
+            return
+        self._status_event = None
+        st = int(self._status_host[1])
+        if st:
+            self.failed = st
+            raise OProjAllReduceError(
+                f"rank {self.rank}: fused o_proj + all-reduce failed ({oproj_status_text(st)}); "
+                "its output is NaN and this object must be rebuilt")
+
+    def check(self) -> None:
+        """Raises OProjAllReduceError if any call so far gave up a wait
+        (synchronises with the last call, and reads the device status word
+        itself, so it also covers calls replayed from a CUDA graph)."""
+        if self.failed:
+            raise OProjAllReduceError(f"rank {self.rank}: an earlier call failed "
+                                      f"({oproj_status_text(self.failed)})")
+        self._poll(wait=True)
+        st = int(self.flags[3].item())
+        if st:
+            self.failed = st
+            raise OProjAllReduceError(
+                f"rank {self.rank}: fused o_proj + all-reduce failed ({oproj_status_text(st)})")
+
+    def tiling(self) -> tuple[int, int]:
+        """(TN, S) of the last call's launch (synchronises)."""
+        return oproj_tiling(int(self.flags[2].item()))
+
     def __call__(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None):
+        if self.failed:
+            raise OProjAllReduceError(f"rank {self.rank}: an earlier call failed "
+                                      f"({oproj_status_text(self.failed)}); rebuild the object")
+        capturing = torch.cuda.is_current_stream_capturing()
+        if not capturing:
+            self._poll(wait=False)
+        out = self._launch(x, w, out)
+        if not capturing:
+            self._status_host.copy_(self.flags[2:4], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(x.device))
+            self._status_event = ev
+        return out
+
+    def _launch(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None):
         T, K = x.shape
         N = w.shape[0]
         assert N == self.hidden and T <= self.max_tokens and w.shape[1] == K

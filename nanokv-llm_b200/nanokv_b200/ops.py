@@ -365,11 +365,14 @@ def window_compress(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     context_lens: torch.Tensor, selected: torch.Tensor, window_blocks: int,
                     keep_tokens: int, obs_window: int = 1, softmax_scale: float | None = None,
                     out_keep_idx: torch.Tensor | None = None,
-                    out_new_lens: torch.Tensor | None = None) -> None:
+                    out_new_lens: torch.Tensor | None = None,
+                    out_importance: torch.Tensor | None = None) -> None:
     """Periodic window compression of one layer (SnapKV scoring + compaction).
 
     `selected` is an int32 device tensor of batch indices; context_lens is
     updated in place. softmax_scale defaults to SnapKV's 1/sqrt(head_dim).
+    out_importance (bf16 [m, window_blocks * block_size - obs_window]), if
+    given, receives the importance SnapKV ranked.
     """
     _require_cuda("window_compress", q, k_cache, v_cache, block_tables, base_context_lens,
                   context_lens, selected)
@@ -384,13 +387,16 @@ def window_compress(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     assert base_context_lens.dtype == torch.int32 and context_lens.dtype == torch.int32
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(D)
+    if out_importance is not None:
+        assert out_importance.dtype == torch.bfloat16 and out_importance.is_contiguous()
+        assert out_importance.shape == (m, window_blocks * block_size - obs_window)
     lib = _lib.load()
     _lib.check("nkv_window_compress", lib.nkv_window_compress(
         q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), num_blocks,
         block_tables.data_ptr(), block_tables.size(1), base_context_lens.data_ptr(),
         context_lens.data_ptr(), selected.data_ptr(), m, window_blocks, keep_tokens, obs_window,
         Hq, Hk, D, block_size, float(softmax_scale), _ptr(out_keep_idx), _ptr(out_new_lens),
-        _stream(q.device)))
+        _ptr(out_importance), _stream(q.device)))
 
 
 # ---------------------------------------------------------------- KvChat threshold path
@@ -416,8 +422,11 @@ def threshold_compress(ring: torch.Tensor, ring_slot_of_selected: torch.Tensor, 
                        k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                        context_lens: torch.Tensor, selected: torch.Tensor, S: int, R: int,
                        softmax_scale: float | None = None,
-                       out_keep_idx: torch.Tensor | None = None) -> None:
-    """KvChat threshold compression S -> R of one layer; context_lens[sel] = R."""
+                       out_keep_idx: torch.Tensor | None = None,
+                       out_importance: torch.Tensor | None = None) -> None:
+    """KvChat threshold compression S -> R of one layer; context_lens[sel] = R.
+    out_importance (bf16 [m, S - W]), if given, receives the importance
+    SnapKV ranked."""
     _require_cuda("threshold_compress", ring, ring_slot_of_selected, k_cache, v_cache,
                   block_tables, context_lens, selected)
     m = selected.numel()
@@ -428,9 +437,13 @@ def threshold_compress(ring: torch.Tensor, ring_slot_of_selected: torch.Tensor, 
     assert Dk == D and ring.is_contiguous() and block_tables.is_contiguous()
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(D)
+    if out_importance is not None:
+        assert out_importance.dtype == torch.bfloat16 and out_importance.is_contiguous()
+        assert out_importance.shape == (m, S - W)
     lib = _lib.load()
     _lib.check("nkv_threshold_compress", lib.nkv_threshold_compress(
         ring.data_ptr(), slots, layers, W, layer_id, ring_slot_of_selected.data_ptr(),
         k_cache.data_ptr(), v_cache.data_ptr(), num_blocks, block_tables.data_ptr(),
         block_tables.size(1), context_lens.data_ptr(), selected.data_ptr(), m, S, R, Hq, Hk, D,
-        block_size, float(softmax_scale), _ptr(out_keep_idx), _stream(k_cache.device)))
+        block_size, float(softmax_scale), _ptr(out_keep_idx), _ptr(out_importance),
+        _stream(k_cache.device)))

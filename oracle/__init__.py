@@ -15,6 +15,10 @@ reference computes on the path that libnkv replaces:
                                       :218-252) and its query window
                                       (KvChat/engine/query_window_manager.py)
   * unified-step metadata            (nanokvllm/engine/model_runner.py:154-219)
+  * request state and block manager  (nanokvllm/engine/sequence.py,
+                                      nanokvllm/engine/block_manager.py): the
+                                      stand-ins the host tests drive the
+                                      product's event appliers with
 
 It is the checker, never the product: only tests/, __graft_entry__.smoke()
 and bench.py's CPU-baseline leg import it. The product (nanokv_b200) never

@@ -18,22 +18,39 @@ from __future__ import annotations
 import torch
 
 
-def snapkv_importance(Q: torch.Tensor, K: torch.Tensor, window: int) -> torch.Tensor:
+def snapkv_importance(Q: torch.Tensor, K: torch.Tensor, window: int,
+                      exact_scores: bool = False) -> torch.Tensor:
     """key_importance [B, L - window] (bf16) exactly as CompressMethod.py:19-42.
 
     Q: [B, Hq, window, D]; K: [B, Hk, L, D] (bf16).
+
+    exact_scores: the bf16 q.k products are rounded once from their exact
+    value (an fp64 product rounded to fp32, then to bf16) instead of from
+    torch's CPU bf16 matmul, whose fp32 accumulation order is the CPU
+    library's and can land on the other side of a bf16 rounding boundary
+    (38 of the 654,720 scores of a 20-sequence Qwen3-8B event, changing one
+    importance value by one bf16 ulp). Every later step is the
+    reference's. This is the platform-independent definition libnkv's
+    window kernel implements; with exact_scores=False the function is the
+    reference's own computation on this CPU.
     """
     B, Hk, L, D = K.shape
     Hq = Q.size(1)
     K_cut = K[:, :, :-window, :]
     scale = 1.0 / (D ** 0.5)
+
+    def mm(a, b):
+        if exact_scores:
+            return torch.matmul(a.double(), b.double()).float().to(torch.bfloat16)
+        return torch.matmul(a, b)
+
     if Hq == Hk:
-        scores = torch.matmul(Q, K_cut.transpose(-1, -2)) * scale
+        scores = mm(Q, K_cut.transpose(-1, -2)) * scale
     else:
         g = Hq // Hk
         Qg = Q.view(B, Hk, g, window, D)
         Kt = K_cut.transpose(-1, -2).unsqueeze(2)
-        scores = (torch.matmul(Qg, Kt) * scale).view(B, Hq, window, L - window)
+        scores = (mm(Qg, Kt) * scale).view(B, Hq, window, L - window)
     scores[:, :, :, 0] = -float("inf")
     probs = torch.softmax(scores, dim=-1)
     imp = probs.sum(dim=2)
@@ -53,14 +70,15 @@ def topk_low_index(values: torch.Tensor, k: int) -> torch.Tensor:
     return torch.sort(kept, dim=-1).values
 
 
-def snapkv_keep(Q: torch.Tensor, K: torch.Tensor, num_keep: int, window: int):
+def snapkv_keep(Q: torch.Tensor, K: torch.Tensor, num_keep: int, window: int,
+                exact_scores: bool = False):
     """final_idx [B, 1 + num_keep + window] = cat(0, kept ascending, last
     `window` positions), or False when the reference skips
     (CompressMethod.py:17-18). Also returns the importance."""
     B, Hk, L, D = K.shape
     if L - window <= 0 or L <= num_keep + window:
         return False, None
-    imp = snapkv_importance(Q, K, window)
+    imp = snapkv_importance(Q, K, window, exact_scores)
     kept = topk_low_index(imp, num_keep)
     tail = torch.arange(L - window, L).unsqueeze(0).expand(B, -1)
     bos = torch.zeros((B, 1), dtype=torch.long)

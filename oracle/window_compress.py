@@ -34,12 +34,14 @@ def window_compress_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
                         block_tables: torch.Tensor, base_lens: torch.Tensor,
                         context_lens: torch.Tensor, seq_idxs: list[int], block_size: int,
                         window_blocks: int, keep_blocks: int, keep_extra_tokens: int,
-                        keep_idx_override: torch.Tensor | None = None):
+                        keep_idx_override: torch.Tensor | None = None,
+                        exact_scores: bool = False):
     """One layer of MyCompressCompact on CPU tensors, in place.
 
     Returns (keep_idx [m, keep_tokens] window-relative, new_lens [m]) or
     False where the reference returns False. `keep_idx_override` replaces the
-    SnapKV selection (to check the compaction alone on a given kept set).
+    SnapKV selection (to check the compaction alone on a given kept set);
+    `exact_scores` as in oracle.snapkv.snapkv_importance.
     """
     if not seq_idxs:
         return False
@@ -52,7 +54,8 @@ def window_compress_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
     kf = k_cache.view(-1, Hk, D)
     k_sub = kf[slots].permute(0, 2, 1, 3).contiguous()
     if keep_idx_override is None:
-        keep_idx, _ = snapkv_keep(q_sub, k_sub, num_keep=keep_tokens - 2, window=1)
+        keep_idx, _ = snapkv_keep(q_sub, k_sub, num_keep=keep_tokens - 2, window=1,
+                                  exact_scores=exact_scores)
         if keep_idx is False:
             return False
     else:
@@ -101,11 +104,30 @@ def compression_events(block_tables: torch.Tensor, seq_idxs: list[int], new_lens
 
 def window_importance(q: torch.Tensor, k_cache: torch.Tensor, block_tables: torch.Tensor,
                       base_lens: torch.Tensor, seq_idxs: list[int], block_size: int,
-                      window_blocks: int) -> torch.Tensor:
+                      window_blocks: int, exact_scores: bool = False) -> torch.Tensor:
     """The bf16 SnapKV importance [m, window_tokens - 1] that MyCompressCompact
-    ranks for each selected sequence (used for tie bands in parity checks)."""
+    ranks for each selected sequence."""
     from .snapkv import snapkv_importance
     slots, _, _, _ = tail_window(block_tables, base_lens, seq_idxs, block_size, window_blocks)
     _, _, Hk, D = k_cache.shape
     k_sub = k_cache.view(-1, Hk, D)[slots].permute(0, 2, 1, 3).contiguous()
-    return snapkv_importance(q[seq_idxs].unsqueeze(2), k_sub, 1)
+    return snapkv_importance(q[seq_idxs].unsqueeze(2), k_sub, 1, exact_scores)
+
+
+def window_score_rounding_keys(q: torch.Tensor, k_cache: torch.Tensor, block_tables: torch.Tensor,
+                               base_lens: torch.Tensor, seq_idxs: list[int], block_size: int,
+                               window_blocks: int) -> torch.Tensor:
+    """[m, window_tokens - 1] bool: keys where, for some q head, the CPU bf16
+    matmul's score differs from the exactly rounded score -- the only keys
+    at which the reference's importance on this CPU and the exact-score
+    importance may differ."""
+    slots, _, _, _ = tail_window(block_tables, base_lens, seq_idxs, block_size, window_blocks)
+    _, _, Hk, D = k_cache.shape
+    K = k_cache.view(-1, Hk, D)[slots].permute(0, 2, 1, 3)[:, :, :-1]   # [m, Hk, n, D]
+    Q = q[seq_idxs]                                                     # [m, Hq, D]
+    g = Q.size(1) // Hk
+    Qg = Q.view(len(seq_idxs), Hk, g, 1, D)
+    Kt = K.transpose(-1, -2).unsqueeze(2)
+    cpu = torch.matmul(Qg, Kt)
+    exact = torch.matmul(Qg.double(), Kt.double()).float().to(torch.bfloat16)
+    return (cpu.view(torch.int16) != exact.view(torch.int16)).flatten(1, 3).any(1)

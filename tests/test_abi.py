@@ -25,7 +25,7 @@ def test_library_builds_and_exports_every_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in nkv.h but not exported"
     assert set(declared) == set(_lib.SIGNATURES), "ctypes bindings out of sync with nkv.h"
-    assert lib.nkv_abi_version() == 100
+    assert lib.nkv_abi_version() == 101
     assert lib.nkv_status_string(3) == b"NKV_ERR_WORKSPACE"
 
 
@@ -56,7 +56,7 @@ def test_argument_errors_need_no_gpu():
     assert lib.nkv_store_kvcache(16, 1024, 16, 1024, 16, 16, 100, 16, 0, 8, 128, None) == 0
     # obs_window other than 1 is not the reference's periodic path
     assert lib.nkv_window_compress(16, 4096, 16, 16, 10, 16, 8, 16, 16, 16, 1, 4, 513, 2, 32, 8,
-                                   128, 256, 0.1, None, None, None) == 2
+                                   128, 256, 0.1, None, None, None, None) == 2
 
 
 def test_prefill_argument_errors_need_no_gpu():

@@ -5,9 +5,11 @@ nanokvllm/layers/linear.py:151-155) waits at an in-kernel barrier for every
 rank's arrivals. Here one GPU calls it declaring TWO ranks, and the second
 rank's arrival counter is a word that nothing reads, so this rank's counter
 never reaches its target: every wait must give up after its limit (1 ms),
-raise NKV_DEVERR_WAIT_TIMEOUT and let the kernel finish -- no hang, no trap
--- and the context must stay usable (a following single-rank call gives the
-right result). All pointers are this GPU's own memory.
+raise NKV_DEVERR_WAIT_TIMEOUT, record the barrier bit in the call's status
+word, write NaN (not a plausible partial sum) to y, leave the call's counter
+targets and epoch where they were, and let the kernel finish -- no hang, no
+trap -- and the context must stay usable (a following single-rank call gives
+the right result). All pointers are this GPU's own memory.
 """
 
 import pytest
@@ -56,9 +58,13 @@ def test_oproj_barrier_wait_gives_up_with_status(cuda_lib):
     # this rank arrived once per CTA at both counters; the target needed twice
     arrivals = int(sig[0].item())
     assert arrivals > 0 and int(absent[0].item()) == arrivals
-    # the kernel still finished its sum (rank 1's slot is zero): y is this
-    # rank's own partial, rounded to bf16
-    assert (y.float() - ref).abs().max().item() <= 2.0 ** -7 * ref.abs().max().item() + 1e-3
+    # the barrier never passed: y is NaN everywhere, the status word names
+    # the barrier, and the targets / epoch were not advanced
+    from nanokv_b200.layers.linear import oproj_status_text
+    assert bool(torch.isnan(y.float()).all())
+    status = int(flags[3].item())
+    assert status == 8, oproj_status_text(status)
+    assert int(flags[0].item()) == 0 and int(flags[4].item()) == 0
 
     # the context is usable: a single-rank call completes without error
     sig1 = torch.zeros(4, dtype=torch.int32, device=DEV)
@@ -70,6 +76,6 @@ def test_oproj_barrier_wait_gives_up_with_status(cuda_lib):
                  torch.tensor([sig1.data_ptr()], dtype=torch.int64, device=DEV), sig1, flags1,
                  ws, 1, 1_000_000_000) == 0
     torch.cuda.synchronize()
-    assert _lib.read_device_error(clear=True) == 0
+    assert _lib.read_device_error(clear=True) == 0 and int(flags1[3].item()) == 0
     err = (y1.float() - ref).abs()
     assert bool((err <= 2.0 ** -7 * ref.abs() + 2.0 ** -7 * ref.abs() + 1e-3).all())

@@ -116,7 +116,7 @@ def test_kvchat_attention_threshold_cycle(cuda_lib):
     """KvChat: W decode steps append queries, the last one compresses S -> R."""
     from nanokv_b200.engine.compress_schedule import prepare_threshold_context
     from nanokv_b200.engine.query_window import QueryWindowManager
-    from nanokv_b200.engine.sequence import Sequence
+    from oracle.host_state import SeqState as Sequence
     from nanokv_b200.layers.kvchat import Attention
     from nanokv_b200.utils.context import get_context, reset_context, set_kvchat_context
 

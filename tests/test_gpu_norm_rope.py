@@ -186,7 +186,7 @@ def test_kvchat_forward_qkv_decode_step_with_query_window(cuda_lib):
     store, the reference's QueryWindowManager.append, decode)."""
     from nanokv_b200.engine.compress_schedule import prepare_threshold_context
     from nanokv_b200.engine.query_window import QueryWindowManager
-    from nanokv_b200.engine.sequence import Sequence
+    from oracle.host_state import SeqState as Sequence
     from nanokv_b200.layers.kvchat import Attention as KvChatAttention
     from nanokv_b200.utils.context import get_context, reset_context, set_kvchat_context
 

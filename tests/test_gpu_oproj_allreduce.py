@@ -50,6 +50,10 @@ def _worker(rank, world, port, hidden, k_local, one_shot):
             x = torch.randn(T, k_local, device=dev, generator=g).to(torch.bfloat16)
             w = (torch.randn(hidden, k_local, device=dev, generator=g) * 0.05).to(torch.bfloat16)
             y = op(x, w)
+            try:
+                op.check()  # the call's status word: no bounded wait gave up
+            except RuntimeError as e:
+                errors.append(f"rank {rank} call {call}: {e}")
             part = F.linear(x.float(), w.float())
             ref = part.clone()
             dist.all_reduce(ref)

@@ -1,8 +1,12 @@
 """Host-side compression metadata vs traces recorded from the reference
 (tests/golden/host_metadata.json, made by tests/golden/make_golden.py):
-BlockManager + Scheduler.postprocess event application, the periodic
-selection of ModelRunner.prepare_decode, and KvChat's
-prepare_compression_context. CPU only."""
+Scheduler.postprocess event application (the product's apply_window_events
+/ apply_threshold_events driving a block manager's truncate_blocks), the
+periodic selection of ModelRunner.prepare_decode, and KvChat's
+prepare_compression_context. The requests and the block manager are the
+oracle's models (oracle/host_state.py), which the same traces pin to the
+reference's Sequence and BlockManager; in deployment the product drives the
+reference's own objects. CPU only."""
 
 import json
 import types
@@ -11,13 +15,12 @@ from itertools import count
 import numpy as np
 import pytest
 
-from nanokv_b200.engine.block_manager import BlockManager
 from nanokv_b200.engine.compress_schedule import (DecodeMetadata, PeriodicCompressScheduler,
                                                   apply_threshold_events, apply_window_events,
                                                   prepare_threshold_context)
 from nanokv_b200.engine.query_window import QueryWindowManager
-from nanokv_b200.engine.sequence import Sequence
 from nanokv_b200.utils.context import Context
+from oracle.host_state import BlockPool, Scheduled, SeqState
 
 
 @pytest.fixture(scope="module")
@@ -32,8 +35,7 @@ def _seq_state(s):
 
 
 def _bm_state(bm):
-    return {"free": list(bm.free_block_ids), "used": sorted(bm.used_block_ids),
-            "ref": [b.ref_count for b in bm.blocks], "hash_set": [b.hash != -1 for b in bm.blocks]}
+    return bm.state()
 
 
 def _replay_block_manager(trace, check: bool):
@@ -45,9 +47,9 @@ def _replay_block_manager(trace, check: bool):
                rng.integers(0, 50000, 1100).tolist(),
                rng.integers(0, 50000, 255).tolist()]
     assert prompts == tr["prompts"]
-    Sequence.counter = count()
-    bm = BlockManager(num_blocks=40, block_size=256)
-    seqs = [Sequence(p, max_tokens=10**6, ignore_eos=True) for p in prompts]
+    SeqState.counter = count()
+    bm = BlockPool(num_blocks=40, block_size=256)
+    seqs = [SeqState(p, max_tokens=10**6, ignore_eos=True) for p in prompts]
     for s in seqs:
         bm.allocate(s)
         s.num_computed_tokens = s.num_prompt_tokens
@@ -103,7 +105,7 @@ def test_block_manager_release_and_prefix_reuse(trace):
     bm.deallocate(seqs[1])
     rec = next(rel)
     assert [_seq_state(s) for s in seqs] == rec["seqs"] and _bm_state(bm) == rec["bm"]
-    new = Sequence(trace["block_manager_release"]["new_prompt"], max_tokens=10**6, ignore_eos=True)
+    new = SeqState(trace["block_manager_release"]["new_prompt"], max_tokens=10**6, ignore_eos=True)
     assert bm.can_allocate(new) == next(rel)["value"]
     bm.allocate(new)
     rec = next(rel)
@@ -117,10 +119,10 @@ def test_block_manager_release_and_prefix_reuse(trace):
 
 def test_periodic_selection_matches_prepare_decode(trace):
     tr = trace["periodic_selection"]
-    Sequence.counter = count()
+    SeqState.counter = count()
     seqs = []
     for L, t in zip(tr["lens"], tr["tails"]):
-        s = Sequence(list(range(L)))
+        s = SeqState(list(range(L)))
         s.block_table = list(range(100, 100 + (L + 255) // 256))
         s.tail_uncompressed_len = t
         s.rope_pos = L + 17
@@ -146,8 +148,8 @@ def test_periodic_selection_matches_prepare_decode(trace):
 def test_periodic_fill_context_host_companions():
     import torch
 
-    Sequence.counter = count()
-    seqs = [Sequence(list(range(L))) for L in (1500, 900, 2000)]
+    SeqState.counter = count()
+    seqs = [SeqState(list(range(L))) for L in (1500, 900, 2000)]
     for s, t in zip(seqs, (1024, 2000, 1100)):
         s.block_table = list(range(len(s.block_table), len(s.block_table) + s.num_blocks))
         s.tail_uncompressed_len = t
@@ -167,8 +169,8 @@ def test_kvchat_context_decisions(trace):
     tr = trace["kvchat_context"]
     cfg = types.SimpleNamespace(kv_compress_S=511, kv_compress_R=257, query_window_size=50)
     qwm = QueryWindowManager(1, 50, 2, 128, device="cpu")
-    Sequence.counter = count()
-    seqs = [Sequence(list(range(p))) for p in tr["prompts"]]
+    SeqState.counter = count()
+    seqs = [SeqState(list(range(p))) for p in tr["prompts"]]
     for rec in tr["decisions"]:
         for s in seqs:
             s.num_tokens = s.num_prompt_tokens + rec["extra"]
@@ -182,14 +184,14 @@ def test_kvchat_context_decisions(trace):
 
 
 def test_threshold_events_truncate():
-    Sequence.counter = count()
-    bm = BlockManager(8, 256)
-    s = Sequence(list(range(767)))
+    SeqState.counter = count()
+    bm = BlockPool(8, 256)
+    s = SeqState(list(range(767)))
     bm.allocate(s)
     apply_threshold_events([s], [{"batch_index": 0, "layer": 27, "R": 513, "keep_blocks": 3,
                                   "freed_block_ids": []}], bm)
     assert s.num_tokens == 513 and len(s.block_table) == 3
-    assert list(bm.free_block_ids)[-1] == 3 or 3 in bm.free_block_ids
+    assert list(bm.free)[-1] == 3 or 3 in bm.free
 
 
 def test_device_select_host_half_matches_host_selection():
@@ -201,10 +203,10 @@ def test_device_select_host_half_matches_host_selection():
 
     from oracle.window_compress import compression_events
 
-    Sequence.counter = count()
+    SeqState.counter = count()
     lens = (1500, 900, 2000, 1279, 3000)
     tails = (1024, 2000, 1100, 1024, 5)
-    seqs = [Sequence(list(range(L))) for L in lens]
+    seqs = [SeqState(list(range(L))) for L in lens]
     nxt = 0
     for s, t in zip(seqs, tails):
         s.block_table = list(range(nxt, nxt + s.num_blocks))
@@ -242,20 +244,19 @@ def test_step_metadata_matches_prepare_step(golden_dir):
     (tests/golden/step_metadata.json): every array and the Context it sets."""
     import torch
 
-    from nanokv_b200.engine.sequence import ScheduledSeq
     from nanokv_b200.engine.step_metadata import StepMetadata
     from nanokv_b200.utils.context import get_context, reset_context
 
     tr = json.loads((golden_dir / "step_metadata.json").read_text())
     bs = tr["block_size"]
     for rec in tr["batches"]:
-        Sequence.counter = count()
+        SeqState.counter = count()
         sched = []
         for r in rec["seqs"]:
-            s = Sequence(r["token_ids"])
+            s = SeqState(r["token_ids"])
             s.num_computed_tokens = r["num_computed_tokens"]
             s.block_table = list(r["block_table"])
-            sched.append(ScheduledSeq(s, r["num_new_tokens"]))
+            sched.append(Scheduled(s, r["num_new_tokens"]))
         meta = StepMetadata.build(sched, bs)
         ids, pos, logits_idx = meta.set_context(rec["all_decode"], "cpu")
         c = get_context()
@@ -276,14 +277,13 @@ def test_step_metadata_matches_prepare_step(golden_dir):
 
 
 def test_step_metadata_rejects_token_past_block_table():
-    from nanokv_b200.engine.sequence import ScheduledSeq
     from nanokv_b200.engine.step_metadata import StepMetadata
 
-    Sequence.counter = count()
-    s = Sequence(list(range(300)))
+    SeqState.counter = count()
+    s = SeqState(list(range(300)))
     s.block_table = [7]  # 300 tokens need two 256-token blocks
     with pytest.raises(IndexError):
-        StepMetadata.build([ScheduledSeq(s, 300)], 256)
+        StepMetadata.build([Scheduled(s, 300)], 256)
 
 
 def test_step_metadata_oracle_pinned_and_random_batches(golden_dir):
@@ -291,19 +291,18 @@ def test_step_metadata_oracle_pinned_and_random_batches(golden_dir):
     reference's own outputs (golden), and StepMetadata equals it on 200
     random mixed batches (prefill chunks of 1..2,100 tokens, decode rows,
     ragged block tables, 64- and 256-token blocks)."""
-    from nanokv_b200.engine.sequence import ScheduledSeq
     from nanokv_b200.engine.step_metadata import StepMetadata
     from oracle.step_metadata import prepare_step_ref
 
     tr = json.loads((golden_dir / "step_metadata.json").read_text())
     for rec in tr["batches"]:
-        Sequence.counter = count()
+        SeqState.counter = count()
         sched = []
         for r in rec["seqs"]:
-            s = Sequence(r["token_ids"])
+            s = SeqState(r["token_ids"])
             s.num_computed_tokens = r["num_computed_tokens"]
             s.block_table = list(r["block_table"])
-            sched.append(ScheduledSeq(s, r["num_new_tokens"]))
+            sched.append(Scheduled(s, r["num_new_tokens"]))
         ref = prepare_step_ref(sched, tr["block_size"])
         for key in ("input_ids", "positions", "slot_mapping", "logits_indices", "block_tables",
                     "max_seqlen_q", "max_seqlen_k"):
@@ -317,19 +316,19 @@ def test_step_metadata_oracle_pinned_and_random_batches(golden_dir):
     rng = np.random.default_rng(23)
     for trial in range(200):
         bs = int(rng.choice([64, 256]))
-        Sequence.counter = count()
+        SeqState.counter = count()
         sched, next_block = [], 0
         for _ in range(int(rng.integers(1, 12))):
             total = int(rng.integers(1, 6000))
             computed = int(rng.integers(0, total))
             new = 1 if rng.random() < 0.5 else int(rng.integers(1, min(2100, total - computed) + 1))
             new = min(new, total - computed)
-            s = Sequence(rng.integers(0, 1000, total).tolist())
+            s = SeqState(rng.integers(0, 1000, total).tolist())
             s.num_computed_tokens = computed
             nb = (computed + new + bs - 1) // bs + int(rng.integers(0, 3))  # spare blocks too
             s.block_table = (rng.permutation(nb) + next_block).tolist()
             next_block += nb
-            sched.append(ScheduledSeq(s, new))
+            sched.append(Scheduled(s, new))
         ref = prepare_step_ref(sched, bs)
         m = StepMetadata.build(sched, bs)
         assert m.input_ids.tolist() == ref["input_ids"], trial

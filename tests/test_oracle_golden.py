@@ -51,6 +51,36 @@ def test_snapkv_matches_reference(golden_dir, case):
         assert torch.all(ref_final[i, 1:1 + num_keep].diff() > 0)
 
 
+@pytest.mark.parametrize("case", SNAPKV_CASES + [("config3_event",)],
+                         ids=[c[0] for c in SNAPKV_CASES] + ["config3_event"])
+def test_exact_score_importance_differs_only_at_cpu_rounding_keys(golden_dir, case):
+    """The exact-score variant of the oracle (q.k rounded once from its exact
+    value, the definition libnkv's window kernel implements) against the
+    reference's computation on this CPU: on the golden cases it equals the
+    reference's importance bit for bit; on config 3's 20-sequence event the
+    two differ only at keys where torch's CPU bf16 matmul rounded some head's
+    score differently from the exact value."""
+    if case[0] == "config3_event":
+        from oracle.window_compress import window_importance, window_score_rounding_keys
+        lens = np.random.default_rng(33).integers(1100, 4397, 20).tolist()
+        pb = make_paged_batch(seed=34, lens=lens, Hq=32, Hk=8, outlier_sigma=4.0,
+                              outlier_frac=0.05)
+        args = (pb.q, pb.k_cache, pb.block_tables, pb.context_lens, list(range(20)), 256, 4)
+        exact = window_importance(*args, exact_scores=True)
+        cpu = window_importance(*args)
+        keys = window_score_rounding_keys(*args)
+        differ = exact.view(torch.int16) != cpu.view(torch.int16)
+        assert not bool((differ & ~keys).any())
+        assert int(keys.sum()) <= 5e-3 * keys.numel()  # 38 of 20,460 keys here
+        return
+    name, seed, m, Hq, Hk, L, window, num_keep, outlier = case
+    g = _npz(golden_dir, "snapkv.npz")
+    Q, K = snapkv_inputs(seed, m, Hq, Hk, L, window, outlier)
+    exact = snapkv_importance(Q, K, window, exact_scores=True)
+    ref_imp = torch.from_numpy(g[f"{name}/importance_bits"]).view(torch.bfloat16)
+    assert torch.equal(exact.view(torch.int16), ref_imp.view(torch.int16))
+
+
 @pytest.mark.parametrize("case", WINDOW_CASES, ids=[c[0] for c in WINDOW_CASES])
 def test_window_compress_matches_reference(golden_dir, case):
     name, kw, selected, wb, kb, ke = case

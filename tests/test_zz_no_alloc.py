@@ -6,7 +6,8 @@ is sealed after start-up, and plugin hosts that pass a kernel its inputs and
 outputs but no scratch buffer. nkv_paged_decode_static_scratch serves them
 with a fixed scratch array inside the library. This file checks, through the
 C ABI, that two calls in a row give what the workspace-taking
-nkv_paged_decode gives (same tolerance as the other decode tests), and that a
+nkv_paged_decode gives and what the CPU oracle of flash_attn_with_kvcache
+gives (the decode tests' tolerances: max-abs 2e-2, relative 1e-2), and that a
 problem too large for the array is refused before anything is launched.
 Pytest collects this file last, so a failure here leaves every other test
 already run.
@@ -15,12 +16,14 @@ already run.
 import pytest
 import torch
 
+from oracle.attention import paged_decode_ref
 from oracle.inputs import make_paged_batch
 
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
 ATOL = 2e-2
+RTOL = 1e-2
 
 
 def _static_call(lib, q, kc, vc, bt, cl, out, Hq, Hk, scale):
@@ -42,12 +45,16 @@ def test_static_scratch_decode_matches_workspace_decode(cuda_lib):
     need = lib.nkv_paged_decode_workspace_size(q.shape[0], Hq, Hk, 128, bt.size(1), kc.shape[1])
     assert 0 < need <= _lib.STATIC_SCRATCH_BYTES
     expected = ops.paged_decode(q, kc, vc, bt, cl, scale).float()
+    ref = paged_decode_ref(pb.q, pb.k_cache, pb.v_cache, pb.block_tables, pb.context_lens, scale)
     for _ in range(2):  # the second call sees the first call's leftover scratch
         out = torch.full((q.shape[0], Hq, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
         assert _static_call(lib, q, kc, vc, bt, cl, out, Hq, Hk, scale) == 0
         torch.cuda.synchronize()
         assert torch.isfinite(out.float()).all()
         assert (out.float() - expected).abs().max().item() <= ATOL
+        got = out.float().cpu()
+        assert (got - ref).abs().max().item() <= ATOL
+        assert ((got - ref).norm() / ref.norm()).item() <= RTOL
     assert _lib.read_device_error(clear=True) == 0
 
 
