@@ -47,7 +47,8 @@
 // of that tile is NaN), a failed rank barrier writes NaN to the CTA's rows of
 // y instead of summing slots that may be incomplete -- and CTA 0 does not
 // advance the targets after a barrier it did not pass. CTA 0 also records
-// the tiling that ran in flags[2] ((TN << 8) | S).
+// the tiling that ran in flags[2] ((TN << 8) | S, plus bit 16 when the launch
+// lacked its clusters and each tile ran unsplit).
 #pragma once
 #include "nkv_common.cuh"
 #include "tcgen05.cuh"
@@ -125,11 +126,14 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
+__device__ __forceinline__ uint32_t cluster_nctarank() {
   uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
   return r;
 }
+
+// flags[2] bit: the launch lacked its clusters and ran unsplit (see below).
+constexpr uint32_t kOpTilingUnclustered = 1u << 16;
 
 __device__ __forceinline__ uint4 pack8_bf16(const float (&a)[8]) {
   return make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
@@ -238,12 +242,21 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int S = p.splits;
-  const int split = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-  const int tile = blockIdx.x / S;
+  // A tile's p.splits CTAs are consecutive in x (one cluster). If the launch
+  // did not get its clusters (a tool that relaunches the kernel may drop the
+  // attribute: %cluster_nctarank is then 1), the CTAs cannot synchronise to
+  // sum K ranges, so every CTA computes its tile over the whole K (S = 1)
+  // and only the tile's first CTA sends it: the result is the same, only
+  // slower. `nct` CTAs share a tile; S is the number of K ranges.
+  const int nct = p.splits;
+  const bool clustered = nct == 1 || static_cast<int>(cluster_nctarank()) == nct;
+  const int S = clustered ? nct : 1;
+  const int split = static_cast<int>(blockIdx.x) % nct;
+  const bool publisher = S > 1 || split == 0;  // sends (part of) the tile
+  const int tile = blockIdx.x / nct;
   const int n0 = tile * p.tn;
   const int kper = p.K / S;
-  const int k0 = split * kper;
+  const int k0 = S > 1 ? split * kper : 0;
   // The call's epoch and counter targets live on the device (so the launch
   // can be replayed from a CUDA graph): every CTA reads them here, before
   // its first arrival; CTA 0 advances them after the call's last barrier.
@@ -264,7 +277,9 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     mbar_init(smem_u32(acc_full), 1);
     fence_barrier_init();
     *cta_status = 0u;
-    if (blockIdx.x == 0) p.flags[2] = (static_cast<uint32_t>(p.tn) << 8) | static_cast<uint32_t>(S);
+    if (blockIdx.x == 0)
+      p.flags[2] = (static_cast<uint32_t>(p.tn) << 8) | static_cast<uint32_t>(S) |
+                   (clustered ? 0u : kOpTilingUnclustered);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), cols);
@@ -470,7 +485,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
       __syncthreads();
       if (threadIdx.x == 0) send_rows(p, smem_u32(block), tile, r0, row0, crows, parity);
     }
-  } else if (threadIdx.x == 0 && nrows > 0) {
+  } else if (publisher && threadIdx.x == 0 && nrows > 0) {
     send_rows(p, smem_u32(block), tile, 0, 0, nrows, parity);
   }
   if (threadIdx.x == 0) send_wait();
@@ -483,7 +498,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
       // a rank's partials may be missing: this CTA's rows of y become NaN
       if (threadIdx.x == 0) op_fail(p, kOpStatusBarrier);
       const uint4 nan8 = make_uint4(kBf16NanPair, kBf16NanPair, kBf16NanPair, kBf16NanPair);
-      for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
+      for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += nct * kOpThreads) {
         const int r = i / per_row;
         *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(r) * p.ldy + n0 +
                                   (i - r * per_row) * 8) = nan8;
@@ -503,7 +518,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
                                 static_cast<int64_t>(parity) * p.world * p.slot_stride +
                                 static_cast<int64_t>(tile) * p.T * p.tn;
     const int items = p.T * per_row;
-    const int step = S * kOpThreads;
+    const int step = nct * kOpThreads;
     for (int i0 = split * kOpThreads + threadIdx.x; i0 < items; i0 += kOpSumBatch * step) {
       int64_t off[kOpSumBatch];
 #pragma unroll
@@ -597,7 +612,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
     // the gathered result may be incomplete: this CTA's rows of y become NaN
     if (threadIdx.x == 0) op_fail(p, kOpStatusBarrier);
     const uint4 nan8 = make_uint4(kBf16NanPair, kBf16NanPair, kBf16NanPair, kBf16NanPair);
-    for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
+    for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += nct * kOpThreads) {
       const int r = i / per_row;
       *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(r) * p.ldy + n0 +
                                 (i - r * per_row) * 8) = nan8;
@@ -612,7 +627,7 @@ oproj_allreduce_kernel(const __grid_constant__ CUtensorMap tm_x,
 
   // ---------------------------------------------------------------- copy out
   // the tile's columns of the gathered bf16 result -> y, shared by its S CTAs
-  for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += S * kOpThreads) {
+  for (int i = split * kOpThreads + threadIdx.x; i < p.T * per_row; i += nct * kOpThreads) {
     const int r = i / per_row;
     const int c = n0 + (i - r * per_row) * 8;
     const uint4 v = __ldcg(reinterpret_cast<const uint4*>(

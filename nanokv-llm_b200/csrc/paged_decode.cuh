@@ -165,9 +165,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   }
   __syncthreads();
   // Launched with programmatic stream serialisation: everything above
-  // overlapped the previous kernel (typically the slot write of this layer);
-  // from here on its writes to the cache are visible.
+  // overlapped the previous kernel (typically the previous layer's decode);
+  // from here on its writes (cache rows, the reset workspace counters) are
+  // visible. The next kernel of the stream (the next layer's decode) may be
+  // scheduled from now on: its CTAs take free SMs, run their own set-up and
+  // wait at their grid_dependency_wait until this grid has finished, which
+  // hides a launch's latency and set-up in a chain of small decode launches.
   grid_dependency_wait();
+  allow_dependent_launch();
 
   const int Hk = p.num_kv_heads;
   const int g = p.g;

@@ -40,9 +40,13 @@ def oproj_status_text(status: int) -> str:
     return ", ".join(t for b, t in OPROJ_STATUS_BITS.items() if status & b) or "ok"
 
 
-def oproj_tiling(word: int) -> tuple[int, int]:
-    """(TN output columns per tile, S CTAs per tile) from flags[2]."""
-    return int(word) >> 8, int(word) & 0xFF
+def oproj_tiling(word: int) -> tuple[int, int, bool]:
+    """(TN output columns per tile, S K ranges per tile, clustered) from
+    flags[2]. clustered is False when the launch lacked its thread-block
+    clusters (a profiler that relaunches kernels can drop them) and every
+    tile therefore ran unsplit (S = 1): same result, slower."""
+    w = int(word)
+    return (w >> 8) & 0xFF, w & 0xFF, not (w >> 16) & 1
 
 
 class OProjAllReduceError(RuntimeError):
@@ -166,8 +170,8 @@ class OProjAllReduce:
             raise OProjAllReduceError(
                 f"rank {self.rank}: fused o_proj + all-reduce failed ({oproj_status_text(st)})")
 
-    def tiling(self) -> tuple[int, int]:
-        """(TN, S) of the last call's launch (synchronises)."""
+    def tiling(self) -> tuple[int, int, bool]:
+        """(TN, S, clustered) of the last call's launch (synchronises)."""
         return oproj_tiling(int(self.flags[2].item()))
 
     def __call__(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None):

@@ -58,10 +58,10 @@ def _check(T, K, N, workspace=True, calls=3, expect_splits=None):
         torch.cuda.synchronize()
         dev_err = _lib.read_device_error(clear=True)
         status = int(op.flags[3].item())
-        tn, S = oproj_tiling(int(op.flags[2].item()))
-        where = f"T={T} K={K} N={N} call {call} tiling TN={tn} S={S}"
+        tn, S, clustered = oproj_tiling(int(op.flags[2].item()))
+        where = f"T={T} K={K} N={N} call {call} tiling TN={tn} S={S} clustered={clustered}"
         assert dev_err == 0 and status == 0, f"{where}: device error {dev_err}, status {status}"
-        assert tn in (32, 64, 128) and S in (1, 2, 4), where
+        assert tn in (32, 64, 128) and S in (1, 2, 4) and clustered, where
         if expect_splits is not None:
             assert S == expect_splits, where
         ref = F.linear(x.float(), w.float())
