@@ -340,7 +340,8 @@ def run_gpu(args, rank, world, dev):
     # every holder of a view of the KV (the last layer built above included)
     del kv, st, layers, a
     torch.cuda.empty_cache()
-    extra = {"config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world),
+    extra = {"config3_workload": measure_config3(dev, world),
+             "config5_kvchat": measure_kvchat(dev, world), "config4_decode": measure_config4(dev, world),
              "config4_prefill": measure_prefill(dev, world),
              "qk_norm_rope_store": measure_norm_rope(dev, world)}
     if world > 1:
@@ -562,6 +563,140 @@ def measure_compress(dev, hq, hk):
                 "host syncs), same inputs", "event_layer_us": round(t_ref * 1e3, 1),
         "ours_speedup": round(t_ref / t_layer_ms, 2)}
     return res
+
+
+def config3_trajectory():
+    """BASELINE config 3 on the host, under the reference's rules: 500
+    sequences with prompts U[50, 300] (seed 0) generate 4,096 tokens; every
+    1,024 global decode steps the FIRST 20 eligible sequences in batch order
+    (length % 256 != 255, >= 1,024 uncompressed tokens, >= 4 full blocks;
+    nanokvllm/engine/model_runner.py:305-324) compress their last 4 full
+    blocks to 2 * 256 + 1 tokens. Returns the lengths at the middle of each
+    1,024-step period and, per event, the selected rows and their base
+    lengths."""
+    rng = np.random.default_rng(0)
+    L = rng.integers(50, 301, 500).astype(np.int64)
+    tail = np.zeros(500, dtype=np.int64)
+    mids, events = [], []
+    for t in range(1, 4097):
+        L += 1
+        tail += 1
+        if t % 1024 == 512:
+            mids.append(L.copy())
+        if t % 1024 == 0:
+            elig = np.nonzero((L % BLOCK != BLOCK - 1) & (tail >= 4 * BLOCK) &
+                              (L // BLOCK >= 4))[0][:20]
+            events.append((elig.tolist(), L[elig].copy()))
+            L[elig] += 2 * BLOCK + 1 - 4 * BLOCK
+            tail[elig] = 0
+    return mids, events
+
+
+def measure_config3(dev, world):
+    """BASELINE config 3 as a workload: decode tok/s including the periodic
+    compression over the whole 4,096-step generation of 500 sequences
+    (Qwen3-8B attention shapes, 36 layers, kv heads / world per rank).
+    Decode steps (fused slot write + paged decode, 36 layers) are timed at
+    the middle of each of the four 1,024-step periods with that moment's
+    exact lengths (the step time is linear in the KV length, which grows
+    linearly within a period, so the midpoint gives the period's mean), and
+    each compression event (20 sequences x 36 layers) is timed with the
+    event's rows; total = sum over periods of 1,024 x the midpoint step +
+    the events. Four layer caches are resident and cycled (the full
+    36-layer cache of the last period, ~280 GB, does not fit one GPU); the
+    decode launches stream far more than L2, compression events start from
+    DRAM (L2 flushed)."""
+    from nanokv_b200 import ops
+
+    hq, hk = HQ // world, HK // world
+    R = 4
+    mids, events = config3_trajectory()
+    max_tokens = max(int(m.sum()) for m in mids) + 500 * BLOCK
+    nb_pool = max_tokens // BLOCK + 500
+    kv = torch.empty(2, R, nb_pool, BLOCK, hk, D, dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(30 + torch.distributed.get_rank()
+                                                  if world > 1 else 30)
+    kv.normal_(generator=gen)
+    gq = torch.Generator(device=dev).manual_seed(31)
+    qkv = torch.randn(500, (hq + 2 * hk) * D, device=dev, generator=gq).to(torch.bfloat16)
+    q, k, v = qkv.split([hq * D, hk * D, hk * D], dim=-1)
+    q, k, v = q.view(500, hq, D), k.view(500, hk, D), v.view(500, hk, D)
+    out = torch.empty(500, hq, D, dtype=torch.bfloat16, device=dev)
+    perm_gen = torch.Generator().manual_seed(32)
+
+    def tables_for(lens):
+        nbs = [(int(x) + BLOCK - 1) // BLOCK for x in lens]
+        perm = torch.randperm(nb_pool, generator=perm_gen).tolist()
+        mb = max(nbs)
+        rows, o = [], 0
+        for n in nbs:
+            rows.append(perm[o:o + n] + [-1] * (mb - n))
+            o += n
+        bt = torch.tensor(rows, dtype=torch.int32, device=dev)
+        last = [r[(int(x) - 1) // BLOCK] * BLOCK + (int(x) - 1) % BLOCK for r, x in zip(rows, lens)]
+        return bt, torch.tensor(last, dtype=torch.int32, device=dev), mb
+
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step_ms = []
+    for lens in mids:
+        bt, sm, mb = tables_for(lens)
+        cl = torch.tensor(lens.tolist(), dtype=torch.int32, device=dev)
+        ws = ops.decode_workspace(dev, 500, hq, hk, D, mb, BLOCK)
+
+        def step():
+            for layer in range(LAYERS):
+                c = layer % R
+                ops.decode_step(q, k, v, kv[0, c], kv[1, c], sm, bt, cl, D ** -0.5, out=out,
+                                workspace=ws)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        a.record()
+        for _ in range(3):
+            step()
+        b.record()
+        torch.cuda.synchronize(dev)
+        step_ms.append(a.elapsed_time(b) / 3)
+    event_ms = []
+    for rows, base in events:
+        full_lens = np.array([BLOCK * 8] * 500, dtype=np.int64)  # rows not selected: any length
+        full_lens[rows] = base
+        bt, _, _ = tables_for(full_lens)
+        base_t = torch.tensor(full_lens.tolist(), dtype=torch.int32, device=dev)
+        cl = base_t.clone()
+        sel = torch.tensor(rows, dtype=torch.int32, device=dev)
+        qs = q
+        times = []
+        for it in range(3):
+            cl.copy_(base_t)
+            _flush_l2(dev)
+            a.record()
+            for layer in range(LAYERS):
+                c = layer % R
+                ops.window_compress(qs, kv[0, c], kv[1, c], bt, base_t, cl, sel, 4, 2 * BLOCK + 1)
+            b.record()
+            torch.cuda.synchronize(dev)
+            if it:
+                times.append(a.elapsed_time(b))
+        event_ms.append(statistics.median(times))
+    vals = torch.tensor(step_ms + event_ms, dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    step_ms, event_ms = vals[:len(mids)].tolist(), vals[len(mids):].tolist()
+    total_s = (1024 * sum(step_ms) + sum(event_ms)) * 1e-3
+    del kv
+    return {"workload": "config3: Qwen3-8B attention shapes, 36 layers, 500 sequences, prompts "
+                        "U[50,300] seed 0, 4,096 generated tokens each; every 1,024 steps the first "
+                        "20 eligible sequences compress 4 blocks -> 513 tokens; decode steps timed "
+                        "at each period's midpoint (exact lengths), events timed with their rows; "
+                        f"{R} resident layer caches cycled",
+            "midpoint_step_ms": [round(x, 3) for x in step_ms],
+            "event_ms": [round(x, 3) for x in event_ms],
+            "compress_share": round(sum(event_ms) * 1e-3 / total_s, 5),
+            "total_s": round(total_s, 3), "tok_per_s": round(500 * 4096 / total_s, 1)}
 
 
 def measure_kvchat(dev, world, profile_replays: int = 0):

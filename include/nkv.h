@@ -55,6 +55,7 @@ typedef enum nkv_status {
 #define NKV_DEVERR_RING_RANGE      0x10u /* query-window ring slot / position out of range */
 #define NKV_DEVERR_PREFILL_RANGE   0x20u /* cu_seqlens / max_seqlen_q outside the tensors or the grid */
 #define NKV_DEVERR_ROPE_POSITION   0x40u /* position outside the rotary cos/sin cache (clamped) */
+#define NKV_DEVERR_LAUNCH_SHAPE    0x80u /* a kernel ran without the thread-block clusters it needs (nothing written) */
 
 /* Human-readable name of a status code (static string). */
 const char* nkv_status_string(int status);

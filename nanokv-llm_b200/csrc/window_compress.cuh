@@ -119,6 +119,14 @@ window_compress_kernel(const WindowCompressParams p) {
   __shared__ int s_valid;
   __shared__ int s_tail_block;
 
+  // The kv heads of a sequence are the CTAs of one cluster (their partial
+  // sums meet in distributed shared memory). A launch that lost its
+  // clusters (%cluster_nctarank 1) cannot form them: flag it and write
+  // nothing (the condition is uniform, so no CTA waits at a cluster barrier).
+  if (static_cast<int>(cluster.num_blocks()) != p.num_kv_heads) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) raise_error(NKV_DEVERR_LAUNCH_SHAPE);
+    return;
+  }
   const int b = __ldg(p.selected + sel_i);
   // -1: an unused entry of a fixed-size selection list (device-side
   // selection, graph replay); uniform across the cluster, before any

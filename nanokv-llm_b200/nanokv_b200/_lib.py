@@ -30,6 +30,7 @@ DEVERR_COMPRESS_RANGE = 0x8
 DEVERR_RING_RANGE = 0x10
 DEVERR_PREFILL_RANGE = 0x20
 DEVERR_ROPE_POSITION = 0x40
+DEVERR_LAUNCH_SHAPE = 0x80
 
 # Size of the library's fixed decode scratch (NKV_STATIC_SCRATCH_BYTES, nkv.h).
 STATIC_SCRATCH_BYTES = 16 << 20
