@@ -96,28 +96,82 @@ __device__ __forceinline__ uint32_t bf16_key(float v) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
 }
 
+// One warp finds, from a 256-bin histogram of keys (bin = one byte of the
+// key), the largest bin b whose suffix count (keys in bins >= b) reaches
+// `need`; returns b and the count of keys in bins above b. Lane l holds bins
+// [255 - 8l - 7, 255 - 8l] (lane 0 the highest), so an inclusive scan over
+// lanes is a scan from the top bin down.
+__device__ __forceinline__ void radix_pick_bin(const int* hist, int need, int* out_bin,
+                                               int* out_above) {
+  const int lane = threadIdx.x & 31;
+  int c[8];
+  int tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = hist[255 - 8 * lane - i];
+    tot += c[i];
+  }
+  int incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int excl = incl - tot;
+  if (excl < need && incl >= need) {  // exactly one lane holds the bin
+    int acc = excl;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (acc + c[i] >= need) {
+        *out_bin = 255 - 8 * lane - i;
+        *out_above = acc;
+        break;
+      }
+      acc += c[i];
+    }
+  }
+}
+
 // Selects the `k` largest of keys[0, n) (ties -> lower index) and writes their
-// indices, ascending, to out[0, k). Keys live in shared memory. Each thread
-// owns a contiguous index range so that scans follow index order.
-__device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int* red) {
+// indices, ascending, to out[0, k). Keys live in shared memory; `hist` is 256
+// ints of shared scratch, `red` kReduceSlots. The k-th largest key is found by
+// a two-pass radix select (high byte, then low byte among keys sharing the
+// high byte: two histogram passes instead of a 16-round bitwise search);
+// then each thread, owning a contiguous index range, emits its keys above
+// the cut and, in index order, the first (k - above) keys equal to it.
+__device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int* red, int* hist) {
+  __shared__ int s_bin, s_above;
+  if (k <= 0) {
+    __syncthreads();
+    return;
+  }
+  uint32_t prefix = 0;
+  int above = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int i = threadIdx.x; i < 256; i += kCompressThreads) hist[i] = 0;
+    __syncthreads();
+    for (int t = threadIdx.x; t < n; t += kCompressThreads) {
+      const uint32_t key = keys[t];
+      if (pass == 0) {
+        atomicAdd(&hist[key >> 8], 1);
+      } else if ((key >> 8) == (prefix >> 8)) {
+        atomicAdd(&hist[key & 0xFFu], 1);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) radix_pick_bin(hist, k - above, &s_bin, &s_above);
+    __syncthreads();
+    prefix |= static_cast<uint32_t>(s_bin) << (pass == 0 ? 8 : 0);
+    above += s_above;
+    __syncthreads();  // s_bin / s_above are rewritten by the next pass
+  }
+  // prefix is now the k-th largest key; `above` keys are larger.
   const int per = (n + kCompressThreads - 1) / kCompressThreads;
   const int lo = threadIdx.x * per;
   const int hi = min(lo + per, n);
-  uint32_t prefix = 0;
-  for (int bit = 15; bit >= 0; --bit) {
-    const uint32_t cand = prefix | (1u << bit);
-    int c = 0;
-    for (int t = lo; t < hi; ++t) c += (keys[t] >= cand) ? 1 : 0;
-    if (block_sum_int(c, red) >= k) prefix = cand;
-  }
-  // prefix is now the k-th largest key.
-  int gt = 0, eq = 0;
-  for (int t = lo; t < hi; ++t) {
-    gt += (keys[t] > prefix) ? 1 : 0;
-    eq += (keys[t] == prefix) ? 1 : 0;
-  }
-  const int total_gt = block_sum_int(gt, red);
-  const int need_eq = k - total_gt;
+  const int need_eq = k - above;
+  int eq = 0;
+  for (int t = lo; t < hi; ++t) eq += (keys[t] == prefix) ? 1 : 0;
   const int eq_before = block_excl_scan(eq, red);
   int kept = 0;
   {

@@ -104,7 +104,8 @@ __host__ __device__ constexpr size_t threshold_smem_bytes(int G, int keys_pad, i
          + sizeof(float) * keys_pad                                              // partial
          + sizeof(uint16_t) * (keys_pad + 2)                                     // keys
          + sizeof(int) * R                                                       // final index
-         + sizeof(float) * kReduceSlots;                                         // reductions
+         + sizeof(float) * kReduceSlots                                          // reductions
+         + sizeof(int) * 256;                                                    // top-k histogram
 }
 
 template <int G>
@@ -132,6 +133,7 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   uint16_t* keys = reinterpret_cast<uint16_t*>(partial + kp);               // [kp]
   int* final_idx = reinterpret_cast<int*>(keys + kp + 2);                   // [R]
   float* red = reinterpret_cast<float*>(final_idx + p.R);                   // [kReduceSlots]
+  int* hist = reinterpret_cast<int*>(red + kReduceSlots);                   // [256]
   __shared__ int s_valid;
   __shared__ int s_start;
 
@@ -311,7 +313,7 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
 
   const int num_keep = p.R - W - 1;
   if (threadIdx.x == 0) final_idx[0] = 0;
-  topk_ascending(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red));
+  topk_ascending(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red), hist);
   for (int i = threadIdx.x; i < W; i += kCompressThreads) final_idx[1 + num_keep + i] = p.S - W + i;
   __syncthreads();
 

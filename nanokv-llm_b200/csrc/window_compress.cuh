@@ -16,7 +16,7 @@
 //   2. Cluster barrier; every CTA reads all partials through distributed shared
 //      memory and forms importance = bf16(sum over all local heads), the single
 //      rounding of the reference's head sum. One kept set per (sequence, rank).
-//   3. Top-k over the bf16 importance keys: a 16-step bitwise search finds the
+//   3. Top-k over the bf16 importance keys: a two-pass radix select finds the
 //      k-th largest key, ties at the cut are broken towards the lower index
 //      (a deterministic refinement of torch.topk's unspecified tie order), and
 //      a block scan emits the kept indices in ascending order.
@@ -62,7 +62,8 @@ __host__ __device__ constexpr size_t window_smem_bytes(int G, int keys_pad, int 
          + sizeof(uint16_t) * (keys_pad + 2)              // bf16 importance keys
          + sizeof(int) * keep_tokens                      // final index list
          + sizeof(int) * kMaxWindowBlocks                 // window block ids
-         + sizeof(float) * kReduceSlots;                  // reductions
+         + sizeof(float) * kReduceSlots                   // reductions
+         + sizeof(int) * 256;                             // top-k histogram
 }
 
 // Exact q.k over 128 dims for the G query heads of a group: bf16 products are
@@ -116,6 +117,7 @@ window_compress_kernel(const WindowCompressParams p) {
   int* final_idx = reinterpret_cast<int*>(keys + kp + 2);          // [keep_tokens]
   int* wblk = final_idx + p.keep_tokens;                           // [window_blocks]
   float* red = reinterpret_cast<float*>(wblk + kMaxWindowBlocks);  // [kReduceSlots]
+  int* hist = reinterpret_cast<int*>(red + kReduceSlots);          // [256]
   __shared__ int s_valid;
   __shared__ int s_tail_block;
 
@@ -233,7 +235,7 @@ window_compress_kernel(const WindowCompressParams p) {
   // 4. top-k and the final index list [0] + kept + [last obs_window tokens].
   const int num_keep = p.keep_tokens - 1 - p.obs_window;
   if (threadIdx.x == 0) final_idx[0] = 0;
-  topk_ascending(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red));
+  topk_ascending(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red), hist);
   for (int i = threadIdx.x; i < p.obs_window; i += kCompressThreads)
     final_idx[1 + num_keep + i] = window_tokens - p.obs_window + i;
   __syncthreads();
