@@ -300,7 +300,13 @@ int nkv_oproj_allreduce_p2p(const void* x, int64_t ldx, const void* w, int64_t l
 /* Entries of selected_batch_indices equal to -1 are skipped.                */
 /* The caller guarantees what the reference asserts (full_blocks >=          */
 /* window_blocks); rows violating it are skipped and flag                    */
-/* NKV_DEVERR_COMPRESS_RANGE.                                                */
+/* NKV_DEVERR_COMPRESS_RANGE. The tail rows go to the slots after the last    */
+/* kept slot in slot arithmetic, as the reference moves them; when           */
+/* keep_tokens + tail exceeds the window they run into the next physical     */
+/* block. Each sequence's own rows are read before that write, but two       */
+/* sequences of one call whose escaped rows land in a block the other reads  */
+/* are not ordered (the reference reads every row of the step first).        */
+/* block_size must be a multiple of 64.                                      */
 int nkv_window_compress(const void* q, int64_t q_stride_token,
                         void* k_cache, void* v_cache, int64_t num_blocks,
                         const int32_t* block_tables, int32_t max_blocks,

@@ -129,6 +129,12 @@ constexpr int kMaxDecodePairs = 1 << 16;
 #ifndef NKV_DECODE_TARGET_ITEMS_PER_SM
 #define NKV_DECODE_TARGET_ITEMS_PER_SM 7
 #endif
+// Rows up to this many tokens are not split when the launch has no more
+// (row, kv head) pairs than a 148-SM part has SMs (latency-bound small
+// batches: a split costs a cross-CTA merge). 0 disables.
+#ifndef NKV_DECODE_SMALL_ROW_TOKENS
+#define NKV_DECODE_SMALL_ROW_TOKENS 1024
+#endif
 
 // Split size depends only on the shapes (not on the device or the lengths), so
 // the workspace query and the launch always agree.
@@ -156,6 +162,9 @@ DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block
   if (cb < min_cb &&
       static_cast<int64_t>(pl.pairs) * ((std::max(max_blocks, 1) + min_cb - 1) / min_cb) >= 148)
     cb = min_cb;
+  if (pl.pairs <= 148 && static_cast<int64_t>(std::max(max_blocks, 1)) * block_size <=
+                            NKV_DECODE_SMALL_ROW_TOKENS)
+    cb = std::max(cb, max_blocks);
   const int max_cb = std::max(1, NKV_DECODE_MAX_SPLIT_TOKENS / block_size);
   pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
   pl.chunk_tokens = pl.chunk_blocks * block_size;
@@ -252,11 +261,31 @@ int launch_threshold(const nkv::ThresholdCompressParams& p, int cluster_x, int g
 }
 
 template <int G>
-int launch_window(const nkv::WindowCompressParams& p, int cluster_x, int grid_y, size_t smem,
-                  cudaStream_t stream) {
+int launch_window(const CUtensorMap& tk, const CUtensorMap& tv, const nkv::WindowCompressParams& p,
+                  int cluster_x, int grid_y, size_t smem, cudaStream_t stream) {
   static size_t smem_set[kMaxDevices] = {0};
-  return launch_cluster(nkv::window_compress_kernel<G>, smem_set, p, cluster_x, grid_y, smem,
-                        stream);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || smem > smem_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nkv::window_compress_kernel<G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e);
+    if (dev >= 0 && dev < kMaxDevices) smem_set[dev] = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster_x, grid_y, 1);
+  cfg.blockDim = dim3(nkv::kCompressThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::window_compress_kernel<G>, tk, tv, p));
 }
 
 }  // namespace
@@ -848,11 +877,13 @@ int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, vo
       !selected_batch_indices)
     return NKV_ERR_INVALID_ARGUMENT;
   if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return NKV_ERR_INVALID_ARGUMENT;
-  if (head_dim != nkv::kCompressHeadDim || num_kv_heads > 8 || obs_window != 1 || block_size <= 0)
+  if (head_dim != nkv::kCompressHeadDim || num_kv_heads > 8 || obs_window != 1 || block_size <= 0 ||
+      block_size % nkv::kWinTileTokens != 0)
     return NKV_ERR_UNSUPPORTED;
   const int g = num_q_heads / num_kv_heads;
   if (g > 16) return NKV_ERR_UNSUPPORTED;
   if (window_blocks <= 0 || window_blocks > nkv::kMaxWindowBlocks) return NKV_ERR_UNSUPPORTED;
+  if (num_blocks <= 0) return NKV_ERR_INVALID_ARGUMENT;
   const int window_tokens = window_blocks * block_size;
   // SnapKV's own guard (CompressMethod.py:17-18) is the caller's job: the
   // Python layer skips the call, as the reference returns False.
@@ -887,13 +918,24 @@ int nkv_window_compress(const void* q, int64_t q_stride_token, void* k_cache, vo
   const int G = padded_group(g);
   const size_t smem = nkv::window_smem_bytes(G, p.keys_pad, keep_tokens);
   if (smem > kMaxSmem) return NKV_ERR_UNSUPPORTED;
+  // K (and, for L2 prefetches, V) rows of one head in 64-token tiles (two
+  // 64-dim halves, 128-byte swizzle)
+  CUtensorMap tk, tv;
+  const uint64_t num_slots = static_cast<uint64_t>(num_blocks) * block_size;
+  const uint64_t row_bytes = static_cast<uint64_t>(num_kv_heads) * head_dim * 2;
+  int st = encode_3d(&tk, k_cache, head_dim, num_kv_heads, num_slots, head_dim * 2, row_bytes, 1,
+                     nkv::kWinTileTokens, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (st != NKV_OK) return st;
+  st = encode_3d(&tv, v_cache, head_dim, num_kv_heads, num_slots, head_dim * 2, row_bytes, 1,
+                 nkv::kWinTileTokens, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (st != NKV_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (G) {
-    case 1: return launch_window<1>(p, num_kv_heads, num_selected, smem, s);
-    case 2: return launch_window<2>(p, num_kv_heads, num_selected, smem, s);
-    case 4: return launch_window<4>(p, num_kv_heads, num_selected, smem, s);
-    case 8: return launch_window<8>(p, num_kv_heads, num_selected, smem, s);
-    default: return launch_window<16>(p, num_kv_heads, num_selected, smem, s);
+    case 1: return launch_window<1>(tk, tv, p, num_kv_heads, num_selected, smem, s);
+    case 2: return launch_window<2>(tk, tv, p, num_kv_heads, num_selected, smem, s);
+    case 4: return launch_window<4>(tk, tv, p, num_kv_heads, num_selected, smem, s);
+    case 8: return launch_window<8>(tk, tv, p, num_kv_heads, num_selected, smem, s);
+    default: return launch_window<16>(tk, tv, p, num_kv_heads, num_selected, smem, s);
   }
 }
 

@@ -213,24 +213,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       const int t0 = s * p.chunk_tokens;
       const int t1 = min(t0 + p.chunk_tokens, len);
       const int ntiles = len > 0 ? (t1 - t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
-      // KvChat: this step's query rows of the group join the row's window.
-      if (p.ring_vec != nullptr && s == 0) {
-        const int rs = __ldg(p.ring_slot_of_row + b);
-        if (rs >= 0) {
-          const int pos = __ldg(p.ring_pos_of_row + b);
-          if (rs < p.ring_slots && pos >= 0 && pos < p.ring_window) {
-            const int n = g * (kDecodeHeadDim / 8);  // the group's q rows, 16-byte units
-            const uint4* src = p.q_vec + static_cast<int64_t>(b) * p.q_stride_token_vec +
-                               static_cast<int64_t>(kvh) * n;
-            uint4* dst = p.ring_vec + p.ring_layer_base_vec + rs * p.ring_slot_stride_vec +
-                         static_cast<int64_t>(pos) * p.num_q_heads * (kDecodeHeadDim / 8) +
-                         static_cast<int64_t>(kvh) * n;
-            for (int i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
-          } else if (leader) {
-            raise_error(NKV_DEVERR_RING_RANGE);
-          }
-        }
-      }
       int j = 0;
       do {
         bool waited = true;
@@ -303,6 +285,25 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
             }
           }
           armed[stage] = phase + 1u;
+        }
+        // KvChat: this step's query rows of the group join the row's window
+        // (after the item's first tile is in flight: nothing here waits on it).
+        if (j == 0 && p.ring_vec != nullptr && s == 0) {
+          const int rs = __ldg(p.ring_slot_of_row + b);
+          if (rs >= 0) {
+            const int pos = __ldg(p.ring_pos_of_row + b);
+            if (rs < p.ring_slots && pos >= 0 && pos < p.ring_window) {
+              const int n = g * (kDecodeHeadDim / 8);  // the group's q rows, 16-byte units
+              const uint4* src = p.q_vec + static_cast<int64_t>(b) * p.q_stride_token_vec +
+                                 static_cast<int64_t>(kvh) * n;
+              uint4* dst = p.ring_vec + p.ring_layer_base_vec + rs * p.ring_slot_stride_vec +
+                           static_cast<int64_t>(pos) * p.num_q_heads * (kDecodeHeadDim / 8) +
+                           static_cast<int64_t>(kvh) * n;
+              for (int i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
+            } else if (leader) {
+              raise_error(NKV_DEVERR_RING_RANGE);
+            }
+          }
         }
         if (++stage == kStages) {
           stage = 0;

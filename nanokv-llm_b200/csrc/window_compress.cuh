@@ -10,9 +10,15 @@
 //   1. Each CTA scores the window keys of its kv head against the g query heads
 //      of its GQA group, reproducing the reference's bf16 rounding points:
 //      score = bf16(q.k) (exact fp64 accumulation of the exact bf16 products,
-//      then float, then bf16, as the reference's CPU matmul rounds),
-//      bf16(score * scale), sink key 0 -> -inf, p = bf16(exp(s - max) / sum)
-//      per head, and the CTA's fp32 sum of p over its heads.
+//      then float, then bf16: the exactly rounded score), bf16(score *
+//      scale), sink key 0 -> -inf, p = bf16(exp(s - max) / sum) per head, and
+//      the CTA's fp32 sum of p over its heads. The window's K rows of this
+//      head stream through a ring of four 64-token tiles (TMA, 128-byte
+//      swizzle, no multicast, kept in L2 for the compaction that re-reads the
+//      kept rows); each pair of warps owns one ring stage -- its leader
+//      refills it as soon as both warps are done with it -- and each thread
+//      scores one key from shared memory (conflict-free through the swizzle;
+//      the q rows are a broadcast).
 //   2. Cluster barrier; every CTA reads all partials through distributed shared
 //      memory and forms importance = bf16(sum over all local heads), the single
 //      rounding of the reference's head sum. One kept set per (sequence, rank).
@@ -54,9 +60,18 @@ struct WindowCompressParams {
   int keys_pad;     // num_keys rounded up to kCompressThreads
 };
 
-// Shared-memory bytes of window_compress_kernel<G> (host and device agree).
+constexpr int kWinTileTokens = 64;                    // tokens per K tile
+constexpr int kWinStages = 4;                         // ring stages = warp pairs
+constexpr int kWinHalfBytes = kWinTileTokens * 128;   // 64 dims x 64 tokens, bf16
+constexpr int kWinTileBytes = 2 * kWinHalfBytes;      // 16 KB
+constexpr int kWinRingBytes = kWinStages * kWinTileBytes + 64;  // + the full barriers
+static_assert(kWinStages * 64 == kCompressThreads, "one warp pair (64 keys) per stage");
+
+// Shared-memory bytes of window_compress_kernel<G> (host and device agree):
+// the K ring (1024-byte aligned, hence the slack) and the layout after it.
 __host__ __device__ constexpr size_t window_smem_bytes(int G, int keys_pad, int keep_tokens) {
-  return sizeof(double) * G * kCompressHeadDim          // q rows as doubles
+  return 1024 + kWinRingBytes
+         + sizeof(double) * G * kCompressHeadDim          // q rows as doubles
          + sizeof(float) * static_cast<size_t>(G) * keys_pad  // scores / exp
          + sizeof(float) * keys_pad                       // partial (cluster-visible)
          + sizeof(uint16_t) * (keys_pad + 2)              // bf16 importance keys
@@ -66,41 +81,19 @@ __host__ __device__ constexpr size_t window_smem_bytes(int G, int keys_pad, int 
          + sizeof(int) * 256;                             // top-k histogram
 }
 
-// Exact q.k over 128 dims for the G query heads of a group: bf16 products are
-// exact in fp64 and 128 of them sum exactly for any realistic exponent spread.
-template <int G>
-__device__ __forceinline__ void dot_rows_fp64(const __nv_bfloat16* krow, const double* qd,
-                                              double (&acc)[G]) {
-#pragma unroll
-  for (int r = 0; r < G; ++r) acc[r] = 0.0;
-  const uint4* kv = reinterpret_cast<const uint4*>(krow);
-#pragma unroll 2
-  for (int c = 0; c < kCompressHeadDim / 8; ++c) {
-    const uint4 w = __ldg(kv + c);
-    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-    double kd[8];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      kd[2 * e] = static_cast<double>(__uint_as_float(wv[e] << 16));
-      kd[2 * e + 1] = static_cast<double>(__uint_as_float(wv[e] & 0xffff0000u));
-    }
-#pragma unroll
-    for (int r = 0; r < G; ++r) {
-      const double2* qp = reinterpret_cast<const double2*>(qd + r * kCompressHeadDim + c * 8);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const double2 qq = qp[e];
-        acc[r] = fma(qq.x, kd[2 * e], acc[r]);
-        acc[r] = fma(qq.y, kd[2 * e + 1], acc[r]);
-      }
-    }
-  }
+__device__ __forceinline__ void pair_barrier(int pair) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
 }
 
 template <int G>
 __global__ void __launch_bounds__(kCompressThreads, 2)
-window_compress_kernel(const WindowCompressParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
+window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const WindowCompressParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kWinStages * kWinTileBytes);
+  uint8_t* smem = ring + kWinRingBytes;
   cg::cluster_group cluster = cg::this_cluster();
   const int head = static_cast<int>(cluster.block_rank());  // == blockIdx.x
   const int sel_i = blockIdx.y;
@@ -120,6 +113,8 @@ window_compress_kernel(const WindowCompressParams p) {
   int* hist = reinterpret_cast<int*>(red + kReduceSlots);          // [256]
   __shared__ int s_valid;
   __shared__ int s_tail_block;
+  __shared__ int s_abort;           // a K tile never landed (cluster-visible)
+  __shared__ int s_pair_abort[kWinStages];
 
   // The kv heads of a sequence are the CTAs of one cluster (their partial
   // sums meet in distributed shared memory). A launch that lost its
@@ -157,6 +152,12 @@ window_compress_kernel(const WindowCompressParams p) {
     if (!valid && head == 0) raise_error(NKV_DEVERR_COMPRESS_RANGE);
     s_valid = valid;
     s_tail_block = tb;
+    s_abort = 0;
+    for (int st = 0; st < kWinStages; ++st) {
+      mbar_init(smem_u32(&full[st]), 1);
+      s_pair_abort[st] = 0;
+    }
+    fence_barrier_init();
   }
   // q rows of this GQA group as doubles (rows >= g are zero).
   for (int i = threadIdx.x; i < G * kCompressHeadDim; i += kCompressThreads) {
@@ -170,21 +171,113 @@ window_compress_kernel(const WindowCompressParams p) {
   const bool valid = s_valid != 0;  // identical in every CTA of the cluster
 
   if (valid) {
-    // 1. scores, one thread per key row
-    for (int t = threadIdx.x; t < kp; t += kCompressThreads) {
-      if (t < nk) {
-        const int64_t slot = static_cast<int64_t>(wblk[t / bs]) * bs + (t % bs);
-        double acc[G];
-        dot_rows_fp64<G>(p.k_cache + (slot * p.num_kv_heads + head) * kCompressHeadDim, qd, acc);
+    // 1. scores: tile j (tokens [64 j, 64 j + 64) of the window, two 64-dim
+    // halves of 64 rows x 128 bytes) lands in ring stage j % 4, which warp
+    // pair j % 4 consumes, one key per thread.
+    const int ntiles = window_tokens / kWinTileTokens;
+    const int tiles_per_block = bs / kWinTileTokens;
+    const int pair = threadIdx.x >> 6;
+    const int tp = threadIdx.x & 63;
+    const bool pair_leader = tp == 0;
+    uint8_t* stage = ring + pair * kWinTileBytes;
+    const uint32_t fb = smem_u32(&full[pair]);
+    auto issue = [&](int j) {
+      const int slot0 = wblk[j / tiles_per_block] * bs + (j % tiles_per_block) * kWinTileTokens;
+      const uint64_t pol = l2_policy_evict_last();
+      mbar_arrive_expect_tx(fb, kWinTileBytes);
+      tma_load_3d(smem_u32(stage), &tm_k, fb, 0, head, slot0, pol);
+      tma_load_3d(smem_u32(stage) + kWinHalfBytes, &tm_k, fb, 64, head, slot0, pol);
+    };
+    if (pair_leader && pair < ntiles) {
+      prefetch_tmap(&tm_k);
+      issue(pair);
+    }
+    if (threadIdx.x == 32) {
+      // Every K tile of the window, and the V rows and tail block the
+      // compaction will read, start moving into L2 now, so the ring's loads
+      // and the compaction's reads find them there instead of waiting on
+      // DRAM one tile (or chunk) at a time.
+      prefetch_tmap(&tm_v);
+      for (int jj = kWinStages; jj < ntiles; ++jj) {
+        const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
+        tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
+      }
+      for (int jj = 0; jj < ntiles; ++jj) {
+        const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
+        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
+      }
+      for (int t0 = 0; t0 < tail_len; t0 += kWinTileTokens) {
+        const int slot0 = s_tail_block * bs + t0;
+        tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
+      }
+    }
+    int use = 0;
+    int j = pair;
+    for (; j < ntiles; j += kWinStages, ++use) {
+      if (!mbar_wait_bounded(fb, use & 1)) s_pair_abort[pair] = 1;
+      pair_barrier(pair);
+      if (s_pair_abort[pair]) break;  // uniform across the pair
+      // kAcc independent fp64 sums per head (the sum of exact products does
+      // not depend on their order at the precision kept), so the DFMA
+      // latency overlaps
+      constexpr int kAcc = G <= 4 ? 4 : (G <= 8 ? 2 : 1);
+      double acc[G][kAcc];
+#pragma unroll
+      for (int r = 0; r < G; ++r)
+#pragma unroll
+        for (int a = 0; a < kAcc; ++a) acc[r][a] = 0.0;
+#pragma unroll 2
+      for (int c = 0; c < kCompressHeadDim / 8; ++c) {
+        const int cc = c & 7;
+        const uint4 w = *reinterpret_cast<const uint4*>(stage + (c >> 3) * kWinHalfBytes +
+                                                        tp * 128 + ((cc ^ (tp & 7)) << 4));
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+        double kd[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          kd[2 * e] = static_cast<double>(__uint_as_float(wv[e] << 16));
+          kd[2 * e + 1] = static_cast<double>(__uint_as_float(wv[e] & 0xffff0000u));
+        }
 #pragma unroll
         for (int r = 0; r < G; ++r) {
-          const float s = round_bf16(static_cast<float>(acc[r]));
-          scores[r * kp + t] = (t == 0) ? -INFINITY : round_bf16(s * p.scale);
-        }
-      } else {
+          const double2* qp = reinterpret_cast<const double2*>(qd + r * kCompressHeadDim + c * 8);
 #pragma unroll
-        for (int r = 0; r < G; ++r) scores[r * kp + t] = -INFINITY;
+          for (int e = 0; e < 4; ++e) {
+            const double2 qq = qp[e];
+            acc[r][(2 * e) % kAcc] = fma(qq.x, kd[2 * e], acc[r][(2 * e) % kAcc]);
+            acc[r][(2 * e + 1) % kAcc] = fma(qq.y, kd[2 * e + 1], acc[r][(2 * e + 1) % kAcc]);
+          }
+        }
       }
+      const int t = j * kWinTileTokens + tp;
+      if (t < kp) {
+#pragma unroll
+        for (int r = 0; r < G; ++r) {
+          double sum = acc[r][0];
+#pragma unroll
+          for (int a = 1; a < kAcc; ++a) sum += acc[r][a];
+          const float sc = round_bf16(static_cast<float>(sum));
+          scores[r * kp + t] = (t == 0 || t >= nk) ? -INFINITY : round_bf16(sc * p.scale);
+        }
+      }
+      pair_barrier(pair);  // both warps are done with the stage
+      if (pair_leader && j + kWinStages < ntiles) issue(j + kWinStages);
+    }
+    if (j < ntiles && pair_leader) {
+      // a tile never landed: wait (bounded) for the stage's load in flight,
+      // then the cluster skips this sequence
+      mbar_wait_bounded(fb, use & 1);
+      s_abort = 1;
+    }
+    // keys past the window (padding) never win
+    for (int t = window_tokens + threadIdx.x; t < kp; t += kCompressThreads) {
+#pragma unroll
+      for (int r = 0; r < G; ++r) scores[r * kp + t] = -INFINITY;
     }
     __syncthreads();
     // 2. softmax of every head over the keys (bf16 output), fp32 group sum
@@ -218,7 +311,14 @@ window_compress_kernel(const WindowCompressParams p) {
     }
   }
   cluster.sync();
+  // a CTA whose K ring gave up makes the whole sequence skip (no kept set is
+  // formed from an incomplete importance)
+  bool run = valid;
   if (valid) {
+    for (int c = 0; c < static_cast<int>(cluster.num_blocks()); ++c)
+      run = run && *cluster.map_shared_rank(&s_abort, c) == 0;
+  }
+  if (run) {
     // 3. importance = bf16(sum over all local heads), read across the cluster.
     const int nranks = static_cast<int>(cluster.num_blocks());
     for (int t = threadIdx.x; t < kp; t += kCompressThreads) {
@@ -230,7 +330,7 @@ window_compress_kernel(const WindowCompressParams p) {
     }
   }
   cluster.sync();  // no CTA may leave while a peer still reads its partials
-  if (!valid) return;
+  if (!run) return;
 
   // 4. top-k and the final index list [0] + kept + [last obs_window tokens].
   const int num_keep = p.keep_tokens - 1 - p.obs_window;

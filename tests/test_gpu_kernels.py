@@ -424,11 +424,15 @@ def test_window_compaction_maximal_overlap(cuda_lib):
     exactly one slot, onto the row read just before it. The reference stages
     the rows through .clone() (nanokvllm/layers/compress_utils.py:257-260);
     the kernel reads each 64-row chunk before writing it. Cache bytes must
-    equal the oracle's staged copy bit for bit."""
+    equal the oracle's staged copy bit for bit. The lengths are whole blocks:
+    with a partial tail block, keep_tokens 1,023 would send the tail rows
+    past the window (the reference's slot arithmetic, compress_utils.py:
+    230-231) into whatever physical block follows it -- see
+    test_window_tail_escape_single_sequence."""
     ops = _ops()
     Hq, Hk, D, B, wb = 32, 8, 128, 256, 4
     g = Hq // Hk
-    pb = make_paged_batch(seed=91, lens=[1500, 2600], Hq=Hq, Hk=Hk)
+    pb = make_paged_batch(seed=91, lens=[1536, 2560], Hq=Hq, Hk=Hk)
     k0, v0 = pb.k_cache.clone(), pb.v_cache.clone()
     store_kvcache_ref(pb.k_new, pb.v_new, k0, v0, pb.slot_mapping)
     kf = k0.view(-1, Hk, D)
@@ -454,6 +458,38 @@ def test_window_compaction_maximal_overlap(cuda_lib):
     okeep, _ = window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1,
                                    [0, 1], B, wb, 3, 255)
     assert okeep.tolist() == [expect, expect]
+    assert torch.equal(kd.cpu().view(torch.int16), k1.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v1.view(torch.int16))
+    assert cl.cpu().tolist() == cl1.tolist()
+
+
+def test_window_tail_escape_single_sequence(cuda_lib):
+    """The reference moves the partial tail block to dst_keep[-1] + 1 + j in
+    SLOT arithmetic (nanokvllm/layers/compress_utils.py:230-231): when the kept
+    rows end near the window's last block, the tail rows run past it into the
+    next physical block, whatever it holds. With one selected sequence the
+    kernel reproduces that write bit for bit (its own rows are all read
+    before the tail is written). Two sequences whose escaped rows land in a
+    block the other sequence reads are not ordered by the kernel (the
+    reference stages every read of the step first); such layouts are outside
+    the reference's working configurations (keep_tokens + tail <= window)."""
+    ops = _ops()
+    Hq, Hk, B, wb = 32, 8, 256, 4
+    pb = make_paged_batch(seed=91, lens=[1500, 2600], Hq=Hq, Hk=Hk)
+    keep_tokens = 3 * B + 255
+    k0, v0 = pb.k_cache.clone(), pb.v_cache.clone()
+    store_kvcache_ref(pb.k_new, pb.v_new, k0, v0, pb.slot_mapping)
+    kd, vd = k0.to(DEV), v0.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    sel = torch.tensor([0], dtype=torch.int32, device=DEV)
+    keep_out = torch.full((1, keep_tokens), -7, dtype=torch.int32, device=DEV)
+    ops.window_compress(pb.q.to(DEV), kd, vd, pb.block_tables.to(DEV), cl.clone(), cl, sel, wb,
+                        keep_tokens, out_keep_idx=keep_out)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    k1, v1, cl1 = k0.clone(), v0.clone(), pb.context_lens.clone()
+    window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1, [0], B, wb,
+                        3, 255, keep_idx_override=keep_out.cpu().long())
     assert torch.equal(kd.cpu().view(torch.int16), k1.view(torch.int16))
     assert torch.equal(vd.cpu().view(torch.int16), v1.view(torch.int16))
     assert cl.cpu().tolist() == cl1.tolist()
