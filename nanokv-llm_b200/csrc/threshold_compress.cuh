@@ -277,12 +277,23 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
         }
       }
       __syncthreads();
-      // ---- C: per key, window-ordered sum of each head's bf16 probabilities
+      // ---- C: per key, window-ordered sum of each head's bf16 probabilities.
+      // A head's rows in this group are summed in a register, continuing the
+      // head's running sum from earlier groups (the same fp32 additions in the
+      // same order as one sequential sum); the exponentials and divisions of
+      // successive rows do not depend on each other and overlap.
       for (int t = threadIdx.x; t < nk; t += kCompressThreads) {
-        for (int lr = 0; lr < grows; ++lr) {
+        int lr = 0;
+        while (lr < grows) {
           const int r = (row0 + lr) / W;
-          const float e = expf(__bfloat162float(sc[static_cast<size_t>(lr) * ss + t]) - rmax[lr]);
-          kacc[r * kp + t] += round_bf16(e / rsum[lr]);
+          const int lr_end = min(grows, (r + 1) * W - row0);
+          float acc = kacc[r * kp + t];
+#pragma unroll 4
+          for (; lr < lr_end; ++lr) {
+            const float e = expf(__bfloat162float(sc[static_cast<size_t>(lr) * ss + t]) - rmax[lr]);
+            acc += round_bf16(e / rsum[lr]);
+          }
+          kacc[r * kp + t] = acc;
         }
       }
       __syncthreads();
