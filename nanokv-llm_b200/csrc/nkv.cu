@@ -104,7 +104,7 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint
 // ---------------------------------------------------------------- decode plan
 struct DecodePlan {
   int g;
-  int chunk_blocks;
+  int cluster;  // > 1: splits of a pair form one cluster (its size)
   int chunk_tokens;
   int max_splits;
   int pairs;
@@ -135,6 +135,36 @@ constexpr int kMaxDecodePairs = 1 << 16;
 #ifndef NKV_DECODE_SMALL_ROW_TOKENS
 #define NKV_DECODE_SMALL_ROW_TOKENS 1024
 #endif
+// Small launches -- at most 74 (row, kv head) pairs, so that every pair can
+// have at least two CTAs on a 148-SM part -- split each row over a cluster of
+// up to 8 CTAs whose partials merge through distributed shared memory. One SM
+// pulls only ~85 GB/s through TMA, so a B = 1 step over 8 kv heads would
+// otherwise run on 8 SMs, and a merge through global memory costs several
+// L2 round trips. Rows longer than this many 128-token tiles per CTA use the
+// ordinary splits instead. 0 disables.
+#ifndef NKV_DECODE_CLUSTER_MAX_TILES
+#define NKV_DECODE_CLUSTER_MAX_TILES 64
+#endif
+
+// Opt-in shared memory per block on sm_100 (227 KB).
+constexpr int kSmemOptinBytes = 232448;
+
+// Largest cluster of splits whose receive rows fit next to the kernel's
+// shared memory for padded group width G (0 or 1: no cluster mode).
+template <int G>
+constexpr int decode_cluster_cap() {
+  using S = nkv::DecodeShape<G>;
+  const int room = (kSmemOptinBytes - S::kSmemBytes) / S::kRecvBytesPerSplit;
+  return room < nkv::kDecodeMaxClusterSplits ? room : nkv::kDecodeMaxClusterSplits;
+}
+
+int decode_cluster_cap_for(int g) {
+  if (g <= 1) return decode_cluster_cap<1>();
+  if (g <= 2) return decode_cluster_cap<2>();
+  if (g <= 4) return decode_cluster_cap<4>();
+  if (g <= 8) return decode_cluster_cap<8>();
+  return 0;  // G = 16: the receive rows do not fit
+}
 
 // Split size depends only on the shapes (not on the device or the lengths), so
 // the workspace query and the launch always agree.
@@ -166,9 +196,21 @@ DecodePlan make_decode_plan(int batch, int hq, int hk, int max_blocks, int block
                             NKV_DECODE_SMALL_ROW_TOKENS)
     cb = std::max(cb, max_blocks);
   const int max_cb = std::max(1, NKV_DECODE_MAX_SPLIT_TOKENS / block_size);
-  pl.chunk_blocks = std::min(std::max(cb, 1), max_cb);
-  pl.chunk_tokens = pl.chunk_blocks * block_size;
-  pl.max_splits = std::max(1, (std::max(max_blocks, 1) + pl.chunk_blocks - 1) / pl.chunk_blocks);
+  pl.chunk_tokens = std::min(std::max(cb, 1), max_cb) * block_size;
+  const int64_t row_tokens = static_cast<int64_t>(std::max(max_blocks, 1)) * block_size;
+  const int64_t row_tiles = (row_tokens + nkv::kDecodeTileTokens - 1) / nkv::kDecodeTileTokens;
+  pl.cluster = 0;
+  const int cap = std::min(decode_cluster_cap_for(pl.g), 148 / std::max(pl.pairs, 1));
+  if (NKV_DECODE_CLUSTER_MAX_TILES > 0 && cap >= 2 && row_tiles >= 2) {
+    const int64_t c = std::min<int64_t>(cap, row_tiles);
+    const int64_t tiles = (row_tiles + c - 1) / c;
+    if (tiles <= NKV_DECODE_CLUSTER_MAX_TILES) {
+      pl.chunk_tokens = static_cast<int>(tiles * nkv::kDecodeTileTokens);
+      pl.cluster = static_cast<int>((row_tokens + pl.chunk_tokens - 1) / pl.chunk_tokens);
+      if (pl.cluster < 2) pl.cluster = 0;
+    }
+  }
+  pl.max_splits = static_cast<int>(std::max<int64_t>(1, (row_tokens + pl.chunk_tokens - 1) / pl.chunk_tokens));
   // Layout: [scheduler counters][split counters for kMaxDecodePairs pairs]
   // [partial (m, l)][partial O]. The counter region has a FIXED size so
   // that, whatever shapes share one workspace, a counter never lands on
@@ -189,27 +231,63 @@ template <int G>
 int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tq,
                   const nkv::DecodeParams& p, cudaStream_t stream) {
   using S = nkv::DecodeShape<G>;
+  constexpr int kCap = decode_cluster_cap<G>();
+  constexpr int kMaxSmem = S::kSmemBytes + (kCap > 1 ? kCap : 0) * S::kRecvBytesPerSplit;
   static bool attr_set[kMaxDevices] = {false};
+  // clusters of C splits that fit at once, per device and C (-1 = not asked)
+  static int active_clusters[kMaxDevices][nkv::kDecodeMaxClusterSplits + 1];
+  static std::once_flag init_once;
+  std::call_once(init_once, [] {
+    for (auto& row : active_clusters)
+      for (int& v : row) v = -1;
+  });
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+  if (dev < 0 || dev >= kMaxDevices) return NKV_ERR_CUDA;
+  if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(nkv::paged_decode_kernel<G>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     if (e != cudaSuccess) return cuda_status(e);
     attr_set[dev] = true;
   }
-  const int grid = std::max(1, std::min(sm_count(dev), p.total_items));
+  nkv::DecodeParams q = p;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(nkv::kDecodeThreads, 1, 1);
-  cfg.dynamicSmemBytes = S::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::paged_decode_kernel<G>, tk, tv, tq, p));
+  if (q.cluster > 1 && q.cluster <= kCap) {
+    // One cluster per pair, all resident at once (the leader waits for its
+    // peers); otherwise the same splits merge through global memory.
+    cfg.gridDim = dim3(q.total_items, 1, 1);
+    cfg.dynamicSmemBytes = S::kSmemBytes + q.cluster * S::kRecvBytesPerSplit;
+    attr[1].val.clusterDim.x = q.cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    int& fit = active_clusters[dev][q.cluster];
+    if (fit < 0) {
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, nkv::paged_decode_kernel<G>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      fit = n;
+    }
+    if (fit * q.cluster < q.total_items) q.cluster = 0;
+  } else {
+    q.cluster = 0;
+  }
+  if (q.cluster == 0) {
+    cfg.gridDim = dim3(std::max(1, std::min(sm_count(dev), q.total_items)), 1, 1);
+    cfg.dynamicSmemBytes = S::kSmemBytes;
+    cfg.numAttrs = 1;
+  }
+  return cuda_status(cudaLaunchKernelEx(&cfg, nkv::paged_decode_kernel<G>, tk, tv, tq, q));
 }
 
 int padded_group(int g) {
@@ -435,6 +513,7 @@ int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
   p.block_size = block_size;
   p.chunk_tokens = pl.chunk_tokens;
   p.max_splits = pl.max_splits;
+  p.cluster = pl.cluster;
   p.total_items = pl.pairs * pl.max_splits;
   if (fused != nullptr) {
     const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;

@@ -49,6 +49,11 @@ constexpr int kDecodeMergerWarp = kDecodeConsumerWarps + 1;
 constexpr int kDecodeThreads = (kDecodeConsumerWarps + 2) * 32;
 constexpr int kHalfTileBytes = kDecodeTileTokens * 128;  // 128 rows x 64 dims x 2 B
 constexpr int kDecodeMetaInts = 8;
+// A split's (O, m, l) of one q row as the cluster leader receives it:
+// O[128], m, l, 2 floats of padding (16-byte aligned rows).
+constexpr int kRecvRowFloats = kDecodeHeadDim + 4;
+// Largest cluster of splits (portable cluster size).
+constexpr int kDecodeMaxClusterSplits = 8;
 
 template <int G>
 struct DecodeShape {
@@ -63,9 +68,15 @@ struct DecodeShape {
   static constexpr int kSlotOFloats = kDecodeConsumerWarps * G * kORowStride;
   static constexpr int kSlotMLFloats = 2 * kDecodeConsumerWarps * G;
   static constexpr int kSlotBytes = (kSlotOFloats + kSlotMLFloats) * 4 + 16;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kSlots * kSlotBytes +
-                                    (2 * kStages + 2 * kSlots) * 8 +
-                                    kStages * kDecodeMetaInts * 4 + 16 + 1024 /* alignment */;
+  // [stages][slots][barriers][meta][flags (16 B)][receive barrier (16 B)]
+  // [receive rows: cluster launches only, kRecvRowFloats per (split, row)]
+  static constexpr int kRecvBarOffset = kStages * kStageBytes + kSlots * kSlotBytes +
+                                        (2 * kStages + 2 * kSlots) * 8 +
+                                        kStages * kDecodeMetaInts * 4 + 16;
+  static constexpr int kRecvOffset = kRecvBarOffset + 16;
+  static constexpr int kSmemBytes = kRecvOffset + 1024 /* alignment */;
+  // A cluster launch of C splits adds C * G receive rows.
+  static constexpr int kRecvBytesPerSplit = G * kRecvRowFloats * 4;
 };
 
 struct DecodeParams {
@@ -87,6 +98,10 @@ struct DecodeParams {
   int chunk_tokens;
   int max_splits;
   int total_items;
+  // > 1: launched as clusters of `cluster` CTAs, CTA r of cluster c taking
+  // split r of (row, kv head) pair c and sending its partial to rank 0
+  // through distributed shared memory (no global partials or counters).
+  int cluster;
   // Fused decode step (optional, null when unused): the step's new K/V rows,
   // written by the producer warp right before the TMA that reads them, and
   // the KvChat query-window ring append.
@@ -135,6 +150,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   uint64_t* slot_empty = slot_full + kSlots;   // 1 merger arrival
   int* meta = reinterpret_cast<int*>(slot_empty + kSlots);
   volatile int* flags = meta + kStages * kDecodeMetaInts;  // [0] abort
+  uint64_t* recv_bar = reinterpret_cast<uint64_t*>(smem + S::kRecvBarOffset);
+  float* recv = reinterpret_cast<float*>(smem + S::kRecvOffset);
+  // Cluster split mode needs the launch's clusters; a launch that lost them
+  // (%cluster_nctarank 1) merges its splits through global memory instead.
+  const int csize = p.cluster;
+  const bool cluster_mode = csize > 1 && static_cast<int>(cluster_nctarank()) == csize;
 
   auto slot_o = [&](int s) { return reinterpret_cast<float*>(slot_mem + s * S::kSlotBytes); };
   auto slot_m = [&](int s) { return slot_o(s) + S::kSlotOFloats; };
@@ -155,6 +176,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       mbar_init(smem_u32(&slot_full[s]), kDecodeConsumerWarps * 32);
       mbar_init(smem_u32(&slot_empty[s]), 1);
     }
+    // every CTA's merger lanes arrive once on the leader's receive barrier
+    if (cluster_mode) mbar_init(smem_u32(recv_bar), 32 * csize);
     flags[0] = 0;
     fence_barrier_init();
   }
@@ -164,6 +187,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     prefetch_tmap(&tm_q);
   }
   __syncthreads();
+  // No CTA arrives on the leader's receive barrier before it is initialised.
+  if (cluster_mode) cluster_sync_all();
   // Launched with programmatic stream serialisation: everything above
   // overlapped the previous kernel (typically the previous layer's decode);
   // from here on its writes (cache rows, the reset workspace counters) are
@@ -198,21 +223,112 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     // Items are grabbed one at a time, only when the ring has room for their
     // first tile: claiming the next item early lets a busy CTA hold work an
     // idle one could have taken, which lengthens the tail (measured slower).
+    // A CTA's first item is fixed by its block index; later ones come from
+    // the counter (offset by the grid size).
+    // In a split-cluster launch CTA r of cluster c takes split r of pair c.
+    int static_item = static_cast<int>(blockIdx.x);
+    if (csize > 1)
+      static_item = static_cast<int>(blockIdx.x) % csize * (Hk * p.batch) +
+                    static_cast<int>(blockIdx.x) / csize;
     while (ok) {
-      int item = 0;
-      if (leader) item = static_cast<int>(atomicAdd(&p.counters[0], 1u));
-      item = __shfl_sync(0xffffffffu, item, 0);
+      int item = static_item;
+      if (item < 0) {
+        if (leader) item = static_cast<int>(gridDim.x + atomicAdd(&p.counters[0], 1u));
+        item = __shfl_sync(0xffffffffu, item, 0);
+      }
+      static_item = -1;
       if (item >= p.total_items) break;
       const int kvh = item % Hk;
       const int rest = item / Hk;
       const int b = rest % p.batch;
       const int s = rest / p.batch;
-      const int len = __ldg(p.context_lens + b);
+      const int t0 = s * p.chunk_tokens;
+      const int blk_first = t0 / p.block_size;
+      // Everything the item needs from global memory is requested in one
+      // round, spread over the lanes, so the item costs one load latency
+      // before its first tile instead of a chain of dependent ones: the
+      // scalars (lanes 0-3), 32 block-table entries from the split's first
+      // block, the new K/V head rows (fused slot write) and the group's q
+      // rows (KvChat query window).
+      int scalar = 0;
+      if (lane == 0) {
+        scalar = __ldg(p.context_lens + b);
+      } else if (lane == 1) {
+        scalar = p.new_k != nullptr ? __ldg(p.slot_mapping + b) : -1;
+      } else if (lane == 2 || lane == 3) {
+        if (p.ring_vec != nullptr && s == 0)
+          scalar = __ldg((lane == 2 ? p.ring_slot_of_row : p.ring_pos_of_row) + b);
+      }
+      const int bt_ent = blk_first + lane < p.max_blocks
+                             ? __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
+                                     blk_first + lane)
+                             : -1;
+      constexpr int kHeadVecs = kDecodeHeadDim / 8;  // 16-byte units of one head row
+      uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
+      if (p.new_k != nullptr) {
+        // lanes 0-15: the K head row, 16-31: the V head row
+        const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
+        new_row = lane < kHeadVecs ? __ldg(p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col)
+                                   : __ldg(p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
+      }
+      constexpr int kQVecsPerLane = G >= 2 ? G / 2 : 1;
+      const int q_vecs = g * kHeadVecs;  // the group's q rows
+      uint4 q_rows[kQVecsPerLane];
+      if (p.ring_vec != nullptr && s == 0) {
+        const uint4* src = p.q_vec + static_cast<int64_t>(b) * p.q_stride_token_vec +
+                           static_cast<int64_t>(kvh) * q_vecs;
+#pragma unroll
+        for (int i = 0; i < kQVecsPerLane; ++i)
+          if (lane + 32 * i < q_vecs) q_rows[i] = __ldg(src + lane + 32 * i);
+      }
+      const int len = __shfl_sync(0xffffffffu, scalar, 0);
+      const int slot_new = __shfl_sync(0xffffffffu, scalar, 1);
+      const int ring_slot = __shfl_sync(0xffffffffu, scalar, 2);
+      const int ring_pos = __shfl_sync(0xffffffffu, scalar, 3);
+      // Block index of the cache block holding token position `tok` of row b.
+      auto block_of = [&](int tok) -> int {
+        const int bi = tok / p.block_size - blk_first;
+        int blk = __shfl_sync(0xffffffffu, bt_ent, bi & 31);
+        if (bi >= 32) blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
+                                  tok / p.block_size);
+        return blk;
+      };
+
       const int nsplit = len > 0 ? (len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
       if (s >= nsplit) continue;
-      const int t0 = s * p.chunk_tokens;
       const int t1 = min(t0 + p.chunk_tokens, len);
       const int ntiles = len > 0 ? (t1 - t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
+      // Fused slot write: the current token (position len - 1) lives in the
+      // last split's last tile; its K/V head slice is written before any of
+      // the item's tiles is requested and made visible to the async proxy.
+      if (p.new_k != nullptr && s == nsplit - 1 && ntiles > 0) {
+        const int blk = block_of(len - 1);
+        const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
+        const int64_t want =
+            blk_ok ? static_cast<int64_t>(blk) * p.block_size + (len - 1) % p.block_size : -1;
+        if (slot_new >= 0 && slot_new == want) {
+          const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
+          uint4* dst = lane < kHeadVecs ? p.k_cache_vec : p.v_cache_vec;
+          dst[static_cast<int64_t>(slot_new) * row_vecs + col] = new_row;
+          fence_proxy_async_global();
+        } else if (slot_new != -1 && leader) {
+          raise_error(NKV_DEVERR_STORE_SLOT);
+        }
+        __syncwarp();
+      }
+      // KvChat: this step's query rows of the group join the row's window.
+      if (p.ring_vec != nullptr && s == 0 && ring_slot >= 0) {
+        if (ring_slot < p.ring_slots && ring_pos >= 0 && ring_pos < p.ring_window) {
+          uint4* dst = p.ring_vec + p.ring_layer_base_vec + ring_slot * p.ring_slot_stride_vec +
+                       static_cast<int64_t>(ring_pos) * p.num_q_heads * kHeadVecs +
+                       static_cast<int64_t>(kvh) * q_vecs;
+#pragma unroll
+          for (int i = 0; i < kQVecsPerLane; ++i)
+            if (lane + 32 * i < q_vecs) dst[lane + 32 * i] = q_rows[i];
+        } else if (leader) {
+          raise_error(NKV_DEVERR_RING_RANGE);
+        }
+      }
       int j = 0;
       do {
         bool waited = true;
@@ -238,38 +354,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         if (ntiles == 0) {
           if (leader) mbar_arrive(fb);
         } else {
-          const int blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
-                                tok / p.block_size);
+          const int blk = block_of(tok);
           const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
           // fully out of range: TMA fills zeros
           const int slot = blk_ok ? blk * p.block_size + (tok % p.block_size) : -2 * kDecodeTileTokens;
           if (!blk_ok && leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
-          // Fused slot write: the current token (position len - 1) lives in
-          // this sequence's last tile; its K/V head slice is written here,
-          // made visible to the async proxy, then the tile is loaded.
-          if (p.new_k != nullptr && s == nsplit - 1 && j == ntiles - 1) {
-            const int32_t sm = __ldg(p.slot_mapping + b);
-            const int64_t want = blk_ok ? static_cast<int64_t>(blk) * p.block_size +
-                                              (len - 1) % p.block_size
-                                        : -1;
-            if (sm >= 0 && sm == want) {
-              // a 128-dim head row is 16 x 16 B: lanes 0-15 copy K, 16-31 V
-              constexpr int kHeadVecs = kDecodeHeadDim / 8;
-              const int u = lane & (kHeadVecs - 1);
-              const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + u;
-              if (lane < kHeadVecs) {
-                p.k_cache_vec[static_cast<int64_t>(sm) * row_vecs + col] =
-                    __ldg(p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col);
-              } else {
-                p.v_cache_vec[static_cast<int64_t>(sm) * row_vecs + col] =
-                    __ldg(p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
-              }
-              fence_proxy_async_global();
-            } else if (sm != -1 && leader) {
-              raise_error(NKV_DEVERR_STORE_SLOT);
-            }
-            __syncwarp();
-          }
           if (leader) {
             const uint32_t bytes = 4u * kHalfTileBytes + (j == 0 ? q_bytes : 0u);
             mbar_arrive_expect_tx(fb, bytes);
@@ -285,25 +374,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
             }
           }
           armed[stage] = phase + 1u;
-        }
-        // KvChat: this step's query rows of the group join the row's window
-        // (after the item's first tile is in flight: nothing here waits on it).
-        if (j == 0 && p.ring_vec != nullptr && s == 0) {
-          const int rs = __ldg(p.ring_slot_of_row + b);
-          if (rs >= 0) {
-            const int pos = __ldg(p.ring_pos_of_row + b);
-            if (rs < p.ring_slots && pos >= 0 && pos < p.ring_window) {
-              const int n = g * (kDecodeHeadDim / 8);  // the group's q rows, 16-byte units
-              const uint4* src = p.q_vec + static_cast<int64_t>(b) * p.q_stride_token_vec +
-                                 static_cast<int64_t>(kvh) * n;
-              uint4* dst = p.ring_vec + p.ring_layer_base_vec + rs * p.ring_slot_stride_vec +
-                           static_cast<int64_t>(pos) * p.num_q_heads * (kDecodeHeadDim / 8) +
-                           static_cast<int64_t>(kvh) * n;
-              for (int i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
-            } else if (leader) {
-              raise_error(NKV_DEVERR_RING_RANGE);
-            }
-          }
         }
         if (++stage == kStages) {
           stage = 0;
@@ -343,6 +413,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     // -------------------------------------------------------------- merger
     int slot = 0;
     uint32_t sphase = 0;
+    bool arrived = false;      // cluster mode: this CTA's lanes arrived at the leader
+    bool recv_waited = false;  // cluster mode, leader: waited for all arrivals
     const int d0 = 4 * lane;  // this lane's 4 dims
     while (true) {
       if (!mbar_wait_bounded(smem_u32(&slot_full[slot]), sphase)) {
@@ -384,12 +456,17 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
                            static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
                        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        } else if (cluster_mode) {
+          // this split's row into the leader's receive rows
+          const uint32_t dst =
+              mapa_shared(smem_u32(recv + (s * G + row) * kRecvRowFloats), 0);
+          st_cluster_f32x4(dst + 4 * d0, acc);
+          if (lane == 0) st_cluster_f32x2(dst + 4 * kDecodeHeadDim, M, L);
         } else {
           const int64_t pidx = (static_cast<int64_t>(pair) * p.max_splits + s) * g + row;
           *reinterpret_cast<float4*>(p.part_o + pidx * kDecodeHeadDim + d0) = acc;
           if (lane == 0) {
-            p.part_ml[pidx * 2 + 0] = M;
-            p.part_ml[pidx * 2 + 1] = L;
+            *reinterpret_cast<float2*>(p.part_ml + pidx * 2) = make_float2(M, L);
           }
         }
       }
@@ -397,7 +474,41 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       // hand-off so the consumers never wait on the split protocol.
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&slot_empty[slot]));
-      if (nsplit > 1) {
+      if (nsplit > 1 && cluster_mode) {
+        // Each lane releases its own stores; the leader (split 0) waits for
+        // every CTA of the cluster, then merges the splits in order.
+        mbar_arrive_cluster(mapa_shared(smem_u32(recv_bar), 0));
+        arrived = true;
+        if (s == 0) {
+          recv_waited = true;
+          if (mbar_wait_cluster_bounded(smem_u32(recv_bar), 0)) {
+            for (int row = 0; row < g; ++row) {
+              float M = NEG_INF;
+              for (int s2 = 0; s2 < nsplit; ++s2)
+                M = fmaxf(M, recv[(s2 * G + row) * kRecvRowFloats + kDecodeHeadDim]);
+              float L = 0.f;
+              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int s2 = 0; s2 < nsplit; ++s2) {
+                const float* r = recv + (s2 * G + row) * kRecvRowFloats;
+                const float ms = r[kDecodeHeadDim];
+                const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
+                L += r[kDecodeHeadDim + 1] * f;
+                const float4 po = *reinterpret_cast<const float4*>(r + d0);
+                acc.x += po.x * f;
+                acc.y += po.y * f;
+                acc.z += po.z * f;
+                acc.w += po.w * f;
+              }
+              const float inv = (L > 0.f) ? 1.f / L : 0.f;
+              store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
+                               static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
+                           make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+            }
+          } else {
+            flags[0] = 1;
+          }
+        }
+      } else if (nsplit > 1) {
         // __syncwarp orders the lanes' partial stores before lane 0's
         // gpu-scope release; the acquire half of the same atomic makes the
         // other splits' partials visible to the last arriver (and, through
@@ -412,23 +523,66 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         last = __shfl_sync(0xffffffffu, last, 0);
         __syncwarp();
         if (last) {
+          // Two rounds of loads per row: the splits' (m, l), one split per
+          // lane, then this lane's 4 dims of every split's partial O, issued
+          // eight at a time (a loop of dependent loads costs one L2 round
+          // trip per split). The sums run in split order; L is summed by a
+          // fixed butterfly, so the result is deterministic.
           for (int row = 0; row < g; ++row) {
             const int64_t base = static_cast<int64_t>(pair) * p.max_splits * g + row;
-            float M = NEG_INF;
-            for (int s2 = 0; s2 < nsplit; ++s2)
-              M = fmaxf(M, __ldcg(p.part_ml + (base + static_cast<int64_t>(s2) * g) * 2));
+            float ms0 = NEG_INF, l0 = 0.f;  // split `lane` (the first 32 splits)
+            if (lane < nsplit) {
+              const float2 ml = __ldcg(reinterpret_cast<const float2*>(
+                  p.part_ml + (base + static_cast<int64_t>(lane) * g) * 2));
+              ms0 = ml.x;
+              l0 = ml.y;
+            }
+            float M = ms0;
+            for (int c = 32; c < nsplit; c += 32)
+              if (c + lane < nsplit)
+                M = fmaxf(M, __ldcg(p.part_ml + (base + static_cast<int64_t>(c + lane) * g) * 2));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
             float L = 0.f;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s2 = 0; s2 < nsplit; ++s2) {
-              const int64_t pi = base + static_cast<int64_t>(s2) * g;
-              const float ms = __ldcg(p.part_ml + pi * 2);
-              const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
-              L += __ldcg(p.part_ml + pi * 2 + 1) * f;
-              const float4 po = __ldcg(reinterpret_cast<const float4*>(p.part_o + pi * kDecodeHeadDim + d0));
-              acc.x += po.x * f;
-              acc.y += po.y * f;
-              acc.z += po.z * f;
-              acc.w += po.w * f;
+            for (int c = 0; c < nsplit; c += 32) {
+              const int cnt = min(32, nsplit - c);
+              float ms = ms0, lw = l0;
+              if (c > 0) {
+                ms = NEG_INF;
+                lw = 0.f;
+                if (lane < cnt) {
+                  const float2 ml = __ldcg(reinterpret_cast<const float2*>(
+                      p.part_ml + (base + static_cast<int64_t>(c + lane) * g) * 2));
+                  ms = ml.x;
+                  lw = ml.y;
+                }
+              }
+              const float f = (lane < cnt && ms != NEG_INF) ? fast_exp2(ms - M) : 0.f;
+              float lf = lw * f;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) lf += __shfl_xor_sync(0xffffffffu, lf, o);
+              L += lf;
+              for (int k0 = 0; k0 < cnt; k0 += 8) {
+                float4 po[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  po[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                  if (k0 + u < cnt)
+                    po[u] = __ldcg(reinterpret_cast<const float4*>(
+                        p.part_o + (base + static_cast<int64_t>(c + k0 + u) * g) * kDecodeHeadDim + d0));
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const float fu = __shfl_sync(0xffffffffu, f, (k0 + u) & 31);
+                  if (k0 + u < cnt) {
+                    acc.x += po[u].x * fu;
+                    acc.y += po[u].y * fu;
+                    acc.z += po[u].z * fu;
+                    acc.w += po[u].w * fu;
+                  }
+                }
+              }
             }
             const float inv = (L > 0.f) ? 1.f / L : 0.f;
             store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
@@ -442,6 +596,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         sphase ^= 1u;
       }
     }
+    if (cluster_mode) {
+      // Every CTA arrives exactly once: here if its split was empty or its
+      // row unsplit. The leader stays until all have arrived, since their
+      // arrivals (and partials) address its shared memory.
+      if (!arrived) mbar_arrive_cluster(mapa_shared(smem_u32(recv_bar), 0));
+      if (cluster_ctarank() == 0 && !recv_waited) mbar_wait_cluster_bounded(smem_u32(recv_bar), 0);
+    }
     return;
   }
 
@@ -451,8 +612,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   const int tig = lane & 3;
   const float scale_log2 = p.scale_log2;
 
+  // Group widths up to 8 compute the transposed products, S^T = K Q^T and
+  // O^T = V^T P^T: the tokens (or dims) fill the 16 rows of each mma.sync
+  // tile and the g heads its 8 columns, so a 2- to 8-head group costs half
+  // the tensor-core instructions of the Q-on-rows form (whose 16 rows would
+  // carry g heads). P^T reaches the B operand through movmatrix.
+  constexpr bool kSwapAB = G <= 8;
   float o[16][4];
-  float m_run[2], l_run[2];
+  float m_run[2], l_run[2];  // swap form: heads 2 tig + e; else rows gid (+ 8)
   uint32_t qa[8][4];
 
   int stage = 0;
@@ -466,7 +633,31 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       flags[0] = 1;
       return false;
     }
-    if (item >= 0) {
+    if (item >= 0 && kSwapAB) {
+      // o[dm][c]: O^T rows dims 16 dm + gid (c 0, 1) and + 8 (c 2, 3),
+      // columns heads 2 tig (c even) and 2 tig + 1 (c odd)
+      float* so = slot_o(cslot);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float l = l_run[e];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        const int h = 2 * tig + e;
+        if (h < g) {
+          if (gid == 0) {
+            slot_m(cslot)[cw * G + h] = m_run[e];
+            slot_l(cslot)[cw * G + h] = l;
+          }
+          float* dst = so + (cw * G + h) * S::kORowStride;
+#pragma unroll
+          for (int dm = 0; dm < 8; ++dm) {
+            dst[16 * dm + gid] = o[dm][e];
+            dst[16 * dm + 8 + gid] = o[dm][2 + e];
+          }
+        }
+      }
+    } else if (item >= 0) {
       constexpr int kRowSets = (G == 16) ? 2 : 1;
       float* so = slot_o(cslot);
 #pragma unroll
@@ -547,7 +738,99 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     }
 
     const int tok_base = cw * 32;
-    if (ntiles > 0 && tok_base < nvalid) {
+    if (kSwapAB && ntiles > 0 && tok_base < nvalid) {
+      const uint32_t sK0 = smem_u32(sbase);
+      const uint32_t sK1 = sK0 + kHalfTileBytes;
+      const uint32_t sV0 = sK0 + 2 * kHalfTileBytes;
+      const uint32_t sV1 = sK0 + 3 * kHalfTileBytes;
+      const int mi = lane >> 3;
+      // S^T = K Q^T: two 16-token m-tiles x 8 head columns, 8 k-steps of 16 dims
+      float sacc[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) sacc[mt][0] = sacc[mt][1] = sacc[mt][2] = sacc[mt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t sK = (kk < 4) ? sK0 : sK1;
+        const uint32_t c = 2u * (kk & 3) + static_cast<uint32_t>(mi >> 1);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const uint32_t r = tok_base + 16 * mt + (mi & 1) * 8 + (lane & 7);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(sK + swz128(r, c), a0, a1, a2, a3);
+          mma_bf16_16816(sacc[mt], a0, a1, a2, a3, qa[kk][0], qa[kk][2]);
+        }
+      }
+      // online softmax per head (column 2 tig + e) over this warp's tokens
+      const bool partial = (tok_base + 32 > nvalid);
+      float mx[2] = {NEG_INF, NEG_INF};
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v = sacc[mt][c] * scale_log2;
+          const int tk = tok_base + 16 * mt + 8 * (c >> 1) + gid;
+          if (partial && tk >= nvalid) v = NEG_INF;
+          sacc[mt][c] = v;
+          mx[c & 1] = fmaxf(mx[c & 1], v);
+        }
+      }
+      float alpha[2], m_use[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+        const float m_new = fmaxf(m_run[e], mx[e]);
+        m_use[e] = (m_new == NEG_INF) ? 0.f : m_new;
+        alpha[e] = fast_exp2(m_run[e] - m_use[e]);
+        m_run[e] = m_new;
+      }
+      float rsum[2] = {0.f, 0.f};
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float pv = fast_exp2(sacc[mt][c] - m_use[c & 1]);
+          sacc[mt][c] = pv;
+          rsum[c & 1] += pv;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) l_run[e] = l_run[e] * alpha[e] + rsum[e];
+#pragma unroll
+      for (int dm = 0; dm < 8; ++dm) {
+        o[dm][0] *= alpha[0];
+        o[dm][1] *= alpha[1];
+        o[dm][2] *= alpha[0];
+        o[dm][3] *= alpha[1];
+      }
+      // O^T += V^T P^T: 8 m-tiles of 16 dims, two 16-token k-steps
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const uint32_t b0 = movmatrix_trans(pack_bf16x2(sacc[jj][0], sacc[jj][1]));
+        const uint32_t b1 = movmatrix_trans(pack_bf16x2(sacc[jj][2], sacc[jj][3]));
+        uint32_t mask_lo = 0xffffffffu, mask_hi = 0xffffffffu;
+        if (partial) {
+          const int ta = tok_base + 16 * jj + 2 * tig;
+          mask_lo = (ta < nvalid ? 0x0000ffffu : 0u) | (ta + 1 < nvalid ? 0xffff0000u : 0u);
+          mask_hi = (ta + 8 < nvalid ? 0x0000ffffu : 0u) | (ta + 9 < nvalid ? 0xffff0000u : 0u);
+        }
+        const uint32_t r = tok_base + 16 * jj + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int dm = 0; dm < 8; ++dm) {
+          const uint32_t c16 = 2 * dm + (mi >> 1);
+          const uint32_t addr = ((c16 < 8) ? sV0 : sV1) + swz128(r, c16 & 7u);
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_trans(addr, v0, v1, v2, v3);
+          // v0 / v1: tokens 0-7 / 8-15 of dims 16 dm..+7; v2 / v3: dims +8
+          v0 &= mask_lo;
+          v2 &= mask_lo;
+          v1 &= mask_hi;
+          v3 &= mask_hi;
+          mma_bf16_16816(o[dm], v0, v2, v1, v3, b0, b1);
+        }
+      }
+    } else if (!kSwapAB && ntiles > 0 && tok_base < nvalid) {
       const uint32_t sK0 = smem_u32(sbase);
       const uint32_t sK1 = sK0 + kHalfTileBytes;
       const uint32_t sV0 = sK0 + 2 * kHalfTileBytes;
