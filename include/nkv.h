@@ -49,7 +49,7 @@ typedef enum nkv_status {
 
 /* Bits of the sticky device error word. */
 #define NKV_DEVERR_STORE_SLOT      0x1u  /* slot_mapping entry outside [-1, num_slots) */
-#define NKV_DEVERR_DECODE_BLOCK    0x2u  /* block_tables entry outside [0, num_blocks) on a live token */
+#define NKV_DEVERR_DECODE_BLOCK    0x2u  /* block_tables entry outside [0, num_blocks) on a live token, or a context length past max_blocks * block_size (clamped) */
 #define NKV_DEVERR_WAIT_TIMEOUT    0x4u  /* a bounded mbarrier / cluster wait gave up */
 #define NKV_DEVERR_COMPRESS_RANGE  0x8u  /* compression window or slot outside the cache */
 #define NKV_DEVERR_RING_RANGE      0x10u /* query-window ring slot / position out of range */

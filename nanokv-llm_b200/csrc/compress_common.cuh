@@ -13,24 +13,28 @@ namespace cg = cooperative_groups;
 constexpr int kCompressThreads = 256;
 constexpr int kCompressWarps = kCompressThreads / 32;
 constexpr int kCompressHeadDim = 128;
-constexpr int kCompactChunkRows = 64;
 constexpr int kMaxWindowBlocks = 64;
 constexpr int kReduceSlots = 16 * kCompressWarps;  // floats/ints of scratch for reductions
 
 // ---------------------------------------------------------------- block helpers
+// kThreads: the block size (a multiple of 32); `red` holds >= kThreads / 32
+// values (16 * kThreads / 32 for block_reduce_vec).
+template <int kThreads = kCompressThreads>
 __device__ __forceinline__ int block_sum_int(int v, int* red) {
+  constexpr int kWarps = kThreads / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = __reduce_add_sync(0xffffffffu, v);
   if (lane == 0) red[warp] = v;
   __syncthreads();
   int tot = 0;
 #pragma unroll
-  for (int w = 0; w < kCompressWarps; ++w) tot += red[w];
+  for (int w = 0; w < kWarps; ++w) tot += red[w];
   __syncthreads();
   return tot;
 }
 
 // Exclusive prefix sum over threads in index order.
+template <int kThreads = kCompressThreads>
 __device__ __forceinline__ int block_excl_scan(int v, int* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
@@ -48,8 +52,9 @@ __device__ __forceinline__ int block_excl_scan(int v, int* red) {
 }
 
 // In-place block-wide max (kMax) or sum over each of N per-thread values.
-template <int N, bool kMax>
+template <int N, bool kMax, int kThreads = kCompressThreads>
 __device__ __forceinline__ void block_reduce_vec_impl(float (&v)[N], float* red) {
+  constexpr int kWarps = kThreads / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int r = 0; r < N; ++r) {
@@ -58,15 +63,15 @@ __device__ __forceinline__ void block_reduce_vec_impl(float (&v)[N], float* red)
       const float x = __shfl_xor_sync(0xffffffffu, v[r], o);
       v[r] = kMax ? fmaxf(v[r], x) : v[r] + x;
     }
-    if (lane == 0) red[r * kCompressWarps + warp] = v[r];
+    if (lane == 0) red[r * kWarps + warp] = v[r];
   }
   __syncthreads();
 #pragma unroll
   for (int r = 0; r < N; ++r) {
-    float a = red[r * kCompressWarps];
+    float a = red[r * kWarps];
 #pragma unroll
-    for (int w = 1; w < kCompressWarps; ++w) {
-      const float x = red[r * kCompressWarps + w];
+    for (int w = 1; w < kWarps; ++w) {
+      const float x = red[r * kWarps + w];
       a = kMax ? fmaxf(a, x) : a + x;
     }
     v[r] = a;
@@ -139,6 +144,7 @@ __device__ __forceinline__ void radix_pick_bin(const int* hist, int need, int* o
 // high byte: two histogram passes instead of a 16-round bitwise search);
 // then each thread, owning a contiguous index range, emits its keys above
 // the cut and, in index order, the first (k - above) keys equal to it.
+template <int kThreads = kCompressThreads>
 __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int* red, int* hist) {
   __shared__ int s_bin, s_above;
   if (k <= 0) {
@@ -148,9 +154,9 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
   uint32_t prefix = 0;
   int above = 0;
   for (int pass = 0; pass < 2; ++pass) {
-    for (int i = threadIdx.x; i < 256; i += kCompressThreads) hist[i] = 0;
+    for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
     __syncthreads();
-    for (int t = threadIdx.x; t < n; t += kCompressThreads) {
+    for (int t = threadIdx.x; t < n; t += kThreads) {
       const uint32_t key = keys[t];
       if (pass == 0) {
         atomicAdd(&hist[key >> 8], 1);
@@ -166,13 +172,13 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
     __syncthreads();  // s_bin / s_above are rewritten by the next pass
   }
   // prefix is now the k-th largest key; `above` keys are larger.
-  const int per = (n + kCompressThreads - 1) / kCompressThreads;
+  const int per = (n + kThreads - 1) / kThreads;
   const int lo = threadIdx.x * per;
   const int hi = min(lo + per, n);
   const int need_eq = k - above;
   int eq = 0;
   for (int t = lo; t < hi; ++t) eq += (keys[t] == prefix) ? 1 : 0;
-  const int eq_before = block_excl_scan(eq, red);
+  const int eq_before = block_excl_scan<kThreads>(eq, red);
   int kept = 0;
   {
     int e = eq_before;
@@ -182,7 +188,7 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
       e += is_eq ? 1 : 0;
     }
   }
-  int pos = block_excl_scan(kept, red);
+  int pos = block_excl_scan<kThreads>(kept, red);
   {
     int e = eq_before;
     for (int t = lo; t < hi; ++t) {
@@ -195,7 +201,8 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
 }
 
 // Moves rows src(i) -> dst(i), i in [0, n), of this CTA's kv-head slice (256
-// bytes of K and of V per row), 64 rows per chunk, with the reads of chunk
+// bytes of K and of V per row), kThreads / 4 rows per chunk (4 threads per
+// row), with the reads of chunk
 // c+1 overlapping the writes of chunk c. Safe for in-place compaction when
 // source index(i) >= i and destinations are the window's positions 0..n-1:
 //   * every source of a chunk lies at or beyond its own first destination,
@@ -204,11 +211,12 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
 //   * a chunk's sources may lie in the NEXT chunk's destination range, so a
 //     barrier separates the reads of chunk c from the writes of chunk c+1.
 // Rows with src == dst or an unresolved slot (< 0) are skipped.
-template <typename SlotFn>
+template <int kThreads = kCompressThreads, typename SlotFn>
 __device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
                                        int num_kv_heads, int head, int n, SlotFn slots) {
+  constexpr int kChunkRows = kThreads / 4;
   const int t = threadIdx.x;
-  const int row = t >> 2;      // 64 rows x 4 threads
+  const int row = t >> 2;      // kChunkRows rows x 4 threads
   const int quarter = t & 3;   // 4 x 64 bytes of a 256-byte head row
   auto kptr = [&](int64_t slot) {
     return reinterpret_cast<uint4*>(k_cache + (slot * num_kv_heads + head) * kCompressHeadDim) +
@@ -236,8 +244,8 @@ __device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_
     }
   }
   __syncthreads();
-  for (int base = 0; base < n; base += kCompactChunkRows) {
-    const int i = base + kCompactChunkRows + row;
+  for (int base = 0; base < n; base += kChunkRows) {
+    const int i = base + kChunkRows + row;
     uint4 kn[4], vn[4];
     int64_t dst_n = -1;
     if (i < n) {

@@ -301,12 +301,13 @@ int padded_group(int g) {
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
-// Launches `kernel` with clusters of cluster_x CTAs along x. `smem_set` is
+// Launches `kernel` (blocks of `threads`) with clusters of cluster_x CTAs
+// along x. `smem_set` is
 // the caller's per-kernel record of the dynamic shared-memory limit already
 // granted on each device; the limit is raised only when a call needs more.
 template <typename Kernel, typename Params>
-int launch_cluster(Kernel kernel, size_t* smem_set, const Params& p, int cluster_x, int grid_y,
-                   size_t smem, cudaStream_t stream) {
+int launch_cluster(Kernel kernel, int threads, size_t* smem_set, const Params& p, int cluster_x,
+                   int grid_y, size_t smem, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices || smem > smem_set[dev]) {
@@ -317,7 +318,7 @@ int launch_cluster(Kernel kernel, size_t* smem_set, const Params& p, int cluster
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster_x, grid_y, 1);
-  cfg.blockDim = dim3(nkv::kCompressThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -334,8 +335,8 @@ template <int G>
 int launch_threshold(const nkv::ThresholdCompressParams& p, int cluster_x, int grid_y,
                      size_t smem, cudaStream_t stream) {
   static size_t smem_set[kMaxDevices] = {0};
-  return launch_cluster(nkv::threshold_compress_kernel<G>, smem_set, p, cluster_x, grid_y, smem,
-                        stream);
+  return launch_cluster(nkv::threshold_compress_kernel<G>, nkv::kThrThreads, smem_set, p,
+                        cluster_x, grid_y, smem, stream);
 }
 
 template <int G>
@@ -1077,6 +1078,8 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
     return NKV_ERR_INVALID_ARGUMENT;
   if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return NKV_ERR_INVALID_ARGUMENT;
   if (head_dim != nkv::kCompressHeadDim || num_kv_heads > 8 || block_size <= 0) return NKV_ERR_UNSUPPORTED;
+  // key slots are held as 32-bit ints
+  if (num_blocks < 0 || num_blocks * static_cast<int64_t>(block_size) > INT32_MAX) return NKV_ERR_UNSUPPORTED;
   const int g = num_q_heads / num_kv_heads;
   const int W = window_size;
   const int num_keep = compress_R - W - 1;
@@ -1112,9 +1115,9 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
   p.mtiles = (p.rows + 15) / 16;
   const int G = padded_group(g);
   if (G == 0) return NKV_ERR_UNSUPPORTED;
-  // As many 16-row m-tiles per row group as shared memory (and the 8 warps)
-  // allow; more groups re-stream the keys from L2.
-  int gm = std::min(p.mtiles, nkv::kCompressWarps);
+  // As many 16-row m-tiles per row group as shared memory (and two warps
+  // per m-tile) allow; more groups re-stream the keys from L2.
+  int gm = std::min(p.mtiles, nkv::kThrWarps / 2);
   while (gm > 0 && nkv::threshold_smem_bytes(G, p.keys_pad, gm, compress_R) > kMaxSmem) --gm;
   if (gm == 0) return NKV_ERR_UNSUPPORTED;
   p.group_mtiles = gm;

@@ -106,20 +106,21 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   return r;
 }
 
-__device__ __forceinline__ void st_cluster_f32x4(uint32_t addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
-               "f"(v.z), "f"(v.w)
-               : "memory");
+// Asynchronous store into the shared memory of a CTA of the cluster; its
+// bytes count towards the transaction count of that CTA's mbarrier `bar`
+// (both addresses from mapa_shared), whose completion makes them visible.
+__device__ __forceinline__ void st_async_f32x4(uint32_t addr, float4 v, uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          addr),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+      : "memory");
 }
 
-__device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
-}
-
-// Arrive on an mbarrier of any CTA of the cluster (address from mapa_shared),
-// releasing this thread's earlier writes at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float a, float b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   addr),
+               "f"(a), "f"(b), "r"(bar)
                : "memory");
 }
 
@@ -224,6 +225,22 @@ __device__ __forceinline__ unsigned int atomic_add_acq_rel_gpu(unsigned int* p, 
   unsigned int old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
+}
+
+// Read-only global loads issued in program order (volatile: the compiler
+// neither drops nor reorders them against each other), so a round of
+// independent loads is in flight together before the first use.
+__device__ __forceinline__ int ldg_nc_s32(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_nc_v4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 // 16-byte global -> shared asynchronous copy (L2 only) and its group fences.

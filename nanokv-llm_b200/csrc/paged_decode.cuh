@@ -176,8 +176,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       mbar_init(smem_u32(&slot_full[s]), kDecodeConsumerWarps * 32);
       mbar_init(smem_u32(&slot_empty[s]), 1);
     }
-    // every CTA's merger lanes arrive once on the leader's receive barrier
-    if (cluster_mode) mbar_init(smem_u32(recv_bar), 32 * csize);
+    // the leader's receive barrier: its own arrival (with the expected
+    // bytes) plus the splits' asynchronous stores
+    if (cluster_mode) mbar_init(smem_u32(recv_bar), 1);
     flags[0] = 0;
     fence_barrier_init();
   }
@@ -187,7 +188,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     prefetch_tmap(&tm_q);
   }
   __syncthreads();
-  // No CTA arrives on the leader's receive barrier before it is initialised.
+  // No CTA stores to the leader's receive rows before its barrier exists.
   if (cluster_mode) cluster_sync_all();
   // Launched with programmatic stream serialisation: everything above
   // overlapped the previous kernel (typically the previous layer's decode);
@@ -252,24 +253,23 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       // rows (KvChat query window).
       int scalar = 0;
       if (lane == 0) {
-        scalar = __ldg(p.context_lens + b);
+        scalar = ldg_nc_s32(p.context_lens + b);
       } else if (lane == 1) {
-        scalar = p.new_k != nullptr ? __ldg(p.slot_mapping + b) : -1;
+        scalar = p.new_k != nullptr ? ldg_nc_s32(p.slot_mapping + b) : -1;
       } else if (lane == 2 || lane == 3) {
         if (p.ring_vec != nullptr && s == 0)
-          scalar = __ldg((lane == 2 ? p.ring_slot_of_row : p.ring_pos_of_row) + b);
+          scalar = ldg_nc_s32((lane == 2 ? p.ring_slot_of_row : p.ring_pos_of_row) + b);
       }
-      const int bt_ent = blk_first + lane < p.max_blocks
-                             ? __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
-                                     blk_first + lane)
-                             : -1;
+      int bt_ent = -1;
+      if (blk_first + lane < p.max_blocks)
+        bt_ent = ldg_nc_s32(p.block_tables + static_cast<int64_t>(b) * p.max_blocks + blk_first + lane);
       constexpr int kHeadVecs = kDecodeHeadDim / 8;  // 16-byte units of one head row
       uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
       if (p.new_k != nullptr) {
         // lanes 0-15: the K head row, 16-31: the V head row
         const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
-        new_row = lane < kHeadVecs ? __ldg(p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col)
-                                   : __ldg(p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
+        new_row = ldg_nc_v4(lane < kHeadVecs ? p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col
+                                             : p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
       }
       constexpr int kQVecsPerLane = G >= 2 ? G / 2 : 1;
       const int q_vecs = g * kHeadVecs;  // the group's q rows
@@ -279,9 +279,15 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                            static_cast<int64_t>(kvh) * q_vecs;
 #pragma unroll
         for (int i = 0; i < kQVecsPerLane; ++i)
-          if (lane + 32 * i < q_vecs) q_rows[i] = __ldg(src + lane + 32 * i);
+          if (lane + 32 * i < q_vecs) q_rows[i] = ldg_nc_v4(src + lane + 32 * i);
       }
-      const int len = __shfl_sync(0xffffffffu, scalar, 0);
+      int len = __shfl_sync(0xffffffffu, scalar, 0);
+      // a length past the row's block table is clamped (and flagged) so that
+      // no block-table read leaves the row
+      if (len > p.max_blocks * p.block_size) {
+        if (leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
+        len = p.max_blocks * p.block_size;
+      }
       const int slot_new = __shfl_sync(0xffffffffu, scalar, 1);
       const int ring_slot = __shfl_sync(0xffffffffu, scalar, 2);
       const int ring_pos = __shfl_sync(0xffffffffu, scalar, 3);
@@ -413,8 +419,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     // -------------------------------------------------------------- merger
     int slot = 0;
     uint32_t sphase = 0;
-    bool arrived = false;      // cluster mode: this CTA's lanes arrived at the leader
-    bool recv_waited = false;  // cluster mode, leader: waited for all arrivals
     const int d0 = 4 * lane;  // this lane's 4 dims
     while (true) {
       if (!mbar_wait_bounded(smem_u32(&slot_full[slot]), sphase)) {
@@ -457,11 +461,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                            static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
                        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
         } else if (cluster_mode) {
-          // this split's row into the leader's receive rows
+          // this split's row into the leader's receive rows, counted on its
+          // receive barrier (nothing to wait for here)
           const uint32_t dst =
               mapa_shared(smem_u32(recv + (s * G + row) * kRecvRowFloats), 0);
-          st_cluster_f32x4(dst + 4 * d0, acc);
-          if (lane == 0) st_cluster_f32x2(dst + 4 * kDecodeHeadDim, M, L);
+          const uint32_t rbar = mapa_shared(smem_u32(recv_bar), 0);
+          st_async_f32x4(dst + 4 * d0, acc, rbar);
+          if (lane == 0) st_async_f32x2(dst + 4 * kDecodeHeadDim, M, L, rbar);
         } else {
           const int64_t pidx = (static_cast<int64_t>(pair) * p.max_splits + s) * g + row;
           *reinterpret_cast<float4*>(p.part_o + pidx * kDecodeHeadDim + d0) = acc;
@@ -475,12 +481,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&slot_empty[slot]));
       if (nsplit > 1 && cluster_mode) {
-        // Each lane releases its own stores; the leader (split 0) waits for
-        // every CTA of the cluster, then merges the splits in order.
-        mbar_arrive_cluster(mapa_shared(smem_u32(recv_bar), 0));
-        arrived = true;
+        // The leader (split 0) expects every split's rows, waits for them to
+        // land, then merges the splits in order. Splits past the row's end
+        // send nothing and are not expected.
         if (s == 0) {
-          recv_waited = true;
+          if (lane == 0)
+            mbar_arrive_expect_tx(smem_u32(recv_bar),
+                                  static_cast<uint32_t>(nsplit * g * (4 * kDecodeHeadDim + 8)));
           if (mbar_wait_cluster_bounded(smem_u32(recv_bar), 0)) {
             for (int row = 0; row < g; ++row) {
               float M = NEG_INF;
@@ -595,13 +602,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         slot = 0;
         sphase ^= 1u;
       }
-    }
-    if (cluster_mode) {
-      // Every CTA arrives exactly once: here if its split was empty or its
-      // row unsplit. The leader stays until all have arrived, since their
-      // arrivals (and partials) address its shared memory.
-      if (!arrived) mbar_arrive_cluster(mapa_shared(smem_u32(recv_bar), 0));
-      if (cluster_ctarank() == 0 && !recv_waited) mbar_wait_cluster_bounded(smem_u32(recv_bar), 0);
     }
     return;
   }

@@ -85,9 +85,15 @@ struct ThresholdCompressParams {
   int keys_pad;   // num_keys rounded up to kThrKeyTile
   int rows;       // g * W
   int mtiles;     // ceil(rows / 16)
-  int group_mtiles;  // m-tiles per row group (<= kCompressWarps)
+  int group_mtiles;  // m-tiles per row group (<= kThrWarps / 2)
 };
 
+// 16 warps: two per 16-row m-tile in the scoring, and enough threads that
+// the per-key window sums (one thread per key and head) and the row
+// statistics hide their exp / divide latency.
+constexpr int kThrThreads = 512;
+constexpr int kThrWarps = kThrThreads / 32;
+constexpr int kThrReduceSlots = 16 * kThrWarps;
 constexpr int kThrKeyTile = 64;
 constexpr int kThrKRowElems = kCompressHeadDim + 8;  // padded smem row: conflict-free ldmatrix
 
@@ -104,12 +110,13 @@ __host__ __device__ constexpr size_t threshold_smem_bytes(int G, int keys_pad, i
          + sizeof(float) * keys_pad                                              // partial
          + sizeof(uint16_t) * (keys_pad + 2)                                     // keys
          + sizeof(int) * R                                                       // final index
-         + sizeof(float) * kReduceSlots                                          // reductions
-         + sizeof(int) * 256;                                                    // top-k histogram
+         + sizeof(float) * kThrReduceSlots                                       // reductions
+         + sizeof(int) * 256                                                     // top-k histogram
+         + sizeof(int) * keys_pad;                                               // key slots
 }
 
 template <int G>
-__global__ void __launch_bounds__(kCompressThreads, 1)
+__global__ void __launch_bounds__(kThrThreads, 1)
 threshold_compress_kernel(const ThresholdCompressParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   cg::cluster_group cluster = cg::this_cluster();
@@ -132,8 +139,9 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   float* partial = kacc + G * kp;                                           // [kp]
   uint16_t* keys = reinterpret_cast<uint16_t*>(partial + kp);               // [kp]
   int* final_idx = reinterpret_cast<int*>(keys + kp + 2);                   // [R]
-  float* red = reinterpret_cast<float*>(final_idx + p.R);                   // [kReduceSlots]
-  int* hist = reinterpret_cast<int*>(red + kReduceSlots);                   // [256]
+  float* red = reinterpret_cast<float*>(final_idx + p.R);                   // [kThrReduceSlots]
+  int* hist = reinterpret_cast<int*>(red + kThrReduceSlots);                // [256]
+  int* kslot = hist + 256;                                                  // [kp] cache slot of key t
   __shared__ int s_valid;
   __shared__ int s_start;
 
@@ -166,7 +174,10 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     if (!valid && head == 0) raise_error(NKV_DEVERR_COMPRESS_RANGE);
     s_valid = valid;
   }
-  for (int i = threadIdx.x; i < G * kp; i += kCompressThreads) kacc[i] = 0.f;
+  for (int i = threadIdx.x; i < G * kp; i += kThrThreads) kacc[i] = 0.f;
+  // every key's cache slot, resolved once (-1: unresolved or padding)
+  for (int t = threadIdx.x; t < kp; t += kThrThreads)
+    kslot[t] = t < nk ? static_cast<int>(slot_of(t)) : -1;
   __syncthreads();
   const bool valid = s_valid != 0;
   const int start = s_start;
@@ -185,11 +196,11 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     };
     auto load_ktile = [&](int tile, int buf) {
       const uint32_t base = smem_u32(ktile + buf * kThrKeyTile * kThrKRowElems);
-      for (int i = threadIdx.x; i < kThrKeyTile * 16; i += kCompressThreads) {
+      for (int i = threadIdx.x; i < kThrKeyTile * 16; i += kThrThreads) {
         const int kr = i >> 4, c = i & 15;
         const int t = tile * kThrKeyTile + kr;
         const uint32_t dst = base + (kr * kThrKRowElems + c * 8) * 2;
-        const int64_t slot = (t < nk) ? slot_of(t) : -1;
+        const int64_t slot = kslot[t];
         if (slot >= 0) {
           cp_async_16(dst, p.k_cache + (slot * p.num_kv_heads + head) * kCompressHeadDim + c * 8);
         } else {
@@ -203,12 +214,15 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     for (int group0 = 0; group0 < p.mtiles; group0 += p.group_mtiles) {
       const int gm = min(p.group_mtiles, p.mtiles - group0);
       const int row0 = group0 * 16;
-      // ---- A: scores of this row group
+      // ---- A: scores of this row group; warps 2m and 2m + 1 take m-tile m,
+      // each half of every key tile's eight 8-key columns
       uint32_t qa[8][4];
-      const bool mma_warp = warp < gm;
+      const int mt = warp >> 1;
+      const int nt0 = (warp & 1) * (kThrKeyTile / 16);
+      const bool mma_warp = mt < gm;
       if (mma_warp) {
-        const __nv_bfloat16* q_lo = qrow(row0 + warp * 16 + gid);
-        const __nv_bfloat16* q_hi = qrow(row0 + warp * 16 + gid + 8);
+        const __nv_bfloat16* q_lo = qrow(row0 + mt * 16 + gid);
+        const __nv_bfloat16* q_hi = qrow(row0 + mt * 16 + gid + 8);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const int d = kk * 16 + 2 * tig;
@@ -230,9 +244,9 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
         __syncthreads();
         if (mma_warp) {
           const uint32_t kb = smem_u32(ktile + buf * kThrKeyTile * kThrKRowElems);
-          const int lrow = warp * 16 + gid;
+          const int lrow = mt * 16 + gid;
 #pragma unroll
-          for (int nt = 0; nt < kThrKeyTile / 8; ++nt) {
+          for (int nt = nt0; nt < nt0 + kThrKeyTile / 16; ++nt) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int kq = 0; kq < 4; ++kq) {
@@ -261,7 +275,7 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
       }
       // ---- B: per-row max and sum of exp
       const int grows = min(gm * 16, p.rows - row0);
-      for (int lr = warp; lr < grows; lr += kCompressWarps) {
+      for (int lr = warp; lr < grows; lr += kThrWarps) {
         const __nv_bfloat16* row = sc + static_cast<size_t>(lr) * ss;
         float m = -INFINITY;
         for (int t = lane; t < nk; t += 32) m = fmaxf(m, __bfloat162float(row[t]));
@@ -277,28 +291,29 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
         }
       }
       __syncthreads();
-      // ---- C: per key, window-ordered sum of each head's bf16 probabilities.
-      // A head's rows in this group are summed in a register, continuing the
-      // head's running sum from earlier groups (the same fp32 additions in the
-      // same order as one sequential sum); the exponentials and divisions of
-      // successive rows do not depend on each other and overlap.
-      for (int t = threadIdx.x; t < nk; t += kCompressThreads) {
-        int lr = 0;
-        while (lr < grows) {
-          const int r = (row0 + lr) / W;
-          const int lr_end = min(grows, (r + 1) * W - row0);
-          float acc = kacc[r * kp + t];
+      // ---- C: per (key, head), window-ordered sum of the head's bf16
+      // probabilities. A head's rows in this group are summed in a register,
+      // continuing the head's running sum from earlier groups (the same fp32
+      // additions in the same order as one sequential sum); the exponentials
+      // and divisions of successive rows do not depend on each other and
+      // overlap.
+      const int r_first = row0 / W;
+      const int ntask = ((row0 + grows - 1) / W - r_first + 1) * nk;
+      for (int task = threadIdx.x; task < ntask; task += kThrThreads) {
+        const int r = r_first + task / nk;
+        const int t = task - (r - r_first) * nk;
+        const int lr_end = min(grows, (r + 1) * W - row0);
+        float acc = kacc[r * kp + t];
 #pragma unroll 4
-          for (; lr < lr_end; ++lr) {
-            const float e = expf(__bfloat162float(sc[static_cast<size_t>(lr) * ss + t]) - rmax[lr]);
-            acc += round_bf16(e / rsum[lr]);
-          }
-          kacc[r * kp + t] = acc;
+        for (int lr = max(r * W - row0, 0); lr < lr_end; ++lr) {
+          const float e = expf(__bfloat162float(sc[static_cast<size_t>(lr) * ss + t]) - rmax[lr]);
+          acc += round_bf16(e / rsum[lr]);
         }
+        kacc[r * kp + t] = acc;
       }
       __syncthreads();
     }
-    for (int t = threadIdx.x; t < kp; t += kCompressThreads) {
+    for (int t = threadIdx.x; t < kp; t += kThrThreads) {
       float s = 0.f;
       if (t < nk) {
 #pragma unroll
@@ -311,7 +326,7 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   cluster.sync();
   if (valid) {
     const int nranks = static_cast<int>(cluster.num_blocks());
-    for (int t = threadIdx.x; t < kp; t += kCompressThreads) {
+    for (int t = threadIdx.x; t < kp; t += kThrThreads) {
       float s = 0.f;
       for (int c = 0; c < nranks; ++c) s += cluster.map_shared_rank(partial, c)[t];
       keys[t] = (t < nk) ? static_cast<uint16_t>(bf16_key(s)) : 0;
@@ -324,11 +339,11 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
 
   const int num_keep = p.R - W - 1;
   if (threadIdx.x == 0) final_idx[0] = 0;
-  topk_ascending(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red), hist);
-  for (int i = threadIdx.x; i < W; i += kCompressThreads) final_idx[1 + num_keep + i] = p.S - W + i;
+  topk_ascending<kThrThreads>(keys, nk, num_keep, final_idx + 1, reinterpret_cast<int*>(red), hist);
+  for (int i = threadIdx.x; i < W; i += kThrThreads) final_idx[1 + num_keep + i] = p.S - W + i;
   __syncthreads();
 
-  compact_rows_pipelined(p.k_cache, p.v_cache, p.num_kv_heads, head, p.R,
+  compact_rows_pipelined<kThrThreads>(p.k_cache, p.v_cache, p.num_kv_heads, head, p.R,
                          [&](int i, int64_t& src, int64_t& dst) {
                            src = slot_of(start + final_idx[i]);
                            dst = slot_of(i);
@@ -336,7 +351,7 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   if (head == 0) {
     if (threadIdx.x == 0) p.context_lens[b] = p.R;
     if (p.out_keep_idx) {
-      for (int i = threadIdx.x; i < p.R; i += kCompressThreads)
+      for (int i = threadIdx.x; i < p.R; i += kThrThreads)
         p.out_keep_idx[static_cast<int64_t>(sel_i) * p.R + i] = final_idx[i];
     }
   }
