@@ -529,12 +529,87 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         __syncwarp();
-        if (last) {
-          // Two rounds of loads per row: the splits' (m, l), one split per
-          // lane, then this lane's 4 dims of every split's partial O, issued
-          // eight at a time (a loop of dependent loads costs one L2 round
-          // trip per split). The sums run in split order; L is summed by a
-          // fixed butterfly, so the result is deterministic.
+        if (last && G <= 8 && nsplit <= 32) {
+          // All rows at once, in two rounds of loads: every row's (m, l) of
+          // split `lane`, then this lane's 4 dims of the rows' partial O,
+          // 16 loads in flight per batch (a loop of dependent loads costs an
+          // L2 round trip each, and the last arriver's merge is on the
+          // launch's tail). The sums run in split order; M and L are
+          // reduced by fixed butterflies, so the result is deterministic.
+          constexpr int kRows = G <= 8 ? G : 8;
+          constexpr int kB = 16 / kRows;  // splits per batch
+          const int64_t base0 = static_cast<int64_t>(pair) * p.max_splits * g;
+          float f_r[kRows], inv_r[kRows];
+          {
+            float ms_r[kRows], l_r[kRows];
+#pragma unroll
+            for (int row = 0; row < kRows; ++row) {
+              ms_r[row] = NEG_INF;
+              l_r[row] = 0.f;
+              if (row < g && lane < nsplit) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(
+                    p.part_ml + (base0 + row + static_cast<int64_t>(lane) * g) * 2));
+                ms_r[row] = ml.x;
+                l_r[row] = ml.y;
+              }
+            }
+#pragma unroll
+            for (int row = 0; row < kRows; ++row) {
+              float M = ms_r[row];
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+              const float f = (ms_r[row] != NEG_INF) ? fast_exp2(ms_r[row] - M) : 0.f;
+              float lf = l_r[row] * f;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) lf += __shfl_xor_sync(0xffffffffu, lf, o);
+              f_r[row] = f;
+              inv_r[row] = (lf > 0.f) ? 1.f / lf : 0.f;
+            }
+          }
+          float4 acc[kRows];
+#pragma unroll
+          for (int row = 0; row < kRows; ++row) acc[row] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k0 = 0; k0 < nsplit; k0 += kB) {
+            float4 po[kRows][kB];
+#pragma unroll
+            for (int row = 0; row < kRows; ++row) {
+#pragma unroll
+              for (int u = 0; u < kB; ++u) {
+                po[row][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (row < g && k0 + u < nsplit)
+                  po[row][u] = __ldcg(reinterpret_cast<const float4*>(
+                      p.part_o + (base0 + row + static_cast<int64_t>(k0 + u) * g) * kDecodeHeadDim +
+                      d0));
+              }
+            }
+#pragma unroll
+            for (int row = 0; row < kRows; ++row) {
+#pragma unroll
+              for (int u = 0; u < kB; ++u) {
+                const float fu = __shfl_sync(0xffffffffu, f_r[row], (k0 + u) & 31);
+                if (k0 + u < nsplit) {
+                  acc[row].x += po[row][u].x * fu;
+                  acc[row].y += po[row][u].y * fu;
+                  acc[row].z += po[row][u].z * fu;
+                  acc[row].w += po[row][u].w * fu;
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int row = 0; row < kRows; ++row) {
+            if (row < g) {
+              const float inv = inv_r[row];
+              store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
+                               static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
+                           make_float4(acc[row].x * inv, acc[row].y * inv, acc[row].z * inv,
+                                       acc[row].w * inv));
+            }
+          }
+        } else if (last) {
+          // Any group width and split count: two rounds of loads per row (the
+          // splits' (m, l), one split per lane, then this lane's 4 dims of
+          // every split's partial O, eight at a time), in split order.
           for (int row = 0; row < g; ++row) {
             const int64_t base = static_cast<int64_t>(pair) * p.max_splits * g + row;
             float ms0 = NEG_INF, l0 = 0.f;  // split `lane` (the first 32 splits)
