@@ -1118,10 +1118,10 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
   // As many 16-row m-tiles per row group as shared memory (and two warps
   // per m-tile) allow; more groups re-stream the keys from L2.
   int gm = std::min(p.mtiles, nkv::kThrWarps / 2);
-  while (gm > 0 && nkv::threshold_smem_bytes(G, p.keys_pad, gm, compress_R) > kMaxSmem) --gm;
+  while (gm > 0 && nkv::threshold_smem_bytes(G, p.keys_pad, gm, p.rows, compress_R) > kMaxSmem) --gm;
   if (gm == 0) return NKV_ERR_UNSUPPORTED;
   p.group_mtiles = gm;
-  const size_t smem = nkv::threshold_smem_bytes(G, p.keys_pad, gm, compress_R);
+  const size_t smem = nkv::threshold_smem_bytes(G, p.keys_pad, gm, p.rows, compress_R);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (G) {
     case 1: return launch_threshold<1>(p, num_kv_heads, num_selected, smem, s);

@@ -97,14 +97,25 @@ constexpr int kThrReduceSlots = 16 * kThrWarps;
 constexpr int kThrKeyTile = 64;
 constexpr int kThrKRowElems = kCompressHeadDim + 8;  // padded smem row: conflict-free ldmatrix
 
+constexpr int kThrKStages = 3;  // key-tile ring: two tiles of look-ahead
+
 __host__ __device__ constexpr int thr_score_stride(int keys_pad) { return keys_pad + 8; }
+
+// Bytes of the score region: the rows of the largest row group (bf16), later
+// reused for the compaction's source and destination slot tables (2R ints).
+__host__ __device__ constexpr size_t thr_score_bytes(int group_mtiles, int rows, int keys_pad,
+                                                     int R) {
+  const size_t sc_rows = static_cast<size_t>(group_mtiles * 16 < rows ? group_mtiles * 16 : rows);
+  const size_t sc = sizeof(__nv_bfloat16) * sc_rows * thr_score_stride(keys_pad);
+  const size_t slots = sizeof(int) * 2 * static_cast<size_t>(R);
+  return ((sc > slots ? sc : slots) + 15) / 16 * 16;
+}
 
 // Shared-memory bytes of threshold_compress_kernel (host and device agree).
 __host__ __device__ constexpr size_t threshold_smem_bytes(int G, int keys_pad, int group_mtiles,
-                                                          int R) {
-  return sizeof(__nv_bfloat16) * 2 * kThrKeyTile * kThrKRowElems                 // K tiles
-         + sizeof(__nv_bfloat16) * static_cast<size_t>(group_mtiles) * 16 *
-               thr_score_stride(keys_pad)                                        // scores
+                                                          int rows, int R) {
+  return sizeof(__nv_bfloat16) * kThrKStages * kThrKeyTile * kThrKRowElems       // K tiles
+         + thr_score_bytes(group_mtiles, rows, keys_pad, R)                      // scores
          + sizeof(float) * 2 * group_mtiles * 16                                 // row max, sum
          + sizeof(float) * static_cast<size_t>(G) * keys_pad                     // window sums
          + sizeof(float) * keys_pad                                              // partial
@@ -131,9 +142,10 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   const int gid = lane >> 2, tig = lane & 3;
   const int ss = thr_score_stride(kp);
 
-  __nv_bfloat16* ktile = reinterpret_cast<__nv_bfloat16*>(smem);           // [2][64][136]
-  __nv_bfloat16* sc = ktile + 2 * kThrKeyTile * kThrKRowElems;             // [group rows][ss]
-  float* rmax = reinterpret_cast<float*>(sc + static_cast<size_t>(p.group_mtiles) * 16 * ss);
+  __nv_bfloat16* ktile = reinterpret_cast<__nv_bfloat16*>(smem);           // [3][64][136]
+  __nv_bfloat16* sc = ktile + kThrKStages * kThrKeyTile * kThrKRowElems;   // [group rows][ss]
+  float* rmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sc) +
+                                         thr_score_bytes(p.group_mtiles, p.rows, kp, p.R));
   float* rsum = rmax + p.group_mtiles * 16;
   float* kacc = rsum + p.group_mtiles * 16;                                 // [G][kp]
   float* partial = kacc + G * kp;                                           // [kp]
@@ -232,16 +244,28 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
           qa[kk][3] = q_hi ? *reinterpret_cast<const uint32_t*>(q_hi + d + 8) : 0u;
         }
       }
-      load_ktile(0, 0);
-      for (int tile = 0; tile < ntiles; ++tile) {
-        const int buf = tile & 1;
-        if (tile + 1 < ntiles) {
-          load_ktile(tile + 1, buf ^ 1);
-          cp_async_wait<1>();
+      // key-tile ring: tiles t+1 and t+2 stream while tile t is scored;
+      // every step commits one cp.async group (empty past the last tile)
+#pragma unroll
+      for (int t = 0; t < kThrKStages - 1; ++t) {
+        if (t < ntiles) {
+          load_ktile(t, t);
         } else {
-          cp_async_wait<0>();
+          cp_async_commit();
         }
+      }
+      const int grows = min(gm * 16, p.rows - row0);
+      for (int tile = 0; tile < ntiles; ++tile) {
+        const int buf = tile % kThrKStages;
+        cp_async_wait<kThrKStages - 2>();  // this thread's copies of `tile` landed
+        // all threads' copies of `tile` landed, and tile - 1 is scored: its
+        // buffer takes tile + 2
         __syncthreads();
+        if (tile + kThrKStages - 1 < ntiles) {
+          load_ktile(tile + kThrKStages - 1, (tile + kThrKStages - 1) % kThrKStages);
+        } else {
+          cp_async_commit();
+        }
         if (mma_warp) {
           const uint32_t kb = smem_u32(ktile + buf * kThrKeyTile * kThrKRowElems);
           const int lrow = mt * 16 + gid;
@@ -265,16 +289,18 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
               const int t = t0 + (e & 1);
               v[e] = (t == 0 || t >= nk) ? -INFINITY : round_bf16(round_bf16(acc[e]) * p.scale);
             }
-            *reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(lrow) * ss + t0) =
-                pack_bf16x2(v[0], v[1]);
-            *reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(lrow + 8) * ss + t0) =
-                pack_bf16x2(v[2], v[3]);
+            // rows past the group's real rows (m-tile padding) have no storage
+            if (lrow < grows)
+              *reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(lrow) * ss + t0) =
+                  pack_bf16x2(v[0], v[1]);
+            if (lrow + 8 < grows)
+              *reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(lrow + 8) * ss + t0) =
+                  pack_bf16x2(v[2], v[3]);
           }
         }
-        __syncthreads();  // the buffer is refilled by the next iteration
       }
+      __syncthreads();  // scores complete; the ring's buffers are free
       // ---- B: per-row max and sum of exp
-      const int grows = min(gm * 16, p.rows - row0);
       for (int lr = warp; lr < grows; lr += kThrWarps) {
         const __nv_bfloat16* row = sc + static_cast<size_t>(lr) * ss;
         float m = -INFINITY;
@@ -343,11 +369,21 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
   for (int i = threadIdx.x; i < W; i += kThrThreads) final_idx[1 + num_keep + i] = p.S - W + i;
   __syncthreads();
 
+  // every row's source and destination slot, resolved in one round into the
+  // (now unused) score region, so the compaction's chunks wait on no
+  // block-table lookup
+  int* src_slot = reinterpret_cast<int*>(sc);
+  int* dst_slot = src_slot + p.R;
+  for (int i = threadIdx.x; i < p.R; i += kThrThreads) {
+    src_slot[i] = static_cast<int>(slot_of(start + final_idx[i]));
+    dst_slot[i] = static_cast<int>(slot_of(i));
+  }
+  __syncthreads();
   compact_rows_pipelined<kThrThreads>(p.k_cache, p.v_cache, p.num_kv_heads, head, p.R,
-                         [&](int i, int64_t& src, int64_t& dst) {
-                           src = slot_of(start + final_idx[i]);
-                           dst = slot_of(i);
-                         });
+                                      [&](int i, int64_t& src, int64_t& dst) {
+                                        src = src_slot[i];
+                                        dst = dst_slot[i];
+                                      });
   if (head == 0) {
     if (threadIdx.x == 0) p.context_lens[b] = p.R;
     if (p.out_keep_idx) {
