@@ -198,7 +198,7 @@ def run_gpu(args, rank, world, dev):
                 e0.record()
             # one launch: slot write of the new K/V rows + paged decode
             ops.decode_step(q, k, v, kv[0, c], kv[1, c], sm, bt, cl, scale, out=out[layer],
-                            workspace=ws)
+                            workspace=ws, metadata_ready=True)
             if rec:
                 e1.record()
                 dec_events.append((e0, e1))
@@ -647,7 +647,7 @@ def measure_config3(dev, world):
             for layer in range(LAYERS):
                 c = layer % R
                 ops.decode_step(q, k, v, kv[0, c], kv[1, c], sm, bt, cl, D ** -0.5, out=out,
-                                workspace=ws)
+                                workspace=ws, metadata_ready=True)
 
         for _ in range(2):
             step()
@@ -731,7 +731,7 @@ def measure_kvchat(dev, world, profile_replays: int = 0):
             q, k, v = q.view(1, hq, D), k.view(1, hk, D), v.view(1, hk, D)
             ops.decode_step(q, k, v, kc[layer], vc[layer], sm, bt, cl, D ** -0.5,
                             out=out[layer], ring=ring, layer_id=layer, ring_slot_of_row=zero,
-                            ring_pos_of_row=zero, workspace=ws)
+                            ring_pos_of_row=zero, workspace=ws, metadata_ready=True)
 
     step()
     torch.cuda.synchronize(dev)
@@ -861,7 +861,8 @@ def measure_config4(dev, world):
 
     def layer(i):
         kc, vc = caches[i % 2]
-        ops.decode_step(q, k, v, kc, vc, sm, bt, cl, D ** -0.5, out=out, workspace=ws)
+        ops.decode_step(q, k, v, kc, vc, sm, bt, cl, D ** -0.5, out=out, workspace=ws,
+                        metadata_ready=True)
 
     for i in range(4):
         layer(i)
@@ -1496,7 +1497,7 @@ def run_profile_case(kind: str) -> None:
     q, k, v = qkv.split([HQ * D, HK * D, HK * D], dim=-1)
     for _ in range(4):
         ops.decode_step(q.view(64, HQ, D), k.view(64, HK, D), v.view(64, HK, D), kc, vc, sm, bt,
-                        cl, D ** -0.5)
+                        cl, D ** -0.5, metadata_ready=True)
     torch.cuda.synchronize()
     print(json.dumps({"profile": kind, "kv_tokens": sum(lens),
                       "alg_bytes": algorithmic_decode_bytes(lens, HK, HQ)}))

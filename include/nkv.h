@@ -128,8 +128,18 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
 /* position context_lens[b]-1 (how the reference's decode step builds it,    */
 /* nanokvllm/engine/model_runner.py:194 and :279). Rows violating that are   */
 /* not written and flag NKV_DEVERR_STORE_SLOT. The producer warp writes each */
-/* kv head's new row just before the TMA that reads that tile, so no second  */
+/* kv head's new row to the cache and into the shared-memory copy of the     */
+/* tile that holds it (after that tile's TMA has landed), so no second       */
 /* launch or cross-CTA ordering is needed.                                   */
+/* metadata_ready = 1 lets the launch read block_tables, context_lens,      */
+/* slot_mapping and the ring indices before it waits for the kernel it       */
+/* depends on (programmatic dependent launch): the caller vouches that the   */
+/* kernel launched just before this call on the stream does not write them   */
+/* (host copies and earlier kernels are fine; a compression kernel that     */
+/* rewrites context_lens right before is not). In a chain of decode launches */
+/* that hides a round of metadata loads behind the previous launch's tail.   */
+/* 0 reads everything after the wait. q, key and value are always read after */
+/* it.                                                                       */
 /* ring may be NULL (no query window). Otherwise it is the KvChat ring       */
 /* [num_ring_slots, num_layers, window_size, num_q_heads, head_dim]; row b   */
 /* appends q[b] to ring[ring_slot_of_row[b], layer_id, ring_pos_of_row[b]]   */
@@ -147,6 +157,7 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
                     void* out, int64_t out_stride_token,
                     int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                     int32_t head_dim, int32_t block_size, float softmax_scale,
+                    int32_t metadata_ready,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */

@@ -383,7 +383,7 @@ const char* nkv_status_string(int status) {
   }
 }
 
-int nkv_abi_version(void) { return 101; }
+int nkv_abi_version(void) { return 102; }
 
 int nkv_last_cuda_error(void) { return t_last_cuda_error; }
 
@@ -450,6 +450,7 @@ struct FusedStep {
   int32_t num_ring_slots = 0, num_layers = 0, window_size = 0, layer_id = 0;
   const int32_t* ring_slot_of_row = nullptr;
   const int32_t* ring_pos_of_row = nullptr;
+  int32_t metadata_ready = 0;
 };
 
 int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -528,6 +529,7 @@ int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
     p.new_k_stride_vec = fused->key_stride / 8;
     p.new_v_stride_vec = fused->value_stride / 8;
     p.slot_mapping = fused->slot_mapping;
+    p.metadata_ready = fused->metadata_ready;
     p.k_cache_vec = static_cast<uint4*>(const_cast<void*>(k_cache));
     p.v_cache_vec = static_cast<uint4*>(const_cast<void*>(v_cache));
     if (fused->ring != nullptr) {
@@ -707,9 +709,11 @@ int nkv_decode_step(const void* q, int64_t q_stride_token, int64_t q_stride_head
                     int32_t layer_id, const int32_t* ring_slot_of_row,
                     const int32_t* ring_pos_of_row, void* out, int64_t out_stride_token,
                     int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                    int32_t block_size, float softmax_scale, void* workspace,
-                    size_t workspace_bytes, void* stream) {
+                    int32_t block_size, float softmax_scale, int32_t metadata_ready,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (metadata_ready != 0 && metadata_ready != 1) return NKV_ERR_INVALID_ARGUMENT;
   FusedStep f;
+  f.metadata_ready = metadata_ready;
   f.key = key;
   f.key_stride = key_stride;
   f.value = value;

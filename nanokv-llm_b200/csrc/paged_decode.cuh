@@ -68,11 +68,12 @@ struct DecodeShape {
   static constexpr int kSlotOFloats = kDecodeConsumerWarps * G * kORowStride;
   static constexpr int kSlotMLFloats = 2 * kDecodeConsumerWarps * G;
   static constexpr int kSlotBytes = (kSlotOFloats + kSlotMLFloats) * 4 + 16;
-  // [stages][slots][barriers][meta][flags (16 B)][receive barrier (16 B)]
+  // [stages][slots][barriers][meta][flags (16 B)][pad to 16][receive barrier (16 B)]
   // [receive rows: cluster launches only, kRecvRowFloats per (split, row)]
-  static constexpr int kRecvBarOffset = kStages * kStageBytes + kSlots * kSlotBytes +
-                                        (2 * kStages + 2 * kSlots) * 8 +
-                                        kStages * kDecodeMetaInts * 4 + 16;
+  // barriers: full, empty, patch (per stage), slot full, slot empty
+  static constexpr int kRecvBarOffset = (kStages * kStageBytes + kSlots * kSlotBytes +
+                                         (3 * kStages + 2 * kSlots) * 8 +
+                                         kStages * kDecodeMetaInts * 4 + 16 + 15) / 16 * 16;
   static constexpr int kRecvOffset = kRecvBarOffset + 16;
   static constexpr int kSmemBytes = kRecvOffset + 1024 /* alignment */;
   // A cluster launch of C splits adds C * G receive rows.
@@ -102,6 +103,11 @@ struct DecodeParams {
   // split r of (row, kv head) pair c and sending its partial to rank 0
   // through distributed shared memory (no global partials or counters).
   int cluster;
+  // 1: block_tables, context_lens, slot_mapping and the ring indices are not
+  // written by the kernel this launch depends on, so a CTA's first item's
+  // metadata is read before the dependency wait (the fused decode step's
+  // contract, when its caller vouches for it).
+  int metadata_ready;
   // Fused decode step (optional, null when unused): the step's new K/V rows,
   // written by the producer warp right before the TMA that reads them, and
   // the KvChat query-window ring append.
@@ -146,7 +152,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   uint8_t* slot_mem = smem + kStages * S::kStageBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(slot_mem + kSlots * S::kSlotBytes);
   uint64_t* empty_bar = full_bar + kStages;
-  uint64_t* slot_full = empty_bar + kStages;   // 128 consumer arrivals
+  uint64_t* patch_bar = empty_bar + kStages;  // TMA of a tile the producer patches
+  uint64_t* slot_full = patch_bar + kStages;   // 128 consumer arrivals
   uint64_t* slot_empty = slot_full + kSlots;   // 1 merger arrival
   int* meta = reinterpret_cast<int*>(slot_empty + kSlots);
   volatile int* flags = meta + kStages * kDecodeMetaInts;  // [0] abort
@@ -171,6 +178,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), kDecodeConsumerWarps);
+      mbar_init(smem_u32(&patch_bar[s]), 1);
     }
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(smem_u32(&slot_full[s]), kDecodeConsumerWarps * 32);
@@ -192,13 +200,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   if (cluster_mode) cluster_sync_all();
   // Launched with programmatic stream serialisation: everything above
   // overlapped the previous kernel (typically the previous layer's decode);
-  // from here on its writes (cache rows, the reset workspace counters) are
-  // visible. The next kernel of the stream (the next layer's decode) may be
-  // scheduled from now on: its CTAs take free SMs, run their own set-up and
-  // wait at their grid_dependency_wait until this grid has finished, which
-  // hides a launch's latency and set-up in a chain of small decode launches.
-  grid_dependency_wait();
-  allow_dependent_launch();
+  // after each role's grid_dependency_wait its writes (q / k / v rows, cache
+  // rows, the reset workspace counters) are visible. The producer allows the
+  // next kernel of the stream (the next layer's decode) to be scheduled right
+  // after its own wait: those CTAs take free SMs, run their set-up (and, with
+  // metadata_ready, their first metadata loads) and wait until this grid has
+  // finished, which hides a launch's latency in a chain of small launches.
 
   const int Hk = p.num_kv_heads;
   const int g = p.g;
@@ -231,6 +238,61 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     if (csize > 1)
       static_item = static_cast<int>(blockIdx.x) % csize * (Hk * p.batch) +
                     static_cast<int>(blockIdx.x) / csize;
+    constexpr int kHeadVecs = kDecodeHeadDim / 8;  // 16-byte units of one head row
+    // An item's metadata in one round, spread over the lanes: its length,
+    // slot-mapping entry and query-window slot / position (lanes 0-3) and 32
+    // block-table entries from its split's first block (one per lane).
+    auto meta_loads = [&](int it, int& scalar, int& bt) {
+      const int kvh_ = it % Hk;
+      const int rest_ = it / Hk;
+      const int b_ = rest_ % p.batch;
+      const int s_ = rest_ / p.batch;
+      (void)kvh_;
+      scalar = 0;
+      if (lane == 0) {
+        scalar = ldg_nc_s32(p.context_lens + b_);
+      } else if (lane == 1) {
+        scalar = p.new_k != nullptr ? ldg_nc_s32(p.slot_mapping + b_) : -1;
+      } else if (lane == 2 || lane == 3) {
+        if (p.ring_vec != nullptr && s_ == 0)
+          scalar = ldg_nc_s32((lane == 2 ? p.ring_slot_of_row : p.ring_pos_of_row) + b_);
+      }
+      const int blk0 = s_ * p.chunk_tokens / p.block_size;
+      bt = -1;
+      if (blk0 + lane < p.max_blocks)
+        bt = ldg_nc_s32(p.block_tables + static_cast<int64_t>(b_) * p.max_blocks + blk0 + lane);
+    };
+    // With metadata_ready the first item's metadata is requested before the
+    // dependency wait, so it arrives while the previous kernel drains.
+    const bool early = p.metadata_ready != 0 && static_item < p.total_items;
+    int pre_scalar = 0, pre_bt = -1;
+    if (early) {
+      meta_loads(static_item, pre_scalar, pre_bt);
+      // ... and its first K/V tile is requested into L2 (a hint: the loads
+      // after the wait read the coherent data), which also brings the
+      // tensor maps' first use forward
+      const int len0 = __shfl_sync(0xffffffffu, pre_scalar, 0);
+      const int s0 = static_item / Hk / p.batch;
+      const int tok0 = s0 * p.chunk_tokens;
+      const int blk = __shfl_sync(0xffffffffu, pre_bt, 0);
+      if (leader && tok0 < len0 && blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks) {
+        const int kvh0 = static_item % Hk;
+        const int slot0 = blk * p.block_size + tok0 % p.block_size;
+        tma_prefetch_l2_3d(&tm_k, 0, kvh0, slot0);
+        tma_prefetch_l2_3d(&tm_k, 64, kvh0, slot0);
+        tma_prefetch_l2_3d(&tm_v, 0, kvh0, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, kvh0, slot0);
+      }
+    }
+    grid_dependency_wait();
+    allow_dependent_launch();
+    bool first = true;
+    // patch_armed[s] = parity + 1 of a patch-barrier transaction issued into
+    // stage s and not yet waited for (only after an abort).
+    uint32_t patch_armed[kStages];
+    uint32_t patch_phase = 0;  // bit s: parity of stage s's next patch transaction
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) patch_armed[s] = 0;
     while (ok) {
       int item = static_item;
       if (item < 0) {
@@ -245,28 +307,19 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       const int s = rest / p.batch;
       const int t0 = s * p.chunk_tokens;
       const int blk_first = t0 / p.block_size;
-      // Everything the item needs from global memory is requested in one
-      // round, spread over the lanes, so the item costs one load latency
-      // before its first tile instead of a chain of dependent ones: the
-      // scalars (lanes 0-3), 32 block-table entries from the split's first
-      // block, the new K/V head rows (fused slot write) and the group's q
-      // rows (KvChat query window).
-      int scalar = 0;
-      if (lane == 0) {
-        scalar = ldg_nc_s32(p.context_lens + b);
-      } else if (lane == 1) {
-        scalar = p.new_k != nullptr ? ldg_nc_s32(p.slot_mapping + b) : -1;
-      } else if (lane == 2 || lane == 3) {
-        if (p.ring_vec != nullptr && s == 0)
-          scalar = ldg_nc_s32((lane == 2 ? p.ring_slot_of_row : p.ring_pos_of_row) + b);
+      int scalar, bt_ent;
+      if (first && early) {
+        scalar = pre_scalar;
+        bt_ent = pre_bt;
+      } else {
+        meta_loads(item, scalar, bt_ent);
       }
-      int bt_ent = -1;
-      if (blk_first + lane < p.max_blocks)
-        bt_ent = ldg_nc_s32(p.block_tables + static_cast<int64_t>(b) * p.max_blocks + blk_first + lane);
-      constexpr int kHeadVecs = kDecodeHeadDim / 8;  // 16-byte units of one head row
+      first = false;
+      // The data rows come from the kernel this launch depends on (after the
+      // wait): the new K/V head rows of the fused slot write (lanes 0-15 K,
+      // 16-31 V) and the group's q rows for the KvChat query window.
       uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
       if (p.new_k != nullptr) {
-        // lanes 0-15: the K head row, 16-31: the V head row
         const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
         new_row = ldg_nc_v4(lane < kHeadVecs ? p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col
                                              : p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
@@ -305,8 +358,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       const int t1 = min(t0 + p.chunk_tokens, len);
       const int ntiles = len > 0 ? (t1 - t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
       // Fused slot write: the current token (position len - 1) lives in the
-      // last split's last tile; its K/V head slice is written before any of
-      // the item's tiles is requested and made visible to the async proxy.
+      // last split's last tile. Its K/V head slice goes to the cache, and --
+      // so that the tile's load need not wait for that write -- into the
+      // tile's shared-memory copy once the TMA has landed, before the
+      // consumers are released (patch_row >= 0: the row inside that tile).
+      int patch_row = -1;
       if (p.new_k != nullptr && s == nsplit - 1 && ntiles > 0) {
         const int blk = block_of(len - 1);
         const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
@@ -316,23 +372,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
           uint4* dst = lane < kHeadVecs ? p.k_cache_vec : p.v_cache_vec;
           dst[static_cast<int64_t>(slot_new) * row_vecs + col] = new_row;
-          fence_proxy_async_global();
+          patch_row = (len - 1) - (t0 + (ntiles - 1) * kDecodeTileTokens);
         } else if (slot_new != -1 && leader) {
           raise_error(NKV_DEVERR_STORE_SLOT);
-        }
-        __syncwarp();
-      }
-      // KvChat: this step's query rows of the group join the row's window.
-      if (p.ring_vec != nullptr && s == 0 && ring_slot >= 0) {
-        if (ring_slot < p.ring_slots && ring_pos >= 0 && ring_pos < p.ring_window) {
-          uint4* dst = p.ring_vec + p.ring_layer_base_vec + ring_slot * p.ring_slot_stride_vec +
-                       static_cast<int64_t>(ring_pos) * p.num_q_heads * kHeadVecs +
-                       static_cast<int64_t>(kvh) * q_vecs;
-#pragma unroll
-          for (int i = 0; i < kQVecsPerLane; ++i)
-            if (lane + 32 * i < q_vecs) dst[lane + 32 * i] = q_rows[i];
-        } else if (leader) {
-          raise_error(NKV_DEVERR_RING_RANGE);
         }
       }
       int j = 0;
@@ -365,27 +407,70 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           // fully out of range: TMA fills zeros
           const int slot = blk_ok ? blk * p.block_size + (tok % p.block_size) : -2 * kDecodeTileTokens;
           if (!blk_ok && leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
+          const bool patch = patch_row >= 0 && j == ntiles - 1;
+          // a patched tile's transaction completes on the patch barrier; the
+          // producer releases the consumers itself after the patch
+          const uint32_t tb = patch ? smem_u32(&patch_bar[stage]) : fb;
+          const uint32_t base = smem_u32(stage_mem + stage * S::kStageBytes);
           if (leader) {
             const uint32_t bytes = 4u * kHalfTileBytes + (j == 0 ? q_bytes : 0u);
-            mbar_arrive_expect_tx(fb, bytes);
-            const uint32_t base = smem_u32(stage_mem + stage * S::kStageBytes);
-            tma_load_3d(base + 0 * kHalfTileBytes, &tm_k, fb, 0, kvh, slot, pol_stream);
-            tma_load_3d(base + 1 * kHalfTileBytes, &tm_k, fb, 64, kvh, slot, pol_stream);
-            tma_load_3d(base + 2 * kHalfTileBytes, &tm_v, fb, 0, kvh, slot, pol_stream);
-            tma_load_3d(base + 3 * kHalfTileBytes, &tm_v, fb, 64, kvh, slot, pol_stream);
+            mbar_arrive_expect_tx(tb, bytes);
+            tma_load_3d(base + 0 * kHalfTileBytes, &tm_k, tb, 0, kvh, slot, pol_stream);
+            tma_load_3d(base + 1 * kHalfTileBytes, &tm_k, tb, 64, kvh, slot, pol_stream);
+            tma_load_3d(base + 2 * kHalfTileBytes, &tm_v, tb, 0, kvh, slot, pol_stream);
+            tma_load_3d(base + 3 * kHalfTileBytes, &tm_v, tb, 64, kvh, slot, pol_stream);
             if (j == 0) {
               const uint32_t qb = base + 4 * kHalfTileBytes;
-              tma_load_3d(qb, &tm_q, fb, 0, kvh * g, b, pol_q);
-              tma_load_3d(qb + S::kQHalfBytes, &tm_q, fb, 64, kvh * g, b, pol_q);
+              tma_load_3d(qb, &tm_q, tb, 0, kvh * g, b, pol_q);
+              tma_load_3d(qb + S::kQHalfBytes, &tm_q, tb, 64, kvh * g, b, pol_q);
             }
           }
-          armed[stage] = phase + 1u;
+          if (!patch) {
+            armed[stage] = phase + 1u;
+          } else {
+            const uint32_t pp = (patch_phase >> stage) & 1u;
+            patch_phase ^= 1u << stage;
+            patch_armed[stage] = pp + 1u;
+            // every lane observes the transaction's completion before it
+            // overwrites part of what the TMA wrote
+            const bool landed = mbar_wait_bounded(smem_u32(&patch_bar[stage]), pp);
+            if (!__all_sync(0xffffffffu, landed)) {
+              if (leader) flags[0] = 1;
+              ok = false;
+              break;
+            }
+            patch_armed[stage] = 0;
+            // lane u < 16: K dims [8u, 8u + 8) -> half u / 8, 16-byte chunk
+            // u % 8 of the row's 128-byte swizzled line; lanes 16-31: V
+            const int u = lane & (kHeadVecs - 1);
+            uint8_t* dst = stage_mem + stage * S::kStageBytes +
+                           ((lane < kHeadVecs ? 0 : 2) + (u >> 3)) * kHalfTileBytes +
+                           swz128(static_cast<uint32_t>(patch_row), static_cast<uint32_t>(u & 7));
+            *reinterpret_cast<uint4*>(dst) = new_row;
+            __syncwarp();
+            if (leader) mbar_arrive(fb);  // releases the tile (and the patch) to the consumers
+          }
         }
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
         }
       } while (++j < ntiles);
+      if (!ok) break;
+      // KvChat: this step's query rows of the group join the row's window
+      // (after the item's tiles are in flight: nothing in this launch reads them).
+      if (p.ring_vec != nullptr && s == 0 && ring_slot >= 0) {
+        if (ring_slot < p.ring_slots && ring_pos >= 0 && ring_pos < p.ring_window) {
+          uint4* dst = p.ring_vec + p.ring_layer_base_vec + ring_slot * p.ring_slot_stride_vec +
+                       static_cast<int64_t>(ring_pos) * p.num_q_heads * kHeadVecs +
+                       static_cast<int64_t>(kvh) * q_vecs;
+#pragma unroll
+          for (int i = 0; i < kQVecsPerLane; ++i)
+            if (lane + 32 * i < q_vecs) dst[lane + 32 * i] = q_rows[i];
+        } else if (leader) {
+          raise_error(NKV_DEVERR_RING_RANGE);
+        }
+      }
     }
     if (leader) {
       if (ok) {
@@ -403,6 +488,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
 #pragma unroll
       for (int s = 0; s < kStages; ++s) {
         if (armed[s]) mbar_wait_bounded(smem_u32(&full_bar[s]), armed[s] - 1u);
+        if (patch_armed[s]) mbar_wait_bounded(smem_u32(&patch_bar[s]), patch_armed[s] - 1u);
       }
       // The last CTA out resets the scheduler counters for the next call.
       __threadfence();
@@ -417,6 +503,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
 
   if (warp == kDecodeMergerWarp) {
     // -------------------------------------------------------------- merger
+    grid_dependency_wait();  // before any global write (out, partials, counters)
     int slot = 0;
     uint32_t sphase = 0;
     const int d0 = 4 * lane;  // this lane's 4 dims
@@ -460,6 +547,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
                            static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
                        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        } else if (cluster_mode && s == 0) {
+          // the leader's own split: straight into its receive rows
+          float* r = recv + row * kRecvRowFloats;
+          *reinterpret_cast<float4*>(r + d0) = acc;
+          if (lane == 0) *reinterpret_cast<float2*>(r + kDecodeHeadDim) = make_float2(M, L);
         } else if (cluster_mode) {
           // this split's row into the leader's receive rows, counted on its
           // receive barrier (nothing to wait for here)
@@ -481,13 +573,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&slot_empty[slot]));
       if (nsplit > 1 && cluster_mode) {
-        // The leader (split 0) expects every split's rows, waits for them to
-        // land, then merges the splits in order. Splits past the row's end
+        // The leader (split 0) expects the other splits' rows, waits for them
+        // to land, then merges the splits in order. Splits past the row's end
         // send nothing and are not expected.
         if (s == 0) {
+          __syncwarp();  // its own rows, stored by all lanes, are visible to all
           if (lane == 0)
             mbar_arrive_expect_tx(smem_u32(recv_bar),
-                                  static_cast<uint32_t>(nsplit * g * (4 * kDecodeHeadDim + 8)));
+                                  static_cast<uint32_t>((nsplit - 1) * g * (4 * kDecodeHeadDim + 8)));
           if (mbar_wait_cluster_bounded(smem_u32(recv_bar), 0)) {
             for (int row = 0; row < g; ++row) {
               float M = NEG_INF;
@@ -682,6 +775,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   }
 
   // -------------------------------------------------------------- consumers
+  grid_dependency_wait();
   const int cw = warp;
   const int gid = lane >> 2;
   const int tig = lane & 3;

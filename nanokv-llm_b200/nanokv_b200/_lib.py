@@ -61,7 +61,7 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, c_int64, c_int64, _P, c_int64, _P, c_int64, _I32P, _P, _P, c_int64, _I32P, c_int32,
          _I32P, _P, c_int32, c_int32, c_int32, c_int32, _I32P, _I32P, _P, c_int64,
-         c_int32, c_int32, c_int32, c_int32, c_int32, c_float, _P, c_size_t, _P],
+         c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_int32, _P, c_size_t, _P],
     ),
     "nkv_qk_norm_rope_store": (
         c_int,

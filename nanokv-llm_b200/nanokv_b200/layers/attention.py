@@ -77,9 +77,12 @@ class Attention(nn.Module):
                             or bool(context.compress_selected_batch_indices)))
         if (not stored and context.use_decode_kernel and not compressing and k_cache.numel()
                 and q.size(0) == context.block_tables.size(0)):
-            # decode step without compression: slot write + decode in one launch
+            # decode step without compression: slot write + decode in one launch;
+            # the step's metadata comes from host copies, so no kernel right
+            # before this one writes it
             o = ops.decode_step(q, k, v, k_cache, v_cache, context.slot_mapping,
-                                context.block_tables, context.context_lens, self.scale)
+                                context.block_tables, context.context_lens, self.scale,
+                                metadata_ready=True)
             return o.unsqueeze(1)
         if not stored and k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)

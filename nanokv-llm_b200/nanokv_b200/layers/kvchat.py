@@ -126,9 +126,10 @@ class Attention(nn.Module):
                 ring_args = dict(ring=qwm.ring, layer_id=Layer,
                                  ring_slot_of_row=context.q_window_row_slot_t,
                                  ring_pos_of_row=context.q_window_row_pos_t)
+            # the step's metadata and ring indices come from host copies
             o = ops.decode_step(q, k, v, k_cache, v_cache, context.slot_mapping,
                                 context.block_tables, context.context_lens, self.scale,
-                                **ring_args)
+                                metadata_ready=True, **ring_args)
             if ring_args:
                 qwm.advance(context.q_window_active_seq_ids, Layer)
             return o.unsqueeze(1)

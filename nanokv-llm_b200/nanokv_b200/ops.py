@@ -157,11 +157,19 @@ def decode_step(q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, k_cache
                 ring: torch.Tensor | None = None, layer_id: int = 0,
                 ring_slot_of_row: torch.Tensor | None = None,
                 ring_pos_of_row: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None,
+                metadata_ready: bool = False) -> torch.Tensor:
     """One fused launch of store_kvcache(key, value, slot_mapping) [+ the
     KvChat query-window append] + paged_decode for a decode step (one new
     token per row, slot_mapping[b] = -1 or the slot of position
-    context_lens[b] - 1)."""
+    context_lens[b] - 1).
+
+    metadata_ready: the caller vouches that the kernel launched just before
+    this call on the stream does not write block_tables, context_lens,
+    slot_mapping or the ring indices (host copies and earlier kernels are
+    fine), so the launch may read them before it waits for that kernel --
+    true of a decode step's layers, whose metadata the engine copies from
+    the host; not of a decode right after a compression kernel."""
     _require_cuda("decode_step", q, key, value, k_cache, v_cache, slot_mapping, block_tables,
                   context_lens)
     B, Hq, D = q.shape
@@ -176,6 +184,7 @@ def decode_step(q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, k_cache
     max_blocks = block_tables.size(1)
     if block_tables.stride(0) != max_blocks:
         block_tables = block_tables.contiguous()
+        metadata_ready = False  # the copy kernel just wrote it
     if out is None:
         out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=q.device)
     if B == 0:
@@ -195,6 +204,7 @@ def decode_step(q: torch.Tensor, key: torch.Tensor, value: torch.Tensor, k_cache
         value.stride(0), slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
         num_blocks, block_tables.data_ptr(), max_blocks, context_lens.data_ptr(), *ring_args,
         out.data_ptr(), out.stride(0), B, Hq, Hk, D, block_size, float(softmax_scale),
+        1 if metadata_ready else 0,
         workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream(q.device)))
     return out
 

@@ -25,7 +25,7 @@ def test_library_builds_and_exports_every_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in nkv.h but not exported"
     assert set(declared) == set(_lib.SIGNATURES), "ctypes bindings out of sync with nkv.h"
-    assert lib.nkv_abi_version() == 101
+    assert lib.nkv_abi_version() == 102
     assert lib.nkv_status_string(3) == b"NKV_ERR_WORKSPACE"
 
 

@@ -22,8 +22,11 @@ def _qkv(B, Hq, Hk, seed):
     return q.view(B, Hq, 128), k.view(B, Hk, 128), v.view(B, Hk, 128)
 
 
+@pytest.mark.parametrize("metadata_ready", [False, True])
 @pytest.mark.parametrize("Hq,Hk", [(32, 8), (16, 8), (4, 1), (64, 8)])
-def test_decode_step_equals_store_then_decode(cuda_lib, Hq, Hk):
+def test_decode_step_equals_store_then_decode(cuda_lib, Hq, Hk, metadata_ready):
+    # metadata_ready: the kernel launched just before (paged_decode) writes
+    # none of the metadata, so reading it before the dependency wait is valid
     from nanokv_b200 import _lib, ops
 
     lens = [1, 300, 0, 4097, 128, 2500, 0, 7000]
@@ -35,7 +38,7 @@ def test_decode_step_equals_store_then_decode(cuda_lib, Hq, Hk):
     kb, vb = ka.clone(), va.clone()
     ops.store_kvcache(k, v, ka, va, sm)
     sep = ops.paged_decode(q, ka, va, bt, cl, 128 ** -0.5)
-    fused = ops.decode_step(q, k, v, kb, vb, sm, bt, cl, 128 ** -0.5)
+    fused = ops.decode_step(q, k, v, kb, vb, sm, bt, cl, 128 ** -0.5, metadata_ready=metadata_ready)
     torch.cuda.synchronize()
     assert torch.equal(ka.view(torch.int16), kb.view(torch.int16))
     assert torch.equal(va.view(torch.int16), vb.view(torch.int16))
@@ -103,11 +106,13 @@ def test_decode_step_replayed_from_graph(cuda_lib):
     v = torch.zeros_like(k)
     out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=DEV)
     ws = ops.decode_workspace(torch.device(DEV), B, Hq, Hk, 128, bt.size(1), 256)
-    ops.decode_step(q, k, v, kd, vd, sm, bt, cl, 128 ** -0.5, out=out, workspace=ws)
+    ops.decode_step(q, k, v, kd, vd, sm, bt, cl, 128 ** -0.5, out=out, workspace=ws,
+                    metadata_ready=True)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        ops.decode_step(q, k, v, kd, vd, sm, bt, cl, 128 ** -0.5, out=out, workspace=ws)
+        ops.decode_step(q, k, v, kd, vd, sm, bt, cl, 128 ** -0.5, out=out, workspace=ws,
+                        metadata_ready=True)
     ref_k, ref_v = pb.k_cache.clone(), pb.v_cache.clone()
     for it in range(3):
         nq, nk, nv = _qkv(B, Hq, Hk, 200 + it)
@@ -118,3 +123,46 @@ def test_decode_step_replayed_from_graph(cuda_lib):
         ref = paged_decode_ref(nq.cpu(), ref_k, ref_v, pb.block_tables, pb.context_lens, 128 ** -0.5)
         assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
         assert torch.equal(kd.cpu().view(torch.int16), ref_k.view(torch.int16))
+
+
+@pytest.mark.parametrize("lens", [[640], [767, 300, 1025], [5000, 12]])
+def test_decode_step_chain_with_metadata_ready(cuda_lib, lens):
+    """Layers' fused steps launched back to back, each reading its metadata
+    before waiting on the previous launch (metadata_ready, as the layers
+    call it), at small batches that split rows over thread-block clusters,
+    with the KvChat ring: every layer's output, cache rows and ring rows
+    must equal the oracle's / the separate append's."""
+    from nanokv_b200 import _lib, ops
+
+    Hq, Hk, W, L = 16, 8, 5, 6
+    B = len(lens)
+    pb = make_paged_batch(seed=300 + B, lens=lens, Hq=Hq, Hk=Hk)
+    bt, cl, sm = pb.block_tables.to(DEV), pb.context_lens.to(DEV), pb.slot_mapping.to(DEV)
+    caches = [(pb.k_cache.to(DEV), pb.v_cache.to(DEV)) for _ in range(L)]
+    steps = [_qkv(B, Hq, Hk, 310 + i) for i in range(L)]
+    ring = torch.zeros(2, L, W, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    ring_ref = ring.clone()
+    slot_of_row = torch.tensor([i % 2 for i in range(B)], dtype=torch.int32, device=DEV)
+    pos_of_row = torch.tensor([(3 * i + 1) % W for i in range(B)], dtype=torch.int32, device=DEV)
+    outs = [torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=DEV) for _ in range(L)]
+    ws = ops.decode_workspace(torch.device(DEV), B, Hq, Hk, 128, bt.size(1), 256)
+    torch.cuda.synchronize()
+    for layer in range(L):
+        q, k, v = steps[layer]
+        ops.decode_step(q, k, v, caches[layer][0], caches[layer][1], sm, bt, cl, 128 ** -0.5,
+                        out=outs[layer], ring=ring, layer_id=layer, ring_slot_of_row=slot_of_row,
+                        ring_pos_of_row=pos_of_row, workspace=ws, metadata_ready=True)
+    torch.cuda.synchronize()
+    assert _lib.read_device_error(clear=True) == 0
+    active = torch.arange(B, dtype=torch.int32, device=DEV)
+    for layer in range(L):
+        q, k, v = steps[layer]
+        ops.query_window_append(q, ring_ref, layer, active, slot_of_row, pos_of_row)
+        kc, vc = pb.k_cache.clone(), pb.v_cache.clone()
+        store_kvcache_ref(k.cpu(), v.cpu(), kc, vc, pb.slot_mapping)
+        assert torch.equal(caches[layer][0].cpu().view(torch.int16), kc.view(torch.int16))
+        assert torch.equal(caches[layer][1].cpu().view(torch.int16), vc.view(torch.int16))
+        ref = paged_decode_ref(q.cpu(), kc, vc, pb.block_tables, pb.context_lens, 128 ** -0.5)
+        assert (outs[layer].float().cpu() - ref).abs().max().item() <= 2e-2, f"layer {layer}"
+    torch.cuda.synchronize()
+    assert torch.equal(ring.view(torch.int16), ring_ref.view(torch.int16))
