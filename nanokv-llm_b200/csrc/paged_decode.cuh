@@ -7,17 +7,22 @@
 //     one sequence for one kv head and ALL g = Hq/Hk query heads of that group
 //     (GQA grouping: a K/V tile is read once for the whole group).
 //   * Persistent CTAs (one per SM), three warp roles:
-//       - warp 4, the producer: one lane grabs work items from a global atomic
-//         counter (dynamic load balance over the ragged context lengths),
-//         resolves block_tables and streams 128-token K and V tiles with
-//         cp.async.bulk.tensor (TMA, 128B swizzle, L2 evict_first, no
-//         multicast) into a 3-stage shared-memory ring guarded by full/empty
-//         mbarriers; the item's query rows ride in its first tile's transaction;
-//       - warps 0-3, the consumers: each owns 32 tokens of every tile,
-//         computes S = Q K^T with mma.sync m16n8k16 (query heads on M, padded
-//         to 16), keeps a warp-private online softmax (exp2 domain) and
-//         accumulates O += P V with P re-packed from the S accumulators. At
-//         the end of an item they only dump their raw (m, l, O) into a
+//       - warp 4, the producer: a CTA's first item is fixed by its block
+//         index, later ones come from a global atomic counter (dynamic load
+//         balance over the ragged context lengths). Per item one round of
+//         loads spread over the lanes (length, slot, ring indices, 32
+//         block-table entries, the fused step's new rows); then 128-token K
+//         and V tiles stream with cp.async.bulk.tensor (TMA, 128B swizzle, L2
+//         evict_first, no multicast) into a 3-stage shared-memory ring
+//         guarded by full/empty mbarriers; the item's query rows ride in its
+//         first tile's transaction. The fused step's new K/V row goes to the
+//         cache and into the shared-memory copy of the tile that holds it
+//         once that tile has landed;
+//       - warps 0-3, the consumers: each owns 32 tokens of every tile and
+//         keeps a warp-private online softmax (exp2 domain). For group widths
+//         up to 8 they compute S^T = K Q^T and O^T = V^T P^T with mma.sync
+//         m16n8k16 (tokens / dims on M, the heads on N), width 16 keeps Q on
+//         M. At the end of an item they only dump their raw (m, l, O) into a
 //         hand-off slot and go on with the next item;
 //       - warp 5, the merger: takes a slot, merges the four warp states in a
 //         fixed order (deterministic), and writes the bf16 output -- or, for
@@ -26,6 +31,13 @@
 //         the output, then resets the counter.
 //     The merge, the global writes and the cross-CTA hand-off therefore never
 //     stall the tensor-core warps or the TMA ring.
+//   * Small launches (few (row, kv head) pairs) are launched as thread-block
+//     clusters, one per pair, CTA r taking split r; the splits' partials go
+//     to the cluster leader's shared memory with st.async and merge there.
+//   * Programmatic dependent launch: the next kernel may start while this one
+//     drains; each role waits (griddepcontrol.wait) before its first access
+//     to data the previous kernel may write. With metadata_ready the producer
+//     reads its first item's metadata before that wait.
 //   * The work counter is reset by the last CTA to finish, so the workspace
 //     counters are back at zero after every call (graph-replay safe).
 //   * Tokens past context_lens in the last tile are masked in S (select, not
