@@ -210,10 +210,14 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
 //     chunk never reads a row an earlier chunk wrote;
 //   * a chunk's sources may lie in the NEXT chunk's destination range, so a
 //     barrier separates the reads of chunk c from the writes of chunk c+1.
-// Rows with src == dst or an unresolved slot (< 0) are skipped.
+// Rows with src == dst or an unresolved slot (< 0) are skipped. `parts`
+// selects the arrays moved: 1 K, 2 V, 3 both (two CTAs may then share a
+// head's compaction, one array each, with no ordering between them).
 template <int kThreads = kCompressThreads, typename SlotFn>
 __device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
-                                       int num_kv_heads, int head, int n, SlotFn slots) {
+                                       int num_kv_heads, int head, int n, SlotFn slots,
+                                       int parts = 3) {
+  const bool do_k = (parts & 1) != 0, do_v = (parts & 2) != 0;
   constexpr int kChunkRows = kThreads / 4;
   const int t = threadIdx.x;
   const int row = t >> 2;      // kChunkRows rows x 4 threads
@@ -236,8 +240,8 @@ __device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_
       const uint4* vs = vptr(src);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        kc[u] = ks[u];
-        vc[u] = vs[u];
+        if (do_k) kc[u] = ks[u];
+        if (do_v) vc[u] = vs[u];
       }
     } else {
       dst_c = -1;
@@ -256,8 +260,8 @@ __device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_
         const uint4* vs = vptr(src);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          kn[u] = ks[u];
-          vn[u] = vs[u];
+          if (do_k) kn[u] = ks[u];
+          if (do_v) vn[u] = vs[u];
         }
       } else {
         dst_n = -1;
@@ -268,8 +272,8 @@ __device__ void compact_rows_pipelined(__nv_bfloat16* k_cache, __nv_bfloat16* v_
       uint4* vd = vptr(dst_c);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        kd[u] = kc[u];
-        vd[u] = vc[u];
+        if (do_k) kd[u] = kc[u];
+        if (do_v) vd[u] = vc[u];
       }
     }
     __syncthreads();

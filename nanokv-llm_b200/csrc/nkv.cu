@@ -301,6 +301,10 @@ int padded_group(int g) {
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
+// launch_threshold: the requested cluster does not fit this GPU (not a
+// public status; the caller falls back to smaller clusters).
+constexpr int kThresholdNoFit = 0x7fff0000;
+
 // Launches `kernel` (blocks of `threads`) with clusters of cluster_x CTAs
 // along x. `smem_set` is
 // the caller's per-kernel record of the dynamic shared-memory limit already
@@ -335,8 +339,46 @@ template <int G>
 int launch_threshold(const nkv::ThresholdCompressParams& p, int cluster_x, int grid_y,
                      size_t smem, cudaStream_t stream) {
   static size_t smem_set[kMaxDevices] = {0};
-  return launch_cluster(nkv::threshold_compress_kernel<G>, nkv::kThrThreads, smem_set, p,
-                        cluster_x, grid_y, smem, stream);
+  auto kernel = nkv::threshold_compress_kernel<G>;
+  if (cluster_x > 8) {
+    // a non-portable cluster size: allowed explicitly, and used only when
+    // such a cluster fits the GPU (else the caller plans 8-CTA clusters)
+    static bool nonportable[kMaxDevices] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) return NKV_ERR_CUDA;
+    if (!nonportable[dev]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+          cudaSuccess) {
+        cudaGetLastError();
+        return kThresholdNoFit;
+      }
+      nonportable[dev] = true;
+    }
+    if (smem > smem_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return cuda_status(e);
+      smem_set[dev] = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cluster_x, 1, 1);
+    cfg.blockDim = dim3(nkv::kThrThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster_x;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      return kThresholdNoFit;
+    }
+  }
+  return launch_cluster(kernel, nkv::kThrThreads, smem_set, p, cluster_x, grid_y, smem, stream);
 }
 
 template <int G>
@@ -1119,21 +1161,38 @@ int nkv_threshold_compress(const void* ring, int32_t num_ring_slots, int32_t num
   p.mtiles = (p.rows + 15) / 16;
   const int G = padded_group(g);
   if (G == 0) return NKV_ERR_UNSUPPORTED;
-  // As many 16-row m-tiles per row group as shared memory (and two warps
-  // per m-tile) allow; more groups re-stream the keys from L2.
-  int gm = std::min(p.mtiles, nkv::kThrWarps / 2);
-  while (gm > 0 && nkv::threshold_smem_bytes(G, p.keys_pad, gm, p.rows, compress_R) > kMaxSmem) --gm;
-  if (gm == 0) return NKV_ERR_UNSUPPORTED;
-  p.group_mtiles = gm;
-  const size_t smem = nkv::threshold_smem_bytes(G, p.keys_pad, gm, p.rows, compress_R);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (G) {
-    case 1: return launch_threshold<1>(p, num_kv_heads, num_selected, smem, s);
-    case 2: return launch_threshold<2>(p, num_kv_heads, num_selected, smem, s);
-    case 4: return launch_threshold<4>(p, num_kv_heads, num_selected, smem, s);
-    case 8: return launch_threshold<8>(p, num_kv_heads, num_selected, smem, s);
-    default: return launch_threshold<16>(p, num_kv_heads, num_selected, smem, s);
-  }
+  // halves CTAs per kv head, each scoring one range of the keys
+  auto run = [&](int halves) -> int {
+    p.halves = halves;
+    const int per = (p.num_keys + halves - 1) / halves;
+    p.keys_half = ((per + nkv::kThrKeyTile - 1) / nkv::kThrKeyTile) * nkv::kThrKeyTile;
+    // As many 16-row m-tiles per row group as shared memory (and two warps
+    // per m-tile) allow; more groups re-stream the keys from L2.
+    int gm = std::min(p.mtiles, nkv::kThrWarps / 2);
+    while (gm > 0 && nkv::threshold_smem_bytes(G, p.keys_pad, p.keys_half, gm, p.rows,
+                                                compress_R) > kMaxSmem)
+      --gm;
+    if (gm == 0) return NKV_ERR_UNSUPPORTED;
+    p.group_mtiles = gm;
+    const size_t smem =
+        nkv::threshold_smem_bytes(G, p.keys_pad, p.keys_half, gm, p.rows, compress_R);
+    const int cx = num_kv_heads * halves;
+    switch (G) {
+      case 1: return launch_threshold<1>(p, cx, num_selected, smem, s);
+      case 2: return launch_threshold<2>(p, cx, num_selected, smem, s);
+      case 4: return launch_threshold<4>(p, cx, num_selected, smem, s);
+      case 8: return launch_threshold<8>(p, cx, num_selected, smem, s);
+      default: return launch_threshold<16>(p, cx, num_selected, smem, s);
+    }
+  };
+  // Two CTAs per kv head (a 16-CTA cluster at 8 kv heads) halve each CTA's
+  // scoring, row statistics, window sums and compaction; where that cluster
+  // does not fit, one CTA per kv head.
+  int st = kThresholdNoFit;
+  if (num_kv_heads * 2 <= 16 && p.num_keys >= 2 * nkv::kThrKeyTile) st = run(2);
+  if (st == kThresholdNoFit || st == NKV_ERR_UNSUPPORTED) st = run(1);
+  return st == kThresholdNoFit ? NKV_ERR_UNSUPPORTED : st;
 }
 
 }  // extern "C"

@@ -86,6 +86,8 @@ struct ThresholdCompressParams {
   int rows;       // g * W
   int mtiles;     // ceil(rows / 16)
   int group_mtiles;  // m-tiles per row group (<= kThrWarps / 2)
+  int halves;     // CTAs per kv head (1 or 2), each taking one range of the keys
+  int keys_half;  // keys per CTA, a multiple of kThrKeyTile (keys_pad when halves = 1)
 };
 
 // 16 warps: two per 16-row m-tile in the scoring, and enough threads that
@@ -112,18 +114,21 @@ __host__ __device__ constexpr size_t thr_score_bytes(int group_mtiles, int rows,
 }
 
 // Shared-memory bytes of threshold_compress_kernel (host and device agree).
-__host__ __device__ constexpr size_t threshold_smem_bytes(int G, int keys_pad, int group_mtiles,
-                                                          int rows, int R) {
+// keys_half: the keys one CTA scores (its score rows, window sums, partial
+// and slots); keys_pad: all keys (the gathered importance for the top-k).
+__host__ __device__ constexpr size_t threshold_smem_bytes(int G, int keys_pad, int keys_half,
+                                                          int group_mtiles, int rows, int R) {
   return sizeof(__nv_bfloat16) * kThrKStages * kThrKeyTile * kThrKRowElems       // K tiles
-         + thr_score_bytes(group_mtiles, rows, keys_pad, R)                      // scores
+         + thr_score_bytes(group_mtiles, rows, keys_half, R)                     // scores
          + sizeof(float) * 2 * group_mtiles * 16                                 // row max, sum
-         + sizeof(float) * static_cast<size_t>(G) * keys_pad                     // window sums
-         + sizeof(float) * keys_pad                                              // partial
+         + sizeof(float) * 4 * group_mtiles * 16                                 // exchange (2 x max, sum)
+         + sizeof(float) * static_cast<size_t>(G) * keys_half                    // window sums
+         + sizeof(float) * keys_half                                             // partial
          + sizeof(uint16_t) * (keys_pad + 2)                                     // keys
          + sizeof(int) * R                                                       // final index
          + sizeof(float) * kThrReduceSlots                                       // reductions
          + sizeof(int) * 256                                                     // top-k histogram
-         + sizeof(int) * keys_pad;                                               // key slots
+         + sizeof(int) * keys_half;                                              // key slots
 }
 
 template <int G>
@@ -131,37 +136,48 @@ __global__ void __launch_bounds__(kThrThreads, 1)
 threshold_compress_kernel(const ThresholdCompressParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   cg::cluster_group cluster = cg::this_cluster();
-  const int head = static_cast<int>(cluster.block_rank());
+  // cluster rank = kv head * halves + half; half h scores keys
+  // [h * keys_half, (h + 1) * keys_half)
+  const int H = p.halves;
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int head = rank / H;
+  const int half = rank - head * H;
   const int sel_i = blockIdx.y;
   const int g = p.g;
   const int nk = p.num_keys;
   const int kp = p.keys_pad;
+  const int kh = p.keys_half;
+  const int k0 = half * kh;                  // this CTA's first key
+  const int nkl = max(0, min(nk - k0, kh));  // its real keys
   const int bs = p.block_size;
   const int W = p.window;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int ss = thr_score_stride(kp);
+  const int ss = thr_score_stride(kh);
+  const int gm16 = p.group_mtiles * 16;
 
   __nv_bfloat16* ktile = reinterpret_cast<__nv_bfloat16*>(smem);           // [3][64][136]
   __nv_bfloat16* sc = ktile + kThrKStages * kThrKeyTile * kThrKRowElems;   // [group rows][ss]
   float* rmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sc) +
-                                         thr_score_bytes(p.group_mtiles, p.rows, kp, p.R));
-  float* rsum = rmax + p.group_mtiles * 16;
-  float* kacc = rsum + p.group_mtiles * 16;                                 // [G][kp]
-  float* partial = kacc + G * kp;                                           // [kp]
-  uint16_t* keys = reinterpret_cast<uint16_t*>(partial + kp);               // [kp]
+                                         thr_score_bytes(p.group_mtiles, p.rows, kh, p.R));
+  float* rsum = rmax + gm16;
+  float* xchg = rsum + gm16;                                                // [2][max, sum][gm16] (cluster-visible)
+  float* kacc = xchg + 4 * gm16;                                            // [G][kh]
+  float* partial = kacc + G * kh;                                           // [kh] (cluster-visible)
+  uint16_t* keys = reinterpret_cast<uint16_t*>(partial + kh);               // [kp] (cluster-visible)
   int* final_idx = reinterpret_cast<int*>(keys + kp + 2);                   // [R]
   float* red = reinterpret_cast<float*>(final_idx + p.R);                   // [kThrReduceSlots]
   int* hist = reinterpret_cast<int*>(red + kThrReduceSlots);                // [256]
-  int* kslot = hist + 256;                                                  // [kp] cache slot of key t
+  int* kslot = hist + 256;                                                  // [kh] cache slot of key k0 + t
   __shared__ int s_valid;
   __shared__ int s_start;
 
-  // The kv heads of a sequence are the CTAs of one cluster (their partial
-  // sums meet in distributed shared memory). A launch that lost its
-  // clusters (%cluster_nctarank 1) cannot form them: flag it and write
-  // nothing (the condition is uniform, so no CTA waits at a cluster barrier).
-  if (static_cast<int>(cluster.num_blocks()) != p.num_kv_heads) {
+  // The kv heads (and key halves) of a sequence are the CTAs of one cluster
+  // (row statistics, partial sums and importance meet in distributed shared
+  // memory). A launch that lost its clusters (%cluster_nctarank 1) cannot
+  // form them: flag it and write nothing (the condition is uniform, so no
+  // CTA waits at a cluster barrier).
+  if (static_cast<int>(cluster.num_blocks()) != p.num_kv_heads * H) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) raise_error(NKV_DEVERR_LAUNCH_SHAPE);
     return;
   }
@@ -183,15 +199,15 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     // every key / source / destination position must resolve to a cache slot
     if (valid && (slot_of(p.S - 1) < 0 || slot_of(s_start + p.S - 1) < 0 || slot_of(0) < 0))
       valid = 0;
-    if (!valid && head == 0) raise_error(NKV_DEVERR_COMPRESS_RANGE);
+    if (!valid && rank == 0) raise_error(NKV_DEVERR_COMPRESS_RANGE);
     s_valid = valid;
   }
-  for (int i = threadIdx.x; i < G * kp; i += kThrThreads) kacc[i] = 0.f;
+  for (int i = threadIdx.x; i < G * kh; i += kThrThreads) kacc[i] = 0.f;
   // every key's cache slot, resolved once (-1: unresolved or padding)
-  for (int t = threadIdx.x; t < kp; t += kThrThreads)
-    kslot[t] = t < nk ? static_cast<int>(slot_of(t)) : -1;
+  for (int t = threadIdx.x; t < kh; t += kThrThreads)
+    kslot[t] = t < nkl ? static_cast<int>(slot_of(k0 + t)) : -1;
   __syncthreads();
-  const bool valid = s_valid != 0;
+  const bool valid = s_valid != 0;  // identical in every CTA of the cluster
   const int start = s_start;
 
   if (valid) {
@@ -199,7 +215,7 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     const __nv_bfloat16* qbase =
         p.ring + (static_cast<int64_t>(rslot) * p.num_layers + p.layer_id) *
                      static_cast<int64_t>(W) * p.num_q_heads * kCompressHeadDim;
-    const int ntiles = kp / kThrKeyTile;
+    const int ntiles = kh / kThrKeyTile;
     // query row rho = r * W + w of this group -> its 128 bf16 values (or null)
     auto qrow = [&](int rho) -> const __nv_bfloat16* {
       if (rho >= p.rows) return nullptr;
@@ -223,11 +239,12 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
       cp_async_commit();
     };
 
+    int group_parity = 0;
     for (int group0 = 0; group0 < p.mtiles; group0 += p.group_mtiles) {
       const int gm = min(p.group_mtiles, p.mtiles - group0);
       const int row0 = group0 * 16;
-      // ---- A: scores of this row group; warps 2m and 2m + 1 take m-tile m,
-      // each half of every key tile's eight 8-key columns
+      // ---- A: scores of this row group over this CTA's keys; warps 2m and
+      // 2m + 1 take m-tile m, each half of every key tile's eight columns
       uint32_t qa[8][4];
       const int mt = warp >> 1;
       const int nt0 = (warp & 1) * (kThrKeyTile / 16);
@@ -282,11 +299,11 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
               mma_bf16_16816(acc, qa[2 * kq + 1][0], qa[2 * kq + 1][1], qa[2 * kq + 1][2],
                              qa[2 * kq + 1][3], b2, b3);
             }
-            const int t0 = tile * kThrKeyTile + nt * 8 + 2 * tig;
+            const int t0 = tile * kThrKeyTile + nt * 8 + 2 * tig;  // local key
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const int t = t0 + (e & 1);
+              const int t = k0 + t0 + (e & 1);  // global key
               v[e] = (t == 0 || t >= nk) ? -INFINITY : round_bf16(round_bf16(acc[e]) * p.scale);
             }
             // rows past the group's real rows (m-tile padding) have no storage
@@ -300,23 +317,43 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
         }
       }
       __syncthreads();  // scores complete; the ring's buffers are free
-      // ---- B: per-row max and sum of exp
+      // ---- B: per-row max and sum of exp over all keys. With two halves
+      // each CTA reduces its own keys and the pair exchanges through
+      // distributed shared memory (buffers by group parity: rewritten two
+      // groups later, after the partner has passed this group's barriers):
+      // the max, then the sum, the sum added in half order so both agree.
+      float* xmax = xchg + group_parity * 2 * gm16;
+      float* xsum = xmax + gm16;
+      const float* pmax = H > 1 ? cluster.map_shared_rank(xmax, rank ^ 1) : nullptr;
+      const float* psum = H > 1 ? cluster.map_shared_rank(xsum, rank ^ 1) : nullptr;
       for (int lr = warp; lr < grows; lr += kThrWarps) {
         const __nv_bfloat16* row = sc + static_cast<size_t>(lr) * ss;
         float m = -INFINITY;
-        for (int t = lane; t < nk; t += 32) m = fmaxf(m, __bfloat162float(row[t]));
+        for (int t = lane; t < nkl; t += 32) m = fmaxf(m, __bfloat162float(row[t]));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) xmax[lr] = m;
+      }
+      if (H > 1) cluster.sync();
+      else __syncthreads();
+      for (int lr = warp; lr < grows; lr += kThrWarps) {
+        const __nv_bfloat16* row = sc + static_cast<size_t>(lr) * ss;
+        const float m = H > 1 ? fmaxf(xmax[lr], pmax[lr]) : xmax[lr];
         float z = 0.f;
-        for (int t = lane; t < nk; t += 32) z += expf(__bfloat162float(row[t]) - m);
+        for (int t = lane; t < nkl; t += 32) z += expf(__bfloat162float(row[t]) - m);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
         if (lane == 0) {
           rmax[lr] = m;
-          rsum[lr] = z;
+          xsum[lr] = z;
         }
       }
+      if (H > 1) cluster.sync();
+      else __syncthreads();
+      for (int lr = threadIdx.x; lr < grows; lr += kThrThreads)
+        rsum[lr] = H > 1 ? (half == 0 ? xsum[lr] + psum[lr] : psum[lr] + xsum[lr]) : xsum[lr];
       __syncthreads();
+      group_parity ^= 1;
       // ---- C: per (key, head), window-ordered sum of the head's bf16
       // probabilities. A head's rows in this group are summed in a register,
       // continuing the head's running sum from earlier groups (the same fp32
@@ -324,43 +361,55 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
       // and divisions of successive rows do not depend on each other and
       // overlap.
       const int r_first = row0 / W;
-      const int ntask = ((row0 + grows - 1) / W - r_first + 1) * nk;
+      const int ntask = ((row0 + grows - 1) / W - r_first + 1) * nkl;
       for (int task = threadIdx.x; task < ntask; task += kThrThreads) {
-        const int r = r_first + task / nk;
-        const int t = task - (r - r_first) * nk;
+        const int r = r_first + task / nkl;
+        const int t = task - (r - r_first) * nkl;
         const int lr_end = min(grows, (r + 1) * W - row0);
-        float acc = kacc[r * kp + t];
+        float acc = kacc[r * kh + t];
 #pragma unroll 4
         for (int lr = max(r * W - row0, 0); lr < lr_end; ++lr) {
           const float e = expf(__bfloat162float(sc[static_cast<size_t>(lr) * ss + t]) - rmax[lr]);
           acc += round_bf16(e / rsum[lr]);
         }
-        kacc[r * kp + t] = acc;
+        kacc[r * kh + t] = acc;
       }
       __syncthreads();
     }
-    for (int t = threadIdx.x; t < kp; t += kThrThreads) {
+    for (int t = threadIdx.x; t < kh; t += kThrThreads) {
       float s = 0.f;
-      if (t < nk) {
+      if (t < nkl) {
 #pragma unroll
         for (int r = 0; r < G; ++r)
-          if (r < g) s += round_bf16(kacc[r * kp + t]);
+          if (r < g) s += round_bf16(kacc[r * kh + t]);
       }
       partial[t] = s;
     }
   }
   cluster.sync();
   if (valid) {
-    const int nranks = static_cast<int>(cluster.num_blocks());
-    for (int t = threadIdx.x; t < kp; t += kThrThreads) {
+    // this CTA's keys: the sum over the heads (CTAs of the same half, in head
+    // order), rounded to bf16 -- the reference's sum(dim=1)
+    for (int t = threadIdx.x; t < nkl; t += kThrThreads) {
       float s = 0.f;
-      for (int c = 0; c < nranks; ++c) s += cluster.map_shared_rank(partial, c)[t];
-      keys[t] = (t < nk) ? static_cast<uint16_t>(bf16_key(s)) : 0;
-      if (head == 0 && p.out_importance != nullptr && t < nk)
-        p.out_importance[static_cast<int64_t>(sel_i) * nk + t] = keys[t];
+      for (int hd = 0; hd < p.num_kv_heads; ++hd)
+        s += cluster.map_shared_rank(partial, hd * H + half)[t];
+      keys[k0 + t] = static_cast<uint16_t>(bf16_key(s));
+      if (head == 0 && p.out_importance != nullptr)
+        p.out_importance[static_cast<int64_t>(sel_i) * nk + k0 + t] = keys[k0 + t];
     }
   }
-  cluster.sync();
+  cluster.sync();  // no CTA may leave while a peer still reads its partials
+  if (H > 1) {
+    // the other half's keys, from the partner CTA of the same head
+    if (valid) {
+      const int pk0 = (half ^ 1) * kh;
+      const int pn = max(0, min(nk - pk0, kh));
+      const uint16_t* pkeys = cluster.map_shared_rank(keys, rank ^ 1);
+      for (int t = threadIdx.x; t < pn; t += kThrThreads) keys[pk0 + t] = pkeys[pk0 + t];
+    }
+    cluster.sync();  // ... nor while its partner still reads its keys
+  }
   if (!valid) return;
 
   const int num_keep = p.R - W - 1;
@@ -379,12 +428,14 @@ threshold_compress_kernel(const ThresholdCompressParams p) {
     dst_slot[i] = static_cast<int>(slot_of(i));
   }
   __syncthreads();
+  // with two CTAs per head, one moves the K rows and the other the V rows
   compact_rows_pipelined<kThrThreads>(p.k_cache, p.v_cache, p.num_kv_heads, head, p.R,
                                       [&](int i, int64_t& src, int64_t& dst) {
                                         src = src_slot[i];
                                         dst = dst_slot[i];
-                                      });
-  if (head == 0) {
+                                      },
+                                      H > 1 ? 1 + half : 3);
+  if (rank == 0) {
     if (threadIdx.x == 0) p.context_lens[b] = p.R;
     if (p.out_keep_idx) {
       for (int i = threadIdx.x; i < p.R; i += kThrThreads)
