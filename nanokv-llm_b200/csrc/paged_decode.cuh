@@ -170,6 +170,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   int* meta = reinterpret_cast<int*>(slot_empty + kSlots);
   volatile int* flags = meta + kStages * kDecodeMetaInts;  // [0] abort
   uint64_t* recv_bar = reinterpret_cast<uint64_t*>(smem + S::kRecvBarOffset);
+  // cluster launches: the consumer warps' own merge (two phases, 128 arrivals)
+  uint64_t* merge_bar = recv_bar + 1;
   float* recv = reinterpret_cast<float*>(smem + S::kRecvOffset);
   // Cluster split mode needs the launch's clusters; a launch that lost them
   // (%cluster_nctarank 1) merges its splits through global memory instead.
@@ -198,7 +200,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     }
     // the leader's receive barrier: its own arrival (with the expected
     // bytes) plus the splits' asynchronous stores
-    if (cluster_mode) mbar_init(smem_u32(recv_bar), 1);
+    if (cluster_mode) {
+      mbar_init(smem_u32(recv_bar), 1);
+      mbar_init(smem_u32(merge_bar), kDecodeConsumerWarps * 32);
+    }
     flags[0] = 0;
     fence_barrier_init();
   }
@@ -559,19 +564,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
                            static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
                        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
-        } else if (cluster_mode && s == 0) {
-          // the leader's own split: straight into its receive rows
-          float* r = recv + row * kRecvRowFloats;
-          *reinterpret_cast<float4*>(r + d0) = acc;
-          if (lane == 0) *reinterpret_cast<float2*>(r + kDecodeHeadDim) = make_float2(M, L);
-        } else if (cluster_mode) {
-          // this split's row into the leader's receive rows, counted on its
-          // receive barrier (nothing to wait for here)
-          const uint32_t dst =
-              mapa_shared(smem_u32(recv + (s * G + row) * kRecvRowFloats), 0);
-          const uint32_t rbar = mapa_shared(smem_u32(recv_bar), 0);
-          st_async_f32x4(dst + 4 * d0, acc, rbar);
-          if (lane == 0) st_async_f32x2(dst + 4 * kDecodeHeadDim, M, L, rbar);
         } else {
           const int64_t pidx = (static_cast<int64_t>(pair) * p.max_splits + s) * g + row;
           *reinterpret_cast<float4*>(p.part_o + pidx * kDecodeHeadDim + d0) = acc;
@@ -584,43 +576,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       // hand-off so the consumers never wait on the split protocol.
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&slot_empty[slot]));
-      if (nsplit > 1 && cluster_mode) {
-        // The leader (split 0) expects the other splits' rows, waits for them
-        // to land, then merges the splits in order. Splits past the row's end
-        // send nothing and are not expected.
-        if (s == 0) {
-          __syncwarp();  // its own rows, stored by all lanes, are visible to all
-          if (lane == 0)
-            mbar_arrive_expect_tx(smem_u32(recv_bar),
-                                  static_cast<uint32_t>((nsplit - 1) * g * (4 * kDecodeHeadDim + 8)));
-          if (mbar_wait_cluster_bounded(smem_u32(recv_bar), 0)) {
-            for (int row = 0; row < g; ++row) {
-              float M = NEG_INF;
-              for (int s2 = 0; s2 < nsplit; ++s2)
-                M = fmaxf(M, recv[(s2 * G + row) * kRecvRowFloats + kDecodeHeadDim]);
-              float L = 0.f;
-              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-              for (int s2 = 0; s2 < nsplit; ++s2) {
-                const float* r = recv + (s2 * G + row) * kRecvRowFloats;
-                const float ms = r[kDecodeHeadDim];
-                const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
-                L += r[kDecodeHeadDim + 1] * f;
-                const float4 po = *reinterpret_cast<const float4*>(r + d0);
-                acc.x += po.x * f;
-                acc.y += po.y * f;
-                acc.z += po.z * f;
-                acc.w += po.w * f;
-              }
-              const float inv = (L > 0.f) ? 1.f / L : 0.f;
-              store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
-                               static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
-                           make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
-            }
-          } else {
-            flags[0] = 1;
-          }
-        }
-      } else if (nsplit > 1) {
+      if (nsplit > 1) {
         // __syncwarp orders the lanes' partial stores before lane 0's
         // gpu-scope release; the acquire half of the same atomic makes the
         // other splits' partials visible to the last arriver (and, through
@@ -809,15 +765,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   uint32_t cphase = 0;
   // Hands the warp states of one item (or the end marker, item < 0) to the
   // merger through the next slot.
-  auto handoff = [&](int item, int nsplit) -> bool {
-    if (!mbar_wait_bounded(smem_u32(&slot_empty[cslot]), cphase ^ 1u)) {
-      flags[0] = 1;
-      return false;
-    }
-    if (item >= 0 && kSwapAB) {
+  // This warp's raw (m, l, O) rows into hand-off slot `sl`.
+  auto write_state = [&](int sl) {
+    if (kSwapAB) {
       // o[dm][c]: O^T rows dims 16 dm + gid (c 0, 1) and + 8 (c 2, 3),
       // columns heads 2 tig (c even) and 2 tig + 1 (c odd)
-      float* so = slot_o(cslot);
+      float* so = slot_o(sl);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float l = l_run[e];
@@ -827,8 +780,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         const int h = 2 * tig + e;
         if (h < g) {
           if (gid == 0) {
-            slot_m(cslot)[cw * G + h] = m_run[e];
-            slot_l(cslot)[cw * G + h] = l;
+            slot_m(sl)[cw * G + h] = m_run[e];
+            slot_l(sl)[cw * G + h] = l;
           }
           float* dst = so + (cw * G + h) * S::kORowStride;
 #pragma unroll
@@ -838,9 +791,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           }
         }
       }
-    } else if (item >= 0) {
+    } else {
       constexpr int kRowSets = (G == 16) ? 2 : 1;
-      float* so = slot_o(cslot);
+      float* so = slot_o(sl);
 #pragma unroll
       for (int rs = 0; rs < kRowSets; ++rs) {
         float l = l_run[rs];
@@ -849,8 +802,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         const int row = gid + 8 * rs;
         if (row < g) {
           if (tig == 0) {
-            slot_m(cslot)[cw * G + row] = m_run[rs];
-            slot_l(cslot)[cw * G + row] = l;
+            slot_m(sl)[cw * G + row] = m_run[rs];
+            slot_l(sl)[cw * G + row] = l;
           }
           float* dst = so + (cw * G + row) * S::kORowStride;
 #pragma unroll
@@ -860,6 +813,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         }
       }
     }
+  };
+  auto handoff = [&](int item, int nsplit) -> bool {
+    if (!mbar_wait_bounded(smem_u32(&slot_empty[cslot]), cphase ^ 1u)) {
+      flags[0] = 1;
+      return false;
+    }
+    if (item >= 0) write_state(cslot);
     if (threadIdx.x == 0) {
       slot_hdr(cslot)[0] = item;
       slot_hdr(cslot)[1] = nsplit;
@@ -1115,6 +1075,106 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     }
 
     if (j + 1 < ntiles) continue;
+    if (cluster_mode) {
+      // A cluster launch gives each CTA one item: the consumer warps merge
+      // their own states (no hand-off to the merger warp, which here only
+      // receives the end marker) and send the split's rows to the leader's
+      // receive rows, or, in the leader, gather the splits and write the
+      // output. Slot 0 holds the warp states (the end marker's hand-off
+      // writes only its header).
+      write_state(0);
+      // all four warps' states in place (a bounded wait: a warp that gave
+      // up earlier leaves the others to time out, not to hang)
+      mbar_arrive(smem_u32(merge_bar));
+      if (!mbar_wait_bounded(smem_u32(merge_bar), 0)) {
+        flags[0] = 1;
+        continue;
+      }
+      const int kvh = item % Hk;
+      const int rest = item / Hk;
+      const int b = rest % p.batch;
+      const int s = rest / p.batch;
+      const int d0 = 4 * lane;
+      const float* so = slot_o(0);
+      const float* smv = slot_m(0);
+      const float* slv = slot_l(0);
+      for (int row = cw; row < g; row += kDecodeConsumerWarps) {
+        float M = NEG_INF;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, smv[w * G + row]);
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+          const float mw = smv[w * G + row];
+          const float f = (mw == NEG_INF) ? 0.f : fast_exp2(mw - M);
+          L += slv[w * G + row] * f;
+          const float4 ow =
+              *reinterpret_cast<const float4*>(so + (w * G + row) * S::kORowStride + d0);
+          acc.x += ow.x * f;
+          acc.y += ow.y * f;
+          acc.z += ow.z * f;
+          acc.w += ow.w * f;
+        }
+        if (nsplit == 1) {
+          const float inv = (L > 0.f) ? 1.f / L : 0.f;
+          store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
+                           static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
+                       make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        } else if (s == 0) {
+          float* r = recv + row * kRecvRowFloats;  // the leader's own split
+          *reinterpret_cast<float4*>(r + d0) = acc;
+          if (lane == 0) *reinterpret_cast<float2*>(r + kDecodeHeadDim) = make_float2(M, L);
+        } else {
+          // into the leader's receive rows, counted on its receive barrier
+          const uint32_t dst = mapa_shared(smem_u32(recv + (s * G + row) * kRecvRowFloats), 0);
+          const uint32_t rbar = mapa_shared(smem_u32(recv_bar), 0);
+          st_async_f32x4(dst + 4 * d0, acc, rbar);
+          if (lane == 0) st_async_f32x2(dst + 4 * kDecodeHeadDim, M, L, rbar);
+        }
+      }
+      if (nsplit > 1 && s == 0) {
+        // The leader expects the other splits' rows (splits past the row's
+        // end send nothing), waits for them to land, then merges the splits
+        // in order.
+        // its own rows are visible to all its warps
+        mbar_arrive(smem_u32(merge_bar));
+        if (!mbar_wait_bounded(smem_u32(merge_bar), 1)) {
+          flags[0] = 1;
+          continue;
+        }
+        if (threadIdx.x == 0)
+          mbar_arrive_expect_tx(smem_u32(recv_bar),
+                                static_cast<uint32_t>((nsplit - 1) * g * (4 * kDecodeHeadDim + 8)));
+        if (mbar_wait_cluster_bounded(smem_u32(recv_bar), 0)) {
+          for (int row = cw; row < g; row += kDecodeConsumerWarps) {
+            float M = NEG_INF;
+            for (int s2 = 0; s2 < nsplit; ++s2)
+              M = fmaxf(M, recv[(s2 * G + row) * kRecvRowFloats + kDecodeHeadDim]);
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s2 = 0; s2 < nsplit; ++s2) {
+              const float* r = recv + (s2 * G + row) * kRecvRowFloats;
+              const float ms = r[kDecodeHeadDim];
+              const float f = (ms == NEG_INF) ? 0.f : fast_exp2(ms - M);
+              L += r[kDecodeHeadDim + 1] * f;
+              const float4 po = *reinterpret_cast<const float4*>(r + d0);
+              acc.x += po.x * f;
+              acc.y += po.y * f;
+              acc.z += po.z * f;
+              acc.w += po.w * f;
+            }
+            const float inv = (L > 0.f) ? 1.f / L : 0.f;
+            store_bf16x4(p.out + static_cast<int64_t>(b) * p.out_stride_token +
+                             static_cast<int64_t>(kvh * g + row) * kDecodeHeadDim + d0,
+                         make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+          }
+        } else {
+          flags[0] = 1;
+        }
+      }
+      continue;
+    }
     if (!handoff(item, nsplit)) break;
   }
   // Consumers leave only after the producer's end marker (or an abort), so
