@@ -260,11 +260,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
     // slot-mapping entry and query-window slot / position (lanes 0-3) and 32
     // block-table entries from its split's first block (one per lane).
     auto meta_loads = [&](int it, int& scalar, int& bt) {
-      const int kvh_ = it % Hk;
       const int rest_ = it / Hk;
       const int b_ = rest_ % p.batch;
       const int s_ = rest_ / p.batch;
-      (void)kvh_;
       scalar = 0;
       if (lane == 0) {
         scalar = ldg_nc_s32(p.context_lens + b_);
@@ -279,26 +277,91 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       if (blk0 + lane < p.max_blocks)
         bt = ldg_nc_s32(p.block_tables + static_cast<int64_t>(b_) * p.max_blocks + blk0 + lane);
     };
-    // With metadata_ready the first item's metadata is requested before the
-    // dependency wait, so it arrives while the previous kernel drains.
+    // Everything about an item that follows from its metadata (no data of
+    // the kernel this launch depends on): computed before the dependency
+    // wait for a CTA's first item when metadata_ready.
+    struct ItemPlan {
+      int item, kvh, b, s, t0, blk_first, bt_ent;
+      int len, nsplit, t1, ntiles;
+      int slot_new, ring_slot, ring_pos;
+      int patch_row;  // >= 0: the new token's row inside the item's last tile
+      int tile0_slot; // first slot of the item's first tile (or the zero-fill coordinate)
+      bool skip;      // no such split
+    };
+    // Block index of the cache block holding token position `tok` of the row.
+    auto block_of = [&](const ItemPlan& P, int tok) -> int {
+      const int bi = tok / p.block_size - P.blk_first;
+      int blk = __shfl_sync(0xffffffffu, P.bt_ent, bi & 31);
+      if (bi >= 32)
+        blk = __ldg(p.block_tables + static_cast<int64_t>(P.b) * p.max_blocks + tok / p.block_size);
+      return blk;
+    };
+    // Slot of the tile starting at `tok` (fully out of range: TMA fills zeros).
+    auto tile_slot = [&](const ItemPlan& P, int tok) -> int {
+      const int blk = block_of(P, tok);
+      const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
+      if (!blk_ok && leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
+      return blk_ok ? blk * p.block_size + (tok % p.block_size) : -2 * kDecodeTileTokens;
+    };
+    auto make_plan = [&](int it, int scalar, int bt) -> ItemPlan {
+      ItemPlan P;
+      P.item = it;
+      P.kvh = it % Hk;
+      const int rest = it / Hk;
+      P.b = rest % p.batch;
+      P.s = rest / p.batch;
+      P.t0 = P.s * p.chunk_tokens;
+      P.blk_first = P.t0 / p.block_size;
+      P.bt_ent = bt;
+      int len = __shfl_sync(0xffffffffu, scalar, 0);
+      // a length past the row's block table is clamped (and flagged) so that
+      // no block-table read leaves the row
+      if (len > p.max_blocks * p.block_size) {
+        if (leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
+        len = p.max_blocks * p.block_size;
+      }
+      P.len = len;
+      P.slot_new = __shfl_sync(0xffffffffu, scalar, 1);
+      P.ring_slot = __shfl_sync(0xffffffffu, scalar, 2);
+      P.ring_pos = __shfl_sync(0xffffffffu, scalar, 3);
+      P.nsplit = len > 0 ? (len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
+      P.skip = P.s >= P.nsplit;
+      P.t1 = min(P.t0 + p.chunk_tokens, len);
+      P.ntiles = (len > 0 && !P.skip) ? (P.t1 - P.t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
+      // Fused slot write: the current token (position len - 1) lives in the
+      // last split's last tile. Its K/V head slice goes to the cache and,
+      // so that the tile's load need not wait for that write, into the
+      // tile's shared-memory copy once the TMA has landed.
+      P.patch_row = -1;
+      if (p.new_k != nullptr && !P.skip && P.s == P.nsplit - 1 && P.ntiles > 0) {
+        const int blk = block_of(P, len - 1);
+        const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
+        const int64_t want =
+            blk_ok ? static_cast<int64_t>(blk) * p.block_size + (len - 1) % p.block_size : -1;
+        if (P.slot_new >= 0 && P.slot_new == want) {
+          P.patch_row = (len - 1) - (P.t0 + (P.ntiles - 1) * kDecodeTileTokens);
+        } else if (P.slot_new != -1 && leader) {
+          raise_error(NKV_DEVERR_STORE_SLOT);
+        }
+      }
+      P.tile0_slot = P.ntiles > 0 ? tile_slot(P, P.t0) : 0;
+      return P;
+    };
+    // With metadata_ready the first item's metadata is requested and planned
+    // before the dependency wait, so it is ready while the previous kernel
+    // drains; its first K/V tile is also requested into L2 (a hint: the
+    // loads after the wait read the coherent data).
     const bool early = p.metadata_ready != 0 && static_item < p.total_items;
-    int pre_scalar = 0, pre_bt = -1;
+    ItemPlan pre;
     if (early) {
-      meta_loads(static_item, pre_scalar, pre_bt);
-      // ... and its first K/V tile is requested into L2 (a hint: the loads
-      // after the wait read the coherent data), which also brings the
-      // tensor maps' first use forward
-      const int len0 = __shfl_sync(0xffffffffu, pre_scalar, 0);
-      const int s0 = static_item / Hk / p.batch;
-      const int tok0 = s0 * p.chunk_tokens;
-      const int blk = __shfl_sync(0xffffffffu, pre_bt, 0);
-      if (leader && tok0 < len0 && blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks) {
-        const int kvh0 = static_item % Hk;
-        const int slot0 = blk * p.block_size + tok0 % p.block_size;
-        tma_prefetch_l2_3d(&tm_k, 0, kvh0, slot0);
-        tma_prefetch_l2_3d(&tm_k, 64, kvh0, slot0);
-        tma_prefetch_l2_3d(&tm_v, 0, kvh0, slot0);
-        tma_prefetch_l2_3d(&tm_v, 64, kvh0, slot0);
+      int sc0, bt0;
+      meta_loads(static_item, sc0, bt0);
+      pre = make_plan(static_item, sc0, bt0);
+      if (leader && pre.ntiles > 0 && pre.tile0_slot >= 0) {
+        tma_prefetch_l2_3d(&tm_k, 0, pre.kvh, pre.tile0_slot);
+        tma_prefetch_l2_3d(&tm_k, 64, pre.kvh, pre.tile0_slot);
+        tma_prefetch_l2_3d(&tm_v, 0, pre.kvh, pre.tile0_slot);
+        tma_prefetch_l2_3d(&tm_v, 64, pre.kvh, pre.tile0_slot);
       }
     }
     grid_dependency_wait();
@@ -318,82 +381,38 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       }
       static_item = -1;
       if (item >= p.total_items) break;
-      const int kvh = item % Hk;
-      const int rest = item / Hk;
-      const int b = rest % p.batch;
-      const int s = rest / p.batch;
-      const int t0 = s * p.chunk_tokens;
-      const int blk_first = t0 / p.block_size;
-      int scalar, bt_ent;
+      ItemPlan P;
       if (first && early) {
-        scalar = pre_scalar;
-        bt_ent = pre_bt;
+        P = pre;
       } else {
-        meta_loads(item, scalar, bt_ent);
+        int sc, bt;
+        meta_loads(item, sc, bt);
+        P = make_plan(item, sc, bt);
       }
       first = false;
+      if (P.skip) continue;
       // The data rows come from the kernel this launch depends on (after the
-      // wait): the new K/V head rows of the fused slot write (lanes 0-15 K,
-      // 16-31 V) and the group's q rows for the KvChat query window.
+      // wait) and are needed only after the item's tiles are requested: the
+      // new K/V head rows of the fused slot write (lanes 0-15 K, 16-31 V)
+      // and the group's q rows for the KvChat query window.
       uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
-      if (p.new_k != nullptr) {
-        const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
-        new_row = ldg_nc_v4(lane < kHeadVecs ? p.new_k + static_cast<int64_t>(b) * p.new_k_stride_vec + col
-                                             : p.new_v + static_cast<int64_t>(b) * p.new_v_stride_vec + col);
+      if (P.patch_row >= 0) {
+        const int64_t col = static_cast<int64_t>(P.kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
+        new_row = ldg_nc_v4(lane < kHeadVecs ? p.new_k + static_cast<int64_t>(P.b) * p.new_k_stride_vec + col
+                                             : p.new_v + static_cast<int64_t>(P.b) * p.new_v_stride_vec + col);
       }
       constexpr int kQVecsPerLane = G >= 2 ? G / 2 : 1;
       const int q_vecs = g * kHeadVecs;  // the group's q rows
+      const bool ring_append = p.ring_vec != nullptr && P.s == 0 && P.ring_slot >= 0;
       uint4 q_rows[kQVecsPerLane];
-      if (p.ring_vec != nullptr && s == 0) {
-        const uint4* src = p.q_vec + static_cast<int64_t>(b) * p.q_stride_token_vec +
-                           static_cast<int64_t>(kvh) * q_vecs;
+      if (ring_append) {
+        const uint4* src = p.q_vec + static_cast<int64_t>(P.b) * p.q_stride_token_vec +
+                           static_cast<int64_t>(P.kvh) * q_vecs;
 #pragma unroll
         for (int i = 0; i < kQVecsPerLane; ++i)
           if (lane + 32 * i < q_vecs) q_rows[i] = ldg_nc_v4(src + lane + 32 * i);
       }
-      int len = __shfl_sync(0xffffffffu, scalar, 0);
-      // a length past the row's block table is clamped (and flagged) so that
-      // no block-table read leaves the row
-      if (len > p.max_blocks * p.block_size) {
-        if (leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
-        len = p.max_blocks * p.block_size;
-      }
-      const int slot_new = __shfl_sync(0xffffffffu, scalar, 1);
-      const int ring_slot = __shfl_sync(0xffffffffu, scalar, 2);
-      const int ring_pos = __shfl_sync(0xffffffffu, scalar, 3);
-      // Block index of the cache block holding token position `tok` of row b.
-      auto block_of = [&](int tok) -> int {
-        const int bi = tok / p.block_size - blk_first;
-        int blk = __shfl_sync(0xffffffffu, bt_ent, bi & 31);
-        if (bi >= 32) blk = __ldg(p.block_tables + static_cast<int64_t>(b) * p.max_blocks +
-                                  tok / p.block_size);
-        return blk;
-      };
-
-      const int nsplit = len > 0 ? (len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
-      if (s >= nsplit) continue;
-      const int t1 = min(t0 + p.chunk_tokens, len);
-      const int ntiles = len > 0 ? (t1 - t0 + kDecodeTileTokens - 1) / kDecodeTileTokens : 0;
-      // Fused slot write: the current token (position len - 1) lives in the
-      // last split's last tile. Its K/V head slice goes to the cache, and --
-      // so that the tile's load need not wait for that write -- into the
-      // tile's shared-memory copy once the TMA has landed, before the
-      // consumers are released (patch_row >= 0: the row inside that tile).
-      int patch_row = -1;
-      if (p.new_k != nullptr && s == nsplit - 1 && ntiles > 0) {
-        const int blk = block_of(len - 1);
-        const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
-        const int64_t want =
-            blk_ok ? static_cast<int64_t>(blk) * p.block_size + (len - 1) % p.block_size : -1;
-        if (slot_new >= 0 && slot_new == want) {
-          const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
-          uint4* dst = lane < kHeadVecs ? p.k_cache_vec : p.v_cache_vec;
-          dst[static_cast<int64_t>(slot_new) * row_vecs + col] = new_row;
-          patch_row = (len - 1) - (t0 + (ntiles - 1) * kDecodeTileTokens);
-        } else if (slot_new != -1 && leader) {
-          raise_error(NKV_DEVERR_STORE_SLOT);
-        }
-      }
+      const int kvh = P.kvh, b = P.b, t0 = P.t0, t1 = P.t1, ntiles = P.ntiles, nsplit = P.nsplit;
       int j = 0;
       do {
         bool waited = true;
@@ -419,12 +438,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
         if (ntiles == 0) {
           if (leader) mbar_arrive(fb);
         } else {
-          const int blk = block_of(tok);
-          const bool blk_ok = blk >= 0 && static_cast<int64_t>(blk) < p.num_blocks;
-          // fully out of range: TMA fills zeros
-          const int slot = blk_ok ? blk * p.block_size + (tok % p.block_size) : -2 * kDecodeTileTokens;
-          if (!blk_ok && leader) raise_error(NKV_DEVERR_DECODE_BLOCK);
-          const bool patch = patch_row >= 0 && j == ntiles - 1;
+          const int slot = j == 0 ? P.tile0_slot : tile_slot(P, tok);
+          const bool patch = P.patch_row >= 0 && j == ntiles - 1;
           // a patched tile's transaction completes on the patch barrier; the
           // producer releases the consumers itself after the patch
           const uint32_t tb = patch ? smem_u32(&patch_bar[stage]) : fb;
@@ -448,6 +463,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
             const uint32_t pp = (patch_phase >> stage) & 1u;
             patch_phase ^= 1u << stage;
             patch_armed[stage] = pp + 1u;
+            // the new row to the cache (for later steps; nothing in this
+            // launch reads that slot from global memory)
+            {
+              const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
+              uint4* gdst = lane < kHeadVecs ? p.k_cache_vec : p.v_cache_vec;
+              gdst[static_cast<int64_t>(P.slot_new) * row_vecs + col] = new_row;
+            }
             // every lane observes the transaction's completion before it
             // overwrites part of what the TMA wrote
             const bool landed = mbar_wait_bounded(smem_u32(&patch_bar[stage]), pp);
@@ -462,7 +484,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
             const int u = lane & (kHeadVecs - 1);
             uint8_t* dst = stage_mem + stage * S::kStageBytes +
                            ((lane < kHeadVecs ? 0 : 2) + (u >> 3)) * kHalfTileBytes +
-                           swz128(static_cast<uint32_t>(patch_row), static_cast<uint32_t>(u & 7));
+                           swz128(static_cast<uint32_t>(P.patch_row), static_cast<uint32_t>(u & 7));
             *reinterpret_cast<uint4*>(dst) = new_row;
             __syncwarp();
             if (leader) mbar_arrive(fb);  // releases the tile (and the patch) to the consumers
@@ -476,10 +498,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       if (!ok) break;
       // KvChat: this step's query rows of the group join the row's window
       // (after the item's tiles are in flight: nothing in this launch reads them).
-      if (p.ring_vec != nullptr && s == 0 && ring_slot >= 0) {
-        if (ring_slot < p.ring_slots && ring_pos >= 0 && ring_pos < p.ring_window) {
-          uint4* dst = p.ring_vec + p.ring_layer_base_vec + ring_slot * p.ring_slot_stride_vec +
-                       static_cast<int64_t>(ring_pos) * p.num_q_heads * kHeadVecs +
+      if (ring_append) {
+        if (P.ring_slot < p.ring_slots && P.ring_pos >= 0 && P.ring_pos < p.ring_window) {
+          uint4* dst = p.ring_vec + p.ring_layer_base_vec + P.ring_slot * p.ring_slot_stride_vec +
+                       static_cast<int64_t>(P.ring_pos) * p.num_q_heads * kHeadVecs +
                        static_cast<int64_t>(kvh) * q_vecs;
 #pragma unroll
           for (int i = 0; i < kQVecsPerLane; ++i)
