@@ -42,12 +42,6 @@ __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Orders this thread's earlier generic-proxy global writes before later
-// async-proxy (TMA) accesses.
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -89,12 +83,6 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ uint32_t cluster_nctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
 
