@@ -546,3 +546,57 @@ def test_threshold_compress_parity(cuda_lib, golden_dir, case):
                            keep_idx_override=gk)
     assert torch.equal(kd.cpu().view(torch.int16), k2.view(torch.int16))
     assert torch.equal(vd.cpu().view(torch.int16), v2.view(torch.int16))
+
+
+@pytest.mark.parametrize("P,S_cfg,R_cfg,W,Hq,Hk", [
+    (20, 100, 60, 30, 16, 8),    # 90 keys: one CTA per kv head (8-CTA cluster)
+    (256, 511, 257, 50, 8, 4),   # two CTAs per kv head, 8-CTA cluster (a TP2 shard)
+    (120, 400, 200, 40, 8, 2),   # two CTAs per kv head, 4-CTA cluster, g = 4
+], ids=["one_cta_per_head", "tp2_shard", "hk2_g4"])
+def test_threshold_compress_against_oracle(cuda_lib, P, S_cfg, R_cfg, W, Hq, Hk):
+    """Shapes beside the golden cases (other kv-head counts, and few enough
+    keys that each kv head keeps one CTA): the ranked importance equals the
+    oracle's SnapKV importance except where the CPU's bf16 matmul rounds a
+    score differently (a handful of keys at most), the kept set is the
+    exact top-k of the importance the kernel ranked, and the compaction is
+    bit-exact for that kept set."""
+    from oracle.snapkv import snapkv_importance, topk_low_index
+    ops = _ops()
+    S, R = P + S_cfg, P + R_cfg
+    L, layer = 1, 0
+    pb, qsteps = threshold_inputs(700 + Hk + P, P, Hq, Hk, W, S_cfg, L)
+    ring = torch.zeros(1, L, W, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    bidx = torch.zeros(1, dtype=torch.int32, device=DEV)
+    rslot = torch.zeros(1, dtype=torch.int32, device=DEV)
+    qref = QueryWindowRef(L, W, Hq, 128)
+    qref.activate(0)
+    for step in range(W):
+        pos = torch.tensor([step], dtype=torch.int32, device=DEV)
+        ops.query_window_append(qsteps[step, 0].to(DEV), ring, 0, bidx, rslot, pos)
+        qref.append([0], 0, qsteps[step, 0])
+    kd, vd = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    keep = torch.zeros(1, R, dtype=torch.int32, device=DEV)
+    imp = torch.full((1, S - W), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.threshold_compress(ring, rslot, layer, kd, vd, pb.block_tables.to(DEV), cl, bidx, S, R,
+                           out_keep_idx=keep, out_importance=imp)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    assert cl.cpu().tolist() == [R]
+    q_sub = qref.gather([0], layer)  # [1, Hq, W, D], window order
+    from oracle.threshold_compress import gather_first_positions
+    k_sub, _ = gather_first_positions(pb.k_cache, pb.v_cache, pb.block_tables, [0], S)
+    ref_imp = snapkv_importance(q_sub, k_sub, W)
+    got = imp.cpu()
+    differ = (got.view(torch.int16) != ref_imp.view(torch.int16)).sum().item()
+    assert differ <= max(3, (S - W) // 100), f"{differ} of {S - W} importance values differ"
+    num_keep = R - W - 1
+    gk = keep.cpu().long()
+    want = topk_low_index(got.float(), num_keep)
+    assert torch.equal(gk[0, 1:1 + num_keep], want[0])
+    assert gk[0, 0].item() == 0
+    assert torch.equal(gk[0, 1 + num_keep:], torch.arange(S - W, S))
+    k2, v2, cl2 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    threshold_compress_ref(q_sub, k2, v2, pb.block_tables, cl2, [0], S, R, W, keep_idx_override=gk)
+    assert torch.equal(kd.cpu().view(torch.int16), k2.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v2.view(torch.int16))
