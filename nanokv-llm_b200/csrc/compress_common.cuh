@@ -201,6 +201,82 @@ __device__ void topk_ascending(const uint16_t* keys, int n, int k, int* out, int
 }
 
 // Moves rows src(i) -> dst(i), i in [0, n), of this CTA's kv-head slice (256
+// bytes of K and of V per row) by bulk asynchronous copies, global -> shared
+// -> global, with no data in registers: kBulkRows rows per chunk, two chunks
+// in flight through `buf` (2 buffers x kBulkRows rows x K and V, 16-byte
+// aligned). Thread t < 2 * kBulkRows owns array t / kBulkRows (0 K, 1 V) of
+// row t % kBulkRows of every chunk: it issues that row's load, its store once
+// the chunk's mbarrier has completed, and the refill of its buffer slot once
+// its own store has read it. Safe for in-place compaction when source index
+// >= destination index (the contract of compact_rows_pipelined): a chunk's
+// stores start after every load of that chunk and of each earlier chunk has
+// landed, and no chunk reads a row an earlier chunk writes. Rows with src ==
+// dst or an unresolved slot (< 0) are skipped. `bars`: two mbarriers, which
+// this function initialises. Returns false, uniformly, when a load never
+// landed (NKV_DEVERR_WAIT_TIMEOUT is raised; that chunk and later ones are not
+// stored); every store issued has been performed when it returns.
+template <int kThreads, int kBulkRows, typename SlotFn>
+__device__ bool compact_rows_bulk(__nv_bfloat16* k_cache, __nv_bfloat16* v_cache, int num_kv_heads,
+                                  int head, int n, SlotFn slots, uint8_t* buf, uint64_t* bars) {
+  static_assert(2 * kBulkRows <= kThreads, "one thread per (row, array)");
+  constexpr uint32_t kRowBytes = kCompressHeadDim * 2;
+  constexpr uint32_t kBufBytes = 2 * kBulkRows * kRowBytes;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    mbar_init(smem_u32(&bars[0]), 2 * kBulkRows);
+    mbar_init(smem_u32(&bars[1]), 2 * kBulkRows);
+    fence_barrier_init();
+  }
+  // the buffers were last accessed through the generic proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncthreads();
+  bool ok = true;
+  if (t < 2 * kBulkRows) {
+    const int arr = t / kBulkRows;
+    const int r = t % kBulkRows;
+    __nv_bfloat16* const base = arr == 0 ? k_cache : v_cache;
+    const uint32_t slot0 = smem_u32(buf) + static_cast<uint32_t>(t) * kRowBytes;
+    const int nchunks = (n + kBulkRows - 1) / kBulkRows;
+    int64_t dst0 = -1, dst1 = -1;  // this thread's destination in buffer 0 / 1
+    auto load = [&](int c) {
+      const int i = c * kBulkRows + r;
+      int64_t src = -1, dst = -1;
+      if (i < n) slots(i, src, dst);
+      const uint32_t bar = smem_u32(&bars[c & 1]);
+      if (i < n && src >= 0 && dst >= 0 && src != dst) {
+        mbar_arrive_expect_tx(bar, kRowBytes);
+        bulk_load_row(slot0 + (c & 1) * kBufBytes,
+                      base + (src * num_kv_heads + head) * kCompressHeadDim, kRowBytes, bar);
+      } else {
+        dst = -1;
+        mbar_arrive(bar);
+      }
+      if (c & 1) dst1 = dst; else dst0 = dst;
+    };
+    if (nchunks > 0) load(0);
+    if (nchunks > 1) load(1);
+    for (int c = 0; c < nchunks; ++c) {
+      if (!mbar_wait_bounded(smem_u32(&bars[c & 1]), (c >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const int64_t dst = (c & 1) ? dst1 : dst0;
+      if (dst >= 0) {
+        bulk_store_row(base + (dst * num_kv_heads + head) * kCompressHeadDim,
+                       slot0 + (c & 1) * kBufBytes, kRowBytes);
+        bulk_commit();
+      }
+      if (c + 2 < nchunks) {
+        if (dst >= 0) bulk_wait_read_all();
+        load(c + 2);
+      }
+    }
+    bulk_wait_all();
+  }
+  return __syncthreads_and(ok ? 1 : 0) != 0;
+}
+
+// Moves rows src(i) -> dst(i), i in [0, n), of this CTA's kv-head slice (256
 // bytes of K and of V per row), kThreads / 4 rows per chunk (4 threads per
 // row), with the reads of chunk
 // c+1 overlapping the writes of chunk c. Safe for in-place compaction when

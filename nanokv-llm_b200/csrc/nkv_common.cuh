@@ -243,6 +243,32 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Untiled bulk copies (addresses 16-byte aligned, size a multiple of 16):
+// global -> this CTA's shared memory, completing `bytes` on mbarrier `bar`;
+// shared -> global in the thread's bulk group, with its commit and waits
+// (.read: the source may be overwritten; plain: the writes are performed).
+__device__ __forceinline__ void bulk_load_row(uint32_t dst, const void* src, uint32_t bytes,
+                                              uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst), "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_store_row(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Programmatic dependent launch: a kernel launched with programmatic stream
 // serialisation may start while its predecessor runs; grid_dependency_wait()
 // blocks until the predecessor has completed and its writes are visible, and

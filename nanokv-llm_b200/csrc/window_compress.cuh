@@ -17,8 +17,9 @@
 //      swizzle, no multicast, kept in L2 for the compaction that re-reads the
 //      kept rows); each pair of warps owns one ring stage -- its leader
 //      refills it as soon as both warps are done with it -- and each thread
-//      scores one key from shared memory (conflict-free through the swizzle;
-//      the q rows are a broadcast).
+//      scores four keys over a quarter of the dims from shared memory
+//      (conflict-free through the swizzle; each q load, a broadcast, feeds
+//      eight fp64 FMAs), the quarters summed by a shuffle reduce-scatter.
 //   2. Cluster barrier; every CTA reads all partials through distributed shared
 //      memory and forms importance = bf16(sum over all local heads), the single
 //      rounding of the reference's head sum. One kept set per (sequence, rank).
@@ -27,8 +28,9 @@
 //      (a deterministic refinement of torch.topk's unspecified tie order), and
 //      a block scan emits the kept indices in ascending order.
 //   4. Compaction of this CTA's kv-head slice of every kept row into the first
-//      keep_tokens window slots (compact_rows_pipelined), then the partial
-//      tail block after them (slot arithmetic as in the reference).
+//      keep_tokens window slots, then the partial tail block after them (slot
+//      arithmetic as in the reference), by bulk asynchronous copies staged
+//      in the K ring (compact_rows_bulk).
 // No host round trip, no scratch memory, no V traffic for scoring.
 #pragma once
 #include "compress_common.cuh"
@@ -66,6 +68,14 @@ constexpr int kWinHalfBytes = kWinTileTokens * 128;   // 64 dims x 64 tokens, bf
 constexpr int kWinTileBytes = 2 * kWinHalfBytes;      // 16 KB
 constexpr int kWinRingBytes = kWinStages * kWinTileBytes + 64;  // + the full barriers
 static_assert(kWinStages * 64 == kCompressThreads, "one warp pair (64 keys) per stage");
+// Compaction: rows per chunk of the bulk copies; two chunks of K and V rows
+// fill the K ring, which scoring no longer uses by then.
+constexpr int kWinBulkRows = 64;
+static_assert(2 * 2 * kWinBulkRows * 256 <= kWinStages * kWinTileBytes, "chunks fit the ring");
+// Keys per thread in the scoring loop (and dim ranges per key), as many as
+// the kWinSplit x G fp64 sums leave registers for without spilling.
+template <int G>
+constexpr int kWinSplit = G <= 4 ? 4 : (G <= 8 ? 2 : 1);
 
 // Shared-memory bytes of window_compress_kernel<G> (host and device agree):
 // the K ring (1024-byte aligned, hence the slack) and the layout after it.
@@ -115,6 +125,7 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
   __shared__ int s_tail_block;
   __shared__ int s_abort;           // a K tile never landed (cluster-visible)
   __shared__ int s_pair_abort[kWinStages];
+  __shared__ alignas(8) uint64_t s_cbar[2];  // compaction chunk barriers
 
   // The kv heads of a sequence are the CTAs of one cluster (their partial
   // sums meet in distributed shared memory). A launch that lost its
@@ -193,27 +204,13 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
       issue(pair);
     }
     if (threadIdx.x == 32) {
-      // Every K tile of the window, and the V rows and tail block the
-      // compaction will read, start moving into L2 now, so the ring's loads
-      // and the compaction's reads find them there instead of waiting on
-      // DRAM one tile (or chunk) at a time.
+      // Every K tile of the window starts moving into L2 now, so the ring's
+      // refills find it there instead of waiting on DRAM one tile at a time.
       prefetch_tmap(&tm_v);
       for (int jj = kWinStages; jj < ntiles; ++jj) {
         const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
         tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
         tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
-      }
-      for (int jj = 0; jj < ntiles; ++jj) {
-        const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
-        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
-        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
-      }
-      for (int t0 = 0; t0 < tail_len; t0 += kWinTileTokens) {
-        const int slot0 = s_tail_block * bs + t0;
-        tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
-        tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
-        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
-        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
       }
     }
     int use = 0;
@@ -222,45 +219,78 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
       if (!mbar_wait_bounded(fb, use & 1)) s_pair_abort[pair] = 1;
       pair_barrier(pair);
       if (s_pair_abort[pair]) break;  // uniform across the pair
-      // kAcc independent fp64 sums per head (the sum of exact products does
-      // not depend on their order at the precision kept), so the DFMA
-      // latency overlaps
-      constexpr int kAcc = G <= 4 ? 4 : (G <= 8 ? 2 : 1);
-      double acc[G][kAcc];
+      // Each thread scores kWinSplit keys of the tile over 128 / kWinSplit
+      // dims: the lanes of a warp form kWinSplit parts of kLanes lanes, part
+      // p taking dims [p * 128 / kWinSplit, ...) of keys kg + kKeyStride * kk.
+      // A q load (one address per 8-lane phase: a broadcast) then feeds
+      // 2 * kWinSplit fp64 FMAs, and the K reads of a phase hit 8 distinct
+      // swizzled chunks. The parts' sums meet by a shuffle reduce-scatter
+      // that leaves lane part p with key kk = p (the sum of exact products
+      // does not depend on its order at the precision kept).
+      constexpr int kSplit = kWinSplit<G>;
+      constexpr int kLanes = 32 / kSplit;
+      constexpr int kKeyStride = kWinTileTokens / kSplit;
+      constexpr int kChunks = (kCompressHeadDim / 8) / kSplit;
+      const int lane = tp & 31;
+      const int part = lane / kLanes;
+      const int kg = (tp >> 5) * kLanes + lane % kLanes;
+      double acc[kSplit][G];
 #pragma unroll
-      for (int r = 0; r < G; ++r)
+      for (int kk = 0; kk < kSplit; ++kk)
 #pragma unroll
-        for (int a = 0; a < kAcc; ++a) acc[r][a] = 0.0;
-#pragma unroll 2
-      for (int c = 0; c < kCompressHeadDim / 8; ++c) {
-        const int cc = c & 7;
-        const uint4 w = *reinterpret_cast<const uint4*>(stage + (c >> 3) * kWinHalfBytes +
-                                                        tp * 128 + ((cc ^ (tp & 7)) << 4));
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-        double kd[8];
+        for (int r = 0; r < G; ++r) acc[kk][r] = 0.0;
+#pragma unroll 1
+      for (int jj = 0; jj < kChunks; ++jj) {
+        const int c = part * kChunks + jj;
+        const uint8_t* half = stage + (c >> 3) * kWinHalfBytes;
+        uint4 w[kSplit];
+#pragma unroll
+        for (int kk = 0; kk < kSplit; ++kk) {
+          const int row = kg + kKeyStride * kk;
+          w[kk] = *reinterpret_cast<const uint4*>(half + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+        }
+        const double2* qp = reinterpret_cast<const double2*>(qd + c * 8);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          kd[2 * e] = static_cast<double>(__uint_as_float(wv[e] << 16));
-          kd[2 * e + 1] = static_cast<double>(__uint_as_float(wv[e] & 0xffff0000u));
-        }
+          double kd[kSplit][2];
 #pragma unroll
-        for (int r = 0; r < G; ++r) {
-          const double2* qp = reinterpret_cast<const double2*>(qd + r * kCompressHeadDim + c * 8);
+          for (int kk = 0; kk < kSplit; ++kk) {
+            const uint32_t wv = e == 0 ? w[kk].x : e == 1 ? w[kk].y : e == 2 ? w[kk].z : w[kk].w;
+            kd[kk][0] = static_cast<double>(__uint_as_float(wv << 16));
+            kd[kk][1] = static_cast<double>(__uint_as_float(wv & 0xffff0000u));
+          }
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const double2 qq = qp[e];
-            acc[r][(2 * e) % kAcc] = fma(qq.x, kd[2 * e], acc[r][(2 * e) % kAcc]);
-            acc[r][(2 * e + 1) % kAcc] = fma(qq.y, kd[2 * e + 1], acc[r][(2 * e + 1) % kAcc]);
+          for (int r = 0; r < G; ++r) {
+            const double2 qq = qp[r * (kCompressHeadDim / 2) + e];
+#pragma unroll
+            for (int kk = 0; kk < kSplit; ++kk) {
+              acc[kk][r] = fma(qq.x, kd[kk][0], acc[kk][r]);
+              acc[kk][r] = fma(qq.y, kd[kk][1], acc[kk][r]);
+            }
           }
         }
       }
-      const int t = j * kWinTileTokens + tp;
+      // reduce-scatter: level l pairs slots (2s, 2s + 1) (key bit l 0 / 1);
+      // a lane keeps the key whose bit l matches its part's bit l
+#pragma unroll
+      for (int l = 0; (1 << l) < kSplit; ++l) {
+        const bool hi = ((part >> l) & 1) != 0;
+        const int mask = kLanes << l;
+#pragma unroll
+        for (int s = 0; s < (kSplit >> (l + 1)); ++s) {
+#pragma unroll
+          for (int r = 0; r < G; ++r) {
+            const double a = acc[2 * s][r], b = acc[2 * s + 1][r];
+            const double other = __shfl_xor_sync(0xffffffffu, hi ? a : b, mask);
+            acc[s][r] = (hi ? b : a) + other;
+          }
+        }
+      }
+      const int t = j * kWinTileTokens + kg + kKeyStride * part;
       if (t < kp) {
 #pragma unroll
         for (int r = 0; r < G; ++r) {
-          double sum = acc[r][0];
-#pragma unroll
-          for (int a = 1; a < kAcc; ++a) sum += acc[r][a];
+          const double sum = acc[0][r];
           const float sc = round_bf16(static_cast<float>(sum));
           scores[r * kp + t] = (t == 0 || t >= nk) ? -INFINITY : round_bf16(sc * p.scale);
         }
@@ -280,6 +310,24 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
       for (int r = 0; r < G; ++r) scores[r * kp + t] = -INFINITY;
     }
     __syncthreads();
+    if (threadIdx.x == 32) {
+      // The V rows and the tail block the compaction reads move into L2
+      // while the softmax, the importance and the top-k run; issued only now
+      // so that the window's K, which the scoring waits on, had DRAM first.
+      const int tiles_per_block = bs / kWinTileTokens;
+      for (int jj = 0; jj < window_tokens / kWinTileTokens; ++jj) {
+        const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
+        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
+      }
+      for (int t0 = 0; t0 < tail_len; t0 += kWinTileTokens) {
+        const int slot0 = s_tail_block * bs + t0;
+        tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
+      }
+    }
     // 2. softmax of every head over the keys (bf16 output), fp32 group sum
     float mx[G], sm[G];
 #pragma unroll
@@ -341,29 +389,34 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
   __syncthreads();
 
   // 5. compaction of this head's slice, then the tail block.
+  // The kept rows, then the tail rows (to dst_keep[-1] + 1 + j in slot
+  // arithmetic), as one list: a tail row is stored only after every kept
+  // row's load has landed, and no tail destination is a later row's source.
   const int* wb = wblk;
   const int keep_tokens = p.keep_tokens;
-  compact_rows_pipelined(p.k_cache, p.v_cache, p.num_kv_heads, head, keep_tokens,
-                         [&](int i, int64_t& src, int64_t& dst) {
-                           const int s = final_idx[i];
-                           src = static_cast<int64_t>(wb[s / bs]) * bs + (s % bs);
-                           dst = static_cast<int64_t>(wb[i / bs]) * bs + (i % bs);
-                         });
-  if (tail_len > 0) {
-    const int64_t last_dst =
-        static_cast<int64_t>(wb[(keep_tokens - 1) / bs]) * bs + ((keep_tokens - 1) % bs);
-    const int64_t num_slots = p.num_blocks * bs;
-    const int64_t tail_block = s_tail_block;
-    compact_rows_pipelined(p.k_cache, p.v_cache, p.num_kv_heads, head, tail_len,
-                           [&](int j, int64_t& src, int64_t& dst) {
-                             src = tail_block * bs + j;
-                             dst = last_dst + 1 + j;
-                             if (dst >= num_slots) {
-                               raise_error(NKV_DEVERR_COMPRESS_RANGE);
-                               dst = -1;
-                             }
-                           });
-  }
+  const int64_t last_dst =
+      static_cast<int64_t>(wb[(keep_tokens - 1) / bs]) * bs + ((keep_tokens - 1) % bs);
+  const int64_t num_slots = p.num_blocks * bs;
+  const int64_t tail_block = s_tail_block;
+  if (!compact_rows_bulk<kCompressThreads, kWinBulkRows>(
+          p.k_cache, p.v_cache, p.num_kv_heads, head, keep_tokens + tail_len,
+          [&](int i, int64_t& src, int64_t& dst) {
+            if (i < keep_tokens) {
+              const int s = final_idx[i];
+              src = static_cast<int64_t>(wb[s / bs]) * bs + (s % bs);
+              dst = static_cast<int64_t>(wb[i / bs]) * bs + (i % bs);
+            } else {
+              const int j = i - keep_tokens;
+              src = tail_block * bs + j;
+              dst = last_dst + 1 + j;
+              if (dst >= num_slots) {
+                raise_error(NKV_DEVERR_COMPRESS_RANGE);
+                dst = -1;
+              }
+            }
+          },
+          ring, s_cbar))
+    return;  // a row never landed (flagged): no metadata from this CTA
 
   // 6. metadata: new length (every layer writes the same value) and outputs.
   const int new_len = L0 - window_tokens + keep_tokens;
