@@ -16,7 +16,8 @@
 //      head stream through a ring of four 64-token tiles (TMA, 128-byte
 //      swizzle, no multicast, kept in L2 for the compaction that re-reads the
 //      kept rows); each pair of warps owns one ring stage -- its leader
-//      refills it as soon as both warps are done with it -- and each thread
+//      refills each 64-dim half of it as soon as both warps are done with
+//      that half, while they score the other -- and each thread
 //      scores four keys over a quarter of the dims from shared memory
 //      (conflict-free through the swizzle; each q load, a broadcast, feeds
 //      eight fp64 FMAs), the quarters summed by a shuffle reduce-scatter.
@@ -66,7 +67,7 @@ constexpr int kWinTileTokens = 64;                    // tokens per K tile
 constexpr int kWinStages = 4;                         // ring stages = warp pairs
 constexpr int kWinHalfBytes = kWinTileTokens * 128;   // 64 dims x 64 tokens, bf16
 constexpr int kWinTileBytes = 2 * kWinHalfBytes;      // 16 KB
-constexpr int kWinRingBytes = kWinStages * kWinTileBytes + 64;  // + the full barriers
+constexpr int kWinRingBytes = kWinStages * kWinTileBytes + 64;  // + 2 barriers per stage
 static_assert(kWinStages * 64 == kCompressThreads, "one warp pair (64 keys) per stage");
 // Compaction: rows per chunk of the bulk copies; two chunks of K and V rows
 // fill the K ring, which scoring no longer uses by then.
@@ -165,7 +166,8 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
     s_tail_block = tb;
     s_abort = 0;
     for (int st = 0; st < kWinStages; ++st) {
-      mbar_init(smem_u32(&full[st]), 1);
+      mbar_init(smem_u32(&full[2 * st]), 1);
+      mbar_init(smem_u32(&full[2 * st + 1]), 1);
       s_pair_abort[st] = 0;
     }
     fence_barrier_init();
@@ -184,25 +186,31 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
   if (valid) {
     // 1. scores: tile j (tokens [64 j, 64 j + 64) of the window, two 64-dim
     // halves of 64 rows x 128 bytes) lands in ring stage j % 4, which warp
-    // pair j % 4 consumes, one key per thread.
+    // pair j % 4 consumes, half by half.
     const int ntiles = window_tokens / kWinTileTokens;
     const int tiles_per_block = bs / kWinTileTokens;
     const int pair = threadIdx.x >> 6;
     const int tp = threadIdx.x & 63;
     const bool pair_leader = tp == 0;
     uint8_t* stage = ring + pair * kWinTileBytes;
-    const uint32_t fb = smem_u32(&full[pair]);
-    auto issue = [&](int j) {
+    // one barrier per 64-dim half of the stage: a half is refilled as soon
+    // as both warps are done with it, while they score the other half
+    const uint32_t fb0 = smem_u32(&full[2 * pair]);
+    const uint32_t fb1 = smem_u32(&full[2 * pair + 1]);
+    int issued[2] = {0, 0}, landed[2] = {0, 0};
+    auto issue_half = [&](int j, int h) {
       const int slot0 = wblk[j / tiles_per_block] * bs + (j % tiles_per_block) * kWinTileTokens;
-      const uint64_t pol = l2_policy_evict_last();
-      mbar_arrive_expect_tx(fb, kWinTileBytes);
-      tma_load_3d(smem_u32(stage), &tm_k, fb, 0, head, slot0, pol);
-      tma_load_3d(smem_u32(stage) + kWinHalfBytes, &tm_k, fb, 64, head, slot0, pol);
+      const uint32_t fb = h ? fb1 : fb0;
+      mbar_arrive_expect_tx(fb, kWinHalfBytes);
+      tma_load_3d(smem_u32(stage) + h * kWinHalfBytes, &tm_k, fb, 64 * h, head, slot0,
+                  l2_policy_evict_last());
     };
     if (pair_leader && pair < ntiles) {
       prefetch_tmap(&tm_k);
-      issue(pair);
+      issue_half(pair, 0);
+      issue_half(pair, 1);
     }
+    if (pair < ntiles) issued[0] = issued[1] = 1;  // every thread tracks the leader's loads
     if (threadIdx.x == 32) {
       // Every K tile of the window starts moving into L2 now, so the ring's
       // refills find it there instead of waiting on DRAM one tile at a time.
@@ -213,63 +221,76 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
         tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
       }
     }
-    int use = 0;
+    // Each thread scores kWinSplit keys of the tile over 128 / kWinSplit dims:
+    // the lanes of a warp form kWinSplit parts of kLanes lanes, part p taking
+    // the 8-dim chunks c = p + kWinSplit * jj (half of them in each 64-dim
+    // half) of keys kg + kKeyStride * kk. A q load (one address per 8-lane
+    // phase: a broadcast) then feeds 2 * kWinSplit fp64 FMAs, and the K reads
+    // of a phase hit 8 distinct swizzled chunks. The parts' sums meet by a
+    // shuffle reduce-scatter that leaves lane part p with key kk = p (the sum
+    // of exact products does not depend on its order at the precision kept).
+    constexpr int kSplit = kWinSplit<G>;
+    constexpr int kLanes = 32 / kSplit;
+    constexpr int kKeyStride = kWinTileTokens / kSplit;
+    constexpr int kChunks = (kCompressHeadDim / 8) / kSplit;
+    const int lane = tp & 31;
+    const int part = lane / kLanes;
+    const int kg = (tp >> 5) * kLanes + lane % kLanes;
+    bool aborted = false;
     int j = pair;
-    for (; j < ntiles; j += kWinStages, ++use) {
-      if (!mbar_wait_bounded(fb, use & 1)) s_pair_abort[pair] = 1;
-      pair_barrier(pair);
-      if (s_pair_abort[pair]) break;  // uniform across the pair
-      // Each thread scores kWinSplit keys of the tile over 128 / kWinSplit
-      // dims: the lanes of a warp form kWinSplit parts of kLanes lanes, part
-      // p taking dims [p * 128 / kWinSplit, ...) of keys kg + kKeyStride * kk.
-      // A q load (one address per 8-lane phase: a broadcast) then feeds
-      // 2 * kWinSplit fp64 FMAs, and the K reads of a phase hit 8 distinct
-      // swizzled chunks. The parts' sums meet by a shuffle reduce-scatter
-      // that leaves lane part p with key kk = p (the sum of exact products
-      // does not depend on its order at the precision kept).
-      constexpr int kSplit = kWinSplit<G>;
-      constexpr int kLanes = 32 / kSplit;
-      constexpr int kKeyStride = kWinTileTokens / kSplit;
-      constexpr int kChunks = (kCompressHeadDim / 8) / kSplit;
-      const int lane = tp & 31;
-      const int part = lane / kLanes;
-      const int kg = (tp >> 5) * kLanes + lane % kLanes;
+    for (; j < ntiles; j += kWinStages) {
       double acc[kSplit][G];
 #pragma unroll
       for (int kk = 0; kk < kSplit; ++kk)
 #pragma unroll
         for (int r = 0; r < G; ++r) acc[kk][r] = 0.0;
-#pragma unroll 1
-      for (int jj = 0; jj < kChunks; ++jj) {
-        const int c = part * kChunks + jj;
-        const uint8_t* half = stage + (c >> 3) * kWinHalfBytes;
-        uint4 w[kSplit];
 #pragma unroll
-        for (int kk = 0; kk < kSplit; ++kk) {
-          const int row = kg + kKeyStride * kk;
-          w[kk] = *reinterpret_cast<const uint4*>(half + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+      for (int h = 0; h < 2; ++h) {
+        if (!mbar_wait_bounded(h ? fb1 : fb0, landed[h] & 1)) s_pair_abort[pair] = 1;
+        pair_barrier(pair);
+        if (s_pair_abort[pair]) {  // uniform across the pair
+          aborted = true;
+          break;
         }
-        const double2* qp = reinterpret_cast<const double2*>(qd + c * 8);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          double kd[kSplit][2];
+        ++landed[h];
+        const uint8_t* half = stage + h * kWinHalfBytes;
+#pragma unroll 1
+        for (int jj = h * (kChunks / 2); jj < (h + 1) * (kChunks / 2); ++jj) {
+          const int c = part + kSplit * jj;  // c >> 3 == h
+          uint4 w[kSplit];
 #pragma unroll
           for (int kk = 0; kk < kSplit; ++kk) {
-            const uint32_t wv = e == 0 ? w[kk].x : e == 1 ? w[kk].y : e == 2 ? w[kk].z : w[kk].w;
-            kd[kk][0] = static_cast<double>(__uint_as_float(wv << 16));
-            kd[kk][1] = static_cast<double>(__uint_as_float(wv & 0xffff0000u));
+            const int row = kg + kKeyStride * kk;
+            w[kk] = *reinterpret_cast<const uint4*>(half + row * 128 + (((c & 7) ^ (row & 7)) << 4));
           }
+          const double2* qp = reinterpret_cast<const double2*>(qd + c * 8);
 #pragma unroll
-          for (int r = 0; r < G; ++r) {
-            const double2 qq = qp[r * (kCompressHeadDim / 2) + e];
+          for (int e = 0; e < 4; ++e) {
+            double kd[kSplit][2];
 #pragma unroll
             for (int kk = 0; kk < kSplit; ++kk) {
-              acc[kk][r] = fma(qq.x, kd[kk][0], acc[kk][r]);
-              acc[kk][r] = fma(qq.y, kd[kk][1], acc[kk][r]);
+              const uint32_t wv = e == 0 ? w[kk].x : e == 1 ? w[kk].y : e == 2 ? w[kk].z : w[kk].w;
+              kd[kk][0] = static_cast<double>(__uint_as_float(wv << 16));
+              kd[kk][1] = static_cast<double>(__uint_as_float(wv & 0xffff0000u));
+            }
+#pragma unroll
+            for (int r = 0; r < G; ++r) {
+              const double2 qq = qp[r * (kCompressHeadDim / 2) + e];
+#pragma unroll
+              for (int kk = 0; kk < kSplit; ++kk) {
+                acc[kk][r] = fma(qq.x, kd[kk][0], acc[kk][r]);
+                acc[kk][r] = fma(qq.y, kd[kk][1], acc[kk][r]);
+              }
             }
           }
         }
+        pair_barrier(pair);  // both warps are done with this half of the stage
+        if (j + kWinStages < ntiles) {
+          if (pair_leader) issue_half(j + kWinStages, h);
+          ++issued[h];
+        }
       }
+      if (aborted) break;
       // reduce-scatter: level l pairs slots (2s, 2s + 1) (key bit l 0 / 1);
       // a lane keeps the key whose bit l matches its part's bit l
 #pragma unroll
@@ -295,13 +316,13 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
           scores[r * kp + t] = (t == 0 || t >= nk) ? -INFINITY : round_bf16(sc * p.scale);
         }
       }
-      pair_barrier(pair);  // both warps are done with the stage
-      if (pair_leader && j + kWinStages < ntiles) issue(j + kWinStages);
     }
-    if (j < ntiles && pair_leader) {
-      // a tile never landed: wait (bounded) for the stage's load in flight,
+    if (aborted && pair_leader) {
+      // a half never landed: wait (bounded) for the loads still in flight,
       // then the cluster skips this sequence
-      mbar_wait_bounded(fb, use & 1);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        if (issued[h] > landed[h]) mbar_wait_bounded(h ? fb1 : fb0, landed[h] & 1);
       s_abort = 1;
     }
     // keys past the window (padding) never win
