@@ -416,6 +416,36 @@ def test_window_compress_config3_event_full_size(cuda_lib):
     assert torch.equal(vd.cpu().view(torch.int16), v2.view(torch.int16))
 
 
+@pytest.mark.parametrize("Hq,Hk", [(16, 8), (8, 1)], ids=["g2", "g8_one_head"])
+def test_window_compress_block512(cuda_lib, Hq, Hk):
+    """kvcache_block_size 512 (the reference's configs allow any multiple of
+    256, nanokvllm/config.py:40): a 2,048-token window, 1,025 kept tokens,
+    partial tail blocks of several lengths and group widths 2 and 8. Kept
+    sets and new lengths equal the exact-score oracle's, the compaction
+    (kept rows in 64-row chunks, then the tail rows) is bit-exact."""
+    ops = _ops()
+    B, wb, kb, ke = 512, 4, 2, 1
+    lens = [2100, 2600, 3071, 4096 + 37]
+    pb = make_paged_batch(seed=55 + Hk, lens=lens, Hq=Hq, Hk=Hk, block_size=B)
+    sel = [0, 1, 2, 3]
+    keep_tokens = kb * B + ke
+    kd, vd = pb.k_cache.to(DEV), pb.v_cache.to(DEV)
+    cl = pb.context_lens.to(DEV)
+    keep_out = torch.full((len(sel), keep_tokens), -7, dtype=torch.int32, device=DEV)
+    ops.window_compress(pb.q.to(DEV), kd, vd, pb.block_tables.to(DEV), cl.clone(), cl,
+                        torch.tensor(sel, dtype=torch.int32, device=DEV), wb, keep_tokens,
+                        out_keep_idx=keep_out)
+    torch.cuda.synchronize()
+    assert _deverr() == 0
+    k1, v1, cl1 = pb.k_cache.clone(), pb.v_cache.clone(), pb.context_lens.clone()
+    okeep, _ = window_compress_ref(pb.q, k1, v1, pb.block_tables, pb.context_lens.clone(), cl1,
+                                   sel, B, wb, kb, ke, exact_scores=True)
+    assert cl.cpu().tolist() == cl1.tolist() == [L - wb * B + keep_tokens for L in lens]
+    assert torch.equal(keep_out.cpu().long(), okeep.long())
+    assert torch.equal(kd.cpu().view(torch.int16), k1.view(torch.int16))
+    assert torch.equal(vd.cpu().view(torch.int16), v1.view(torch.int16))
+
+
 def test_window_compaction_maximal_overlap(cuda_lib):
     """The compaction's read-all-then-write hazard, made maximal: keep 1,021
     of the window's 1,022 candidate keys (keep_tokens 1,023) and make key 1
