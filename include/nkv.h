@@ -132,14 +132,16 @@ int nkv_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_hea
 /* tile that holds it (after that tile's TMA has landed), so no second       */
 /* launch or cross-CTA ordering is needed.                                   */
 /* metadata_ready = 1 lets the launch read block_tables, context_lens,      */
-/* slot_mapping and the ring indices before it waits for the kernel it       */
-/* depends on (programmatic dependent launch): the caller vouches that the   */
-/* kernel launched just before this call on the stream does not write them   */
-/* (host copies and earlier kernels are fine; a compression kernel that     */
-/* rewrites context_lens right before is not). In a chain of decode launches */
-/* that hides a round of metadata loads behind the previous launch's tail.   */
-/* 0 reads everything after the wait. q, key and value are always read after */
-/* it.                                                                       */
+/* slot_mapping, the ring indices and the cached K/V rows other than the     */
+/* step's new ones before it waits for the kernel it depends on             */
+/* (programmatic dependent launch): the caller vouches that the kernel       */
+/* launched just before this call on the stream writes none of them (host    */
+/* copies and earlier kernels are fine; a compression kernel that rewrites   */
+/* context_lens or the cache right before, or a separate slot write of this  */
+/* step's rows, is not). In a chain of decode launches that hides the        */
+/* metadata loads and a CTA's first K/V tile behind the previous launch's    */
+/* tail. 0 reads everything after the wait. q, key and value are always read */
+/* after it.                                                                 */
 /* ring may be NULL (no query window). Otherwise it is the KvChat ring       */
 /* [num_ring_slots, num_layers, window_size, num_q_heads, head_dim]; row b   */
 /* appends q[b] to ring[ring_slot_of_row[b], layer_id, ring_pos_of_row[b]]   */

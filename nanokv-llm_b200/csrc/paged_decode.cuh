@@ -37,7 +37,8 @@
 //   * Programmatic dependent launch: the next kernel may start while this one
 //     drains; each role waits (griddepcontrol.wait) before its first access
 //     to data the previous kernel may write. With metadata_ready the producer
-//     reads its first item's metadata before that wait.
+//     reads its first item's metadata and requests its first K/V tile before
+//     that wait, and only the tile's q rows after it.
 //   * The work counter is reset by the last CTA to finish, so the workspace
 //     counters are back at zero after every call (graph-replay safe).
 //   * Tokens past context_lens in the last tile are masked in S (select, not
@@ -115,10 +116,11 @@ struct DecodeParams {
   // split r of (row, kv head) pair c and sending its partial to rank 0
   // through distributed shared memory (no global partials or counters).
   int cluster;
-  // 1: block_tables, context_lens, slot_mapping and the ring indices are not
-  // written by the kernel this launch depends on, so a CTA's first item's
-  // metadata is read before the dependency wait (the fused decode step's
-  // contract, when its caller vouches for it).
+  // 1: block_tables, context_lens, slot_mapping, the ring indices and the
+  // cached K/V rows (other than the step's new ones) are not written by the
+  // kernel this launch depends on, so a CTA's first item's metadata and its
+  // first K/V tile are requested before the dependency wait (the fused
+  // decode step's contract, when its caller vouches for it).
   int metadata_ready;
   // Fused decode step (optional, null when unused): the step's new K/V rows,
   // written by the producer warp right before the TMA that reads them, and
@@ -221,8 +223,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
   // rows, the reset workspace counters) are visible. The producer allows the
   // next kernel of the stream (the next layer's decode) to be scheduled right
   // after its own wait: those CTAs take free SMs, run their set-up (and, with
-  // metadata_ready, their first metadata loads) and wait until this grid has
-  // finished, which hides a launch's latency in a chain of small launches.
+  // metadata_ready, their first metadata loads and first K/V tile) and wait
+  // until this grid has finished, which hides a launch's latency in a chain
+  // of small launches.
 
   const int Hk = p.num_kv_heads;
   const int g = p.g;
@@ -348,23 +351,56 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       return P;
     };
     // With metadata_ready the first item's metadata is requested and planned
-    // before the dependency wait, so it is ready while the previous kernel
-    // drains; its first K/V tile is also requested into L2 (a hint: the
-    // loads after the wait read the coherent data).
+    // before the dependency wait: the kernel this launch depends on does not
+    // write it (the contract of metadata_ready). In a launch with one item
+    // per CTA (the latency-bound small batches) the item's first K/V tile is
+    // requested then too -- that kernel writes no cache row this launch reads,
+    // and the step's own new row is patched into the tile's shared-memory
+    // copy after the wait -- and only the tile's q rows, which that kernel
+    // may have written, after the wait, first thing. In larger launches,
+    // whose previous kernel is still streaming at full bandwidth, the tile
+    // is only hinted into L2 (demand loads there slowed that kernel's tail).
     const bool early = p.metadata_ready != 0 && static_item < p.total_items;
     ItemPlan pre;
+    bool pre_tile = false;  // the first item's first tile is in flight (all but q)
+    uint32_t pre_tb = 0;    // the barrier its transaction completes on
     if (early) {
       int sc0, bt0;
       meta_loads(static_item, sc0, bt0);
       pre = make_plan(static_item, sc0, bt0);
-      if (leader && pre.ntiles > 0 && pre.tile0_slot >= 0) {
-        tma_prefetch_l2_3d(&tm_k, 0, pre.kvh, pre.tile0_slot);
-        tma_prefetch_l2_3d(&tm_k, 64, pre.kvh, pre.tile0_slot);
-        tma_prefetch_l2_3d(&tm_v, 0, pre.kvh, pre.tile0_slot);
-        tma_prefetch_l2_3d(&tm_v, 64, pre.kvh, pre.tile0_slot);
+      if (p.total_items > static_cast<int>(gridDim.x)) {
+        if (leader && pre.ntiles > 0 && pre.tile0_slot >= 0) {
+          tma_prefetch_l2_3d(&tm_k, 0, pre.kvh, pre.tile0_slot);
+          tma_prefetch_l2_3d(&tm_k, 64, pre.kvh, pre.tile0_slot);
+          tma_prefetch_l2_3d(&tm_v, 0, pre.kvh, pre.tile0_slot);
+          tma_prefetch_l2_3d(&tm_v, 64, pre.kvh, pre.tile0_slot);
+        }
+      } else if (!pre.skip && pre.ntiles > 0) {
+        // stage 0, phase 0: free; the tile is the item's last when ntiles == 1
+        pre_tb = smem_u32(pre.patch_row >= 0 && pre.ntiles == 1 ? &patch_bar[0] : &full_bar[0]);
+        if (leader) {
+          int* m = meta;
+          m[0] = pre.item;
+          m[1] = 0;
+          m[2] = pre.ntiles;
+          m[3] = min(kDecodeTileTokens, pre.t1 - pre.t0);
+          m[4] = pre.nsplit;
+          mbar_arrive_expect_tx(pre_tb, 4u * kHalfTileBytes + q_bytes);
+          const uint32_t base = smem_u32(stage_mem);
+          tma_load_3d(base + 0 * kHalfTileBytes, &tm_k, pre_tb, 0, pre.kvh, pre.tile0_slot, pol_stream);
+          tma_load_3d(base + 1 * kHalfTileBytes, &tm_k, pre_tb, 64, pre.kvh, pre.tile0_slot, pol_stream);
+          tma_load_3d(base + 2 * kHalfTileBytes, &tm_v, pre_tb, 0, pre.kvh, pre.tile0_slot, pol_stream);
+          tma_load_3d(base + 3 * kHalfTileBytes, &tm_v, pre_tb, 64, pre.kvh, pre.tile0_slot, pol_stream);
+        }
+        pre_tile = true;
       }
     }
     grid_dependency_wait();
+    if (pre_tile && leader) {
+      const uint32_t qb = smem_u32(stage_mem) + 4 * kHalfTileBytes;
+      tma_load_3d(qb, &tm_q, pre_tb, 0, pre.kvh * g, pre.b, pol_q);
+      tma_load_3d(qb + S::kQHalfBytes, &tm_q, pre_tb, 64, pre.kvh * g, pre.b, pol_q);
+    }
     allow_dependent_launch();
     bool first = true;
     // patch_armed[s] = parity + 1 of a patch-barrier transaction issued into
@@ -382,6 +418,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
       static_item = -1;
       if (item >= p.total_items) break;
       ItemPlan P;
+      const bool pre_first = first && pre_tile;  // its first tile is already requested
       if (first && early) {
         P = pre;
       } else {
@@ -413,8 +450,61 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
           if (lane + 32 * i < q_vecs) q_rows[i] = ldg_nc_v4(src + lane + 32 * i);
       }
       const int kvh = P.kvh, b = P.b, t0 = P.t0, t1 = P.t1, ntiles = P.ntiles, nsplit = P.nsplit;
+      // After a tile's loads are requested: the tile is armed, or -- the
+      // item's last tile holding the step's new row -- the row goes to the
+      // cache and into the tile's shared-memory copy once the TMA has landed,
+      // and the producer releases the tile itself. false: the wait gave up.
+      auto finish_tile = [&](bool patch, uint32_t fb) -> bool {
+        if (!patch) {
+          armed[stage] = phase + 1u;
+          return true;
+        }
+        const uint32_t pp = (patch_phase >> stage) & 1u;
+        patch_phase ^= 1u << stage;
+        patch_armed[stage] = pp + 1u;
+        // the new row to the cache (for later steps; nothing in this
+        // launch reads that slot from global memory)
+        {
+          const int64_t col = static_cast<int64_t>(P.kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
+          uint4* gdst = lane < kHeadVecs ? p.k_cache_vec : p.v_cache_vec;
+          gdst[static_cast<int64_t>(P.slot_new) * row_vecs + col] = new_row;
+        }
+        // every lane observes the transaction's completion before it
+        // overwrites part of what the TMA wrote
+        const bool landed = mbar_wait_bounded(smem_u32(&patch_bar[stage]), pp);
+        if (!__all_sync(0xffffffffu, landed)) {
+          if (leader) flags[0] = 1;
+          return false;
+        }
+        patch_armed[stage] = 0;
+        // lane u < 16: K dims [8u, 8u + 8) -> half u / 8, 16-byte chunk
+        // u % 8 of the row's 128-byte swizzled line; lanes 16-31: V
+        const int u = lane & (kHeadVecs - 1);
+        uint8_t* dst = stage_mem + stage * S::kStageBytes +
+                       ((lane < kHeadVecs ? 0 : 2) + (u >> 3)) * kHalfTileBytes +
+                       swz128(static_cast<uint32_t>(P.patch_row), static_cast<uint32_t>(u & 7));
+        *reinterpret_cast<uint4*>(dst) = new_row;
+        __syncwarp();
+        if (leader) mbar_arrive(fb);  // releases the tile (and the patch) to the consumers
+        return true;
+      };
+      auto next_stage = [&]() {
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      };
       int j = 0;
-      do {
+      if (pre_first) {
+        // the first tile was requested before the wait (ntiles > 0, stage 0)
+        if (!finish_tile(P.patch_row >= 0 && ntiles == 1, smem_u32(&full_bar[stage]))) {
+          ok = false;
+          break;
+        }
+        next_stage();
+        j = 1;
+      }
+      for (; j < ntiles || (j == 0 && ntiles == 0); ++j) {
         bool waited = true;
         if (leader) {
           waited = !flags[0] && mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u);
@@ -457,44 +547,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
               tma_load_3d(qb + S::kQHalfBytes, &tm_q, tb, 64, kvh * g, b, pol_q);
             }
           }
-          if (!patch) {
-            armed[stage] = phase + 1u;
-          } else {
-            const uint32_t pp = (patch_phase >> stage) & 1u;
-            patch_phase ^= 1u << stage;
-            patch_armed[stage] = pp + 1u;
-            // the new row to the cache (for later steps; nothing in this
-            // launch reads that slot from global memory)
-            {
-              const int64_t col = static_cast<int64_t>(kvh) * kHeadVecs + (lane & (kHeadVecs - 1));
-              uint4* gdst = lane < kHeadVecs ? p.k_cache_vec : p.v_cache_vec;
-              gdst[static_cast<int64_t>(P.slot_new) * row_vecs + col] = new_row;
-            }
-            // every lane observes the transaction's completion before it
-            // overwrites part of what the TMA wrote
-            const bool landed = mbar_wait_bounded(smem_u32(&patch_bar[stage]), pp);
-            if (!__all_sync(0xffffffffu, landed)) {
-              if (leader) flags[0] = 1;
-              ok = false;
-              break;
-            }
-            patch_armed[stage] = 0;
-            // lane u < 16: K dims [8u, 8u + 8) -> half u / 8, 16-byte chunk
-            // u % 8 of the row's 128-byte swizzled line; lanes 16-31: V
-            const int u = lane & (kHeadVecs - 1);
-            uint8_t* dst = stage_mem + stage * S::kStageBytes +
-                           ((lane < kHeadVecs ? 0 : 2) + (u >> 3)) * kHalfTileBytes +
-                           swz128(static_cast<uint32_t>(P.patch_row), static_cast<uint32_t>(u & 7));
-            *reinterpret_cast<uint4*>(dst) = new_row;
-            __syncwarp();
-            if (leader) mbar_arrive(fb);  // releases the tile (and the patch) to the consumers
+          if (!finish_tile(patch, fb)) {
+            ok = false;
+            break;
           }
         }
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      } while (++j < ntiles);
+        next_stage();
+      }
       if (!ok) break;
       // KvChat: this step's query rows of the group join the row's window
       // (after the item's tiles are in flight: nothing in this launch reads them).
