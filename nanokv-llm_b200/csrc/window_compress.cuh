@@ -317,6 +317,25 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
         }
       }
     }
+    if (pair_leader && !aborted) {
+      // This pair is done with its K tiles, and every K load of the window
+      // is requested: the V rows and the tail block the compaction reads
+      // start moving into L2 now (a quarter per pair; after K, which the
+      // scoring waits on, had DRAM first) while the softmax, the importance
+      // and the top-k run.
+      for (int jj = pair; jj < ntiles; jj += kWinStages) {
+        const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
+        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
+      }
+      for (int t0 = pair * kWinTileTokens; t0 < tail_len; t0 += kWinStages * kWinTileTokens) {
+        const int slot0 = s_tail_block * bs + t0;
+        tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
+        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
+      }
+    }
     if (aborted && pair_leader) {
       // a half never landed: wait (bounded) for the loads still in flight,
       // then the cluster skips this sequence
@@ -331,24 +350,6 @@ window_compress_kernel(const __grid_constant__ CUtensorMap tm_k,
       for (int r = 0; r < G; ++r) scores[r * kp + t] = -INFINITY;
     }
     __syncthreads();
-    if (threadIdx.x == 32) {
-      // The V rows and the tail block the compaction reads move into L2
-      // while the softmax, the importance and the top-k run; issued only now
-      // so that the window's K, which the scoring waits on, had DRAM first.
-      const int tiles_per_block = bs / kWinTileTokens;
-      for (int jj = 0; jj < window_tokens / kWinTileTokens; ++jj) {
-        const int slot0 = wblk[jj / tiles_per_block] * bs + (jj % tiles_per_block) * kWinTileTokens;
-        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
-        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
-      }
-      for (int t0 = 0; t0 < tail_len; t0 += kWinTileTokens) {
-        const int slot0 = s_tail_block * bs + t0;
-        tma_prefetch_l2_3d(&tm_k, 0, head, slot0);
-        tma_prefetch_l2_3d(&tm_k, 64, head, slot0);
-        tma_prefetch_l2_3d(&tm_v, 0, head, slot0);
-        tma_prefetch_l2_3d(&tm_v, 64, head, slot0);
-      }
-    }
     // 2. softmax of every head over the keys (bf16 output), fp32 group sum
     float mx[G], sm[G];
 #pragma unroll
