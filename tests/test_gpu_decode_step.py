@@ -166,3 +166,43 @@ def test_decode_step_chain_with_metadata_ready(cuda_lib, lens):
         assert (outs[layer].float().cpu() - ref).abs().max().item() <= 2e-2, f"layer {layer}"
     torch.cuda.synchronize()
     assert torch.equal(ring.view(torch.int16), ring_ref.view(torch.int16))
+
+
+def test_decode_step_chain_one_item_per_cta_without_clusters(cuda_lib):
+    """16 short rows x 8 kv heads: 128 (row, kv head) pairs, each one split,
+    too many for thread-block clusters, so every CTA of the plain launch
+    has exactly one item -- the case where a launch with metadata_ready
+    requests its first K/V tile before waiting on the previous launch. Three
+    layers launched back to back: outputs and cache rows equal the oracle's
+    and the same steps without metadata_ready."""
+    from nanokv_b200 import _lib, ops
+
+    Hq, Hk, L = 32, 8, 3
+    lens = [1 + (37 * i) % 1000 for i in range(16)]
+    pb = make_paged_batch(seed=400, lens=lens, Hq=Hq, Hk=Hk)
+    B = len(lens)
+    bt, cl, sm = pb.block_tables.to(DEV), pb.context_lens.to(DEV), pb.slot_mapping.to(DEV)
+    steps = [_qkv(B, Hq, Hk, 410 + i) for i in range(L)]
+    ws = ops.decode_workspace(torch.device(DEV), B, Hq, Hk, 128, bt.size(1), 256)
+    results = {}
+    for ready in (True, False):
+        caches = [(pb.k_cache.to(DEV), pb.v_cache.to(DEV)) for _ in range(L)]
+        outs = [torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=DEV) for _ in range(L)]
+        torch.cuda.synchronize()
+        for layer in range(L):
+            q, k, v = steps[layer]
+            ops.decode_step(q, k, v, caches[layer][0], caches[layer][1], sm, bt, cl, 128 ** -0.5,
+                            out=outs[layer], workspace=ws, metadata_ready=ready)
+        torch.cuda.synchronize()
+        assert _lib.read_device_error(clear=True) == 0
+        results[ready] = (caches, outs)
+    for layer in range(L):
+        q, k, v = steps[layer]
+        kc, vc = pb.k_cache.clone(), pb.v_cache.clone()
+        store_kvcache_ref(k.cpu(), v.cpu(), kc, vc, pb.slot_mapping)
+        ref = paged_decode_ref(q.cpu(), kc, vc, pb.block_tables, pb.context_lens, 128 ** -0.5)
+        caches, outs = results[True]
+        assert torch.equal(caches[layer][0].cpu().view(torch.int16), kc.view(torch.int16))
+        assert torch.equal(caches[layer][1].cpu().view(torch.int16), vc.view(torch.int16))
+        assert (outs[layer].float().cpu() - ref).abs().max().item() <= 2e-2, f"layer {layer}"
+        assert torch.equal(outs[layer].view(torch.int16), results[False][1][layer].view(torch.int16))
