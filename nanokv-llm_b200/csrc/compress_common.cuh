@@ -84,18 +84,6 @@ __device__ __forceinline__ void block_reduce_vec(float (&v)[N], float* red) {
   block_reduce_vec_impl<N, kMax>(v, red);
 }
 
-__device__ __forceinline__ float block_max_float(float v, float* red) {
-  float a[1] = {v};
-  block_reduce_vec_impl<1, true>(a, red);
-  return a[0];
-}
-
-__device__ __forceinline__ float block_sum_float(float v, float* red) {
-  float a[1] = {v};
-  block_reduce_vec_impl<1, false>(a, red);
-  return a[0];
-}
-
 // Bit pattern of a non-negative bf16 value: monotone in the value.
 __device__ __forceinline__ uint32_t bf16_key(float v) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
